@@ -1,0 +1,374 @@
+"""Benchmark of the Arctic-embed-xs forward on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c1|c4] [--mode w8a8|w8a32|f32]
+
+Default workload: Arctic-embed-xs with int8 weights from the reference's
+quantiser, batch 256 per GPU, seq 128, valid lengths U{16..128}, leading CLS 101, body ids
+U{1000..30521}; the W8A8 tensor-core path.  Weak scaling: every rank runs its own 256 sequences
+(the 256*N-sequence global batch is sharded by work) and the embeddings are gathered to rank 0.
+
+`value`   : sequences/s over all ranks, inputs resident in HBM, device time (CUDA events around
+            each step's forward + gather, L2 flushed before every step), max over ranks.
+`e2e`     : the same metric through the public host API (tz_arctic_forward: host ids in, host
+            embeddings out; H2D + D2H inside the timed call), wall time of the synchronous call.
+`roofline`: the dominant kernel class, its algorithmic FLOPs (or bytes) per launch over its
+            average launch duration, measured with CUDA events recorded between launches on the
+            launching stream during the timed steps.
+`--impl reference`: the reference's CPU algorithm (C restatement; the Zig reference cannot be
+            built here) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "c1": dict(batch=8, seq=128, lmin=16, lmax=128, desc="configs[0] B=8 S=128"),
+    "c2": dict(batch=256, seq=128, lmin=16, lmax=128, desc="configs[1] B=256 S=128"),
+    "c4": dict(batch=8192, seq=512, lmin=32, lmax=512, desc="configs[3] B=8192 S=512"),
+}
+LIN_FLOP_PER_TOKEN = 2 * (4 * 384 * 384 + 2 * 384 * 1536)  # per layer
+CLASS_NAMES = ["embed_ln", "qkv_gemm", "attention", "oproj_gemm", "layernorm", "ffn1_gemm",
+               "ffn1_requant", "ffn2_gemm", "pool_l2"]
+
+
+def flop_useful(lens):
+    L = np.asarray(lens, np.float64)
+    return float(6 * (3538944 * L.sum() + 1536 * (L * L).sum()))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def traffic_table():
+    """Per-launch DRAM bytes from the committed ncu summary (profiles/ncu_traffic.txt), if any."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    out = {}
+    if os.path.exists(p):
+        for line in open(p):
+            line = line.strip()
+            if line and not line.startswith("#") and "=" in line:
+                k, v = line.split("=", 1)
+                try:
+                    out[k.strip()] = float(v.split()[0])
+                except ValueError:
+                    pass
+    return out
+
+
+class Clocks:
+    """Samples nvidia-smi every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_forward_timing(w_ckpt, ids, lens, mode_name, budget_s=12.0, max_seqs=None):
+    """Times the C restatement of the reference CPU forward (forwardBatchParallel semantics: one
+    sequence per task on all host threads) on a bounded sample.  Returns (seq/s, sample, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    blas = os.environ.get("TENZOR_BLAS_LIB")
+    if not blas:
+        cand = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs/libopenblasp-r0-59ffcd50.3.15.so"
+        if os.path.exists(cand):
+            os.environ["TENZOR_BLAS_LIB"] = cand
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+    om = O.OracleModel(w_ckpt)
+    mode = {"f32": O.MODE_F32, "w8a32": O.MODE_W8A32, "w8a8": O.MODE_W8A8}[mode_name]
+    threads = os.cpu_count() or 1
+    # probe: a small batch, then size the sample to ~budget_s
+    n0 = min(len(lens), max(threads, 8))
+    p, cu = _pack(ids[:n0], lens[:n0])
+    t0 = time.perf_counter()
+    om.forward(p, cu, mode, nthreads=threads)
+    dt = time.perf_counter() - t0
+    n = int(max(n0, min(len(lens), n0 * budget_s / max(dt, 1e-3))))
+    if max_seqs:
+        n = min(n, max_seqs)
+    p, cu = _pack(ids[:n], lens[:n])
+    t0 = time.perf_counter()
+    om.forward(p, cu, mode, nthreads=threads)
+    dt = time.perf_counter() - t0
+    sample = f"first {n} sequences of the batch ({int(cu[-1])} tokens), {O.blas_status()}"
+    return n / dt, sample, threads
+
+
+def _pack(ids, lens):
+    from tenzor_b200 import synthetic as S
+    return S.pack(ids, lens)
+
+
+def make_inputs(cfg, world):
+    from tenzor_b200 import synthetic as S
+    c = CONFIGS[cfg]
+    B = c["batch"] * (world if cfg != "c4" else 1)
+    ids, lens = S.token_batch(B, c["seq"], c["lmin"], c["lmax"], seed=7)
+    return ids, lens
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return 0
+    from tenzor_b200 import synthetic as S
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    w = S.arctic_weights(1234)
+    ck = O.quantize_checkpoint(w) if a.mode != "f32" else w
+    ids, lens = make_inputs(a.config, world)
+    ref_mode = "w8a32" if a.mode != "f32" else "f32"  # the reference's own int8 path is W8A32
+    vals = []
+    sample = ""
+    threads = os.cpu_count() or 1
+    per_step_budget = max(2.0, 150.0 / max(1, a.steps + a.warmup))
+    for i in range(a.warmup + a.steps):
+        v, sample, threads = cpu_forward_timing(ck, ids, lens, ref_mode, budget_s=per_step_budget)
+        if i >= a.warmup:
+            vals.append(v)
+    value = float(np.median(vals))
+    line = {
+        "impl": "reference", "metric": "Arctic-embed-xs seq/s @seq128 (int8 weights)" if a.mode != "f32" else "Arctic-embed-xs seq/s @seq128 (f32)",
+        "value": value, "unit": "seq/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if ref_mode == "f32" else "int8-weight/f32 (W8A32)", "data": "synthetic",
+        "config": {"workload": CONFIGS[a.config]["desc"], "mode": ref_mode, "global_batch": int(len(lens)),
+                   "seq_len": CONFIGS[a.config]["seq"], "parallelism": "host threads (one sequence per task)"},
+        "cpu_baseline": {"value": value, "unit": "seq/s", "cores": threads, "kind": "port",
+                         "sample": sample + "; C restatement of arctic.zig forwardBatchParallel (Zig reference unbuildable here)"},
+        "e2e": {"value": value, "unit": "seq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+    from tenzor_b200 import synthetic as S
+    from tenzor_b200 import _lib as L
+    from tenzor_b200.arctic import ArcticModel
+    from tenzor_b200.quantize import quantize_checkpoint
+    from tenzor_b200.runtime import Context
+    from tenzor_b200.shard import gather_to_rank0, shard_by_tokens
+    import ctypes as C
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    ctx = Context(local)
+    w = S.arctic_weights(1234)
+    ck = quantize_checkpoint(ctx, w) if a.mode != "f32" else w
+    model = ArcticModel.from_checkpoint(ctx, ck, a.mode)
+
+    ids, lens = make_inputs(a.config, world)
+    shards = shard_by_tokens(lens, world) if world > 1 else [np.arange(len(lens))]
+    mine = shards[rank]
+    l_ids, l_lens = ids[mine], lens[mine]
+    packed, cu = S.pack(l_ids, l_lens)
+    B, T, maxL = len(l_lens), int(cu[-1]), int(l_lens.max())
+    model.reserve(B, T)
+    d_ids = torch.from_numpy(packed.view(np.int32)).cuda()
+    d_cu = torch.from_numpy(cu).cuda()
+    d_out = torch.empty((B, 384), device="cuda", dtype=torch.float32)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)  # > 126 MB L2
+    stream = torch.cuda.current_stream()
+
+    def step():
+        model.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), B, T, maxL, d_out.data_ptr(),
+                             C.c_void_p(stream.cuda_stream))
+        if world > 1:
+            gather_to_rank0(d_out, mine, len(lens))
+
+    # warm-up (also captures nothing: the device path launches directly)
+    for _ in range(max(a.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    L.check(L.lib().tz_arctic_profile(model.handle, 1))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        for i in range(a.steps):
+            flush.zero_()
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = sum(s.elapsed_time(e) for s, e in evs)
+    ms_t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    cls_ms = (C.c_float * 9)()
+    cls_n = (C.c_int * 9)()
+    L.check(L.lib().tz_arctic_profile_read(model.handle, cls_ms, cls_n))
+    L.check(L.lib().tz_arctic_profile(model.handle, 0))
+    launches_per_fwd = int(sum(cls_n))
+
+    # end to end through the public host API (graph replay inside; H2D of ids + cu, D2H of out)
+    host_out = np.empty((B, 384), np.float32)
+    for _ in range(3):
+        model.forward_packed(packed, cu, out=host_out)
+    e2e_t = 0.0
+    for i in range(a.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.forward_packed(packed, cu, out=host_out)
+        e2e_t += time.perf_counter() - t0
+    e2e_t_t = torch.tensor([e2e_t], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_t_t, op=dist.ReduceOp.MAX)
+    e2e_t = float(e2e_t_t.item())
+
+    total_seqs = len(lens) * a.steps if world > 1 else B * a.steps
+    value = total_seqs / (ms / 1e3)
+    e2e_value = total_seqs / e2e_t
+
+    line = None
+    if rank == 0:
+        hbm, bf16, bf16_sus, src = peaks()
+        # dominant kernel class of the forward
+        per = [(cls_ms[c], c) for c in range(9) if cls_n[c] > 0]
+        dom_ms, dom = max(per)
+        avg_ms = dom_ms / cls_n[dom]
+        Tl = T
+        flops = {1: 2 * Tl * 384 * 1152, 3: 2 * Tl * 384 * 384, 5: 2 * Tl * 384 * 1536, 7: 2 * Tl * 1536 * 384,
+                 2: 4 * 384 * float((l_lens.astype(np.float64) ** 2).sum())}
+        int8 = a.mode == "w8a8"
+        if dom in flops:
+            bound, unit = "tensor", "TFLOP/s"
+            achieved = flops[dom] / (avg_ms / 1e3) / 1e12
+            if dom == 2:
+                peak, peak_note = bf16_sus, f"dense f16 = {src} bf16 sustained"
+            elif int8:
+                peak, peak_note = 2 * bf16_sus, f"int8 = 2 x {src} bf16 sustained (nominal int8:bf16 ratio)"
+            else:
+                peak, peak_note = bf16_sus, f"f16 = {src} bf16 sustained"
+        else:
+            bound, unit = "hbm", "GB/s"
+            byts = {0: Tl * 384 * (4 + 1 + 4) + Tl * 384 * 2, 4: Tl * 384 * (4 + 4 + 1) + Tl * 4,
+                    6: Tl * 1536 * 3 + Tl * 8, 8: B * 384 * 8}[dom]
+            achieved = byts / (avg_ms / 1e3) / 1e9
+            peak, peak_note = hbm, f"{src} HBM copy"
+        tr = traffic_table().get(f"{CLASS_NAMES[dom]}_{a.mode}_{a.config}")
+        dom_flops_or_bytes = flops.get(dom)
+        cfg = CONFIGS[a.config]
+        line = {
+            "metric": f"Arctic-embed-xs seq/s @seq{cfg['seq']} ({'int8 W8A8' if int8 else a.mode})",
+            "value": value, "unit": "seq/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (W8A8, int32 acc)" if int8 else ("f16 operands / f32 acc" if a.mode == "f32" else "int8 weights as f16 / f32 acc"),
+            "data": "synthetic (seeded N(0,0.02) weights, U ids / lengths)",
+            "config": {"workload": cfg["desc"] + (" per GPU" if world > 1 else ""), "model": "Arctic-embed-xs",
+                       "mode": a.mode, "global_batch": int(len(lens)), "per_gpu_batch": B, "tokens_per_gpu": T,
+                       "seq_len": cfg["seq"], "parallelism": f"sequence-sharded x{world}, gather to rank 0",
+                       "l2": "flushed (256 MB write) before every timed step",
+                       "useful_gflop_per_step": flop_useful(lens) / 1e9},
+            "roofline": {"kernel": CLASS_NAMES[dom], "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                         "frac": achieved / peak, "peak_source": peak_note, "traffic": tr,
+                         "per_launch_work": dom_flops_or_bytes, "avg_launch_ms": avg_ms,
+                         "class_ms_per_forward": {CLASS_NAMES[c]: round(cls_ms[c], 4) for c in range(9) if cls_n[c]}},
+            "e2e": {"value": e2e_value, "unit": "seq/s", "h2d_bytes_per_step": int(T * 4 + (B + 1) * 4),
+                    "d2h_bytes_per_step": int(B * 384 * 4)},
+            "gpu_launches": launches_per_fwd * a.steps,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not a.no_cpu:
+            v, sample, thr = cpu_forward_timing(ck, ids, lens, "w8a32" if a.mode != "f32" else "f32", budget_s=12.0)
+            line["cpu_baseline"] = {"value": v, "unit": "seq/s", "cores": thr, "kind": "port",
+                                    "sample": sample + "; reference CPU algorithm (W8A32 int8 path) restated in C"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    model.close()
+    ctx.close()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=list(CONFIGS))
+    ap.add_argument("--mode", default="w8a8", choices=["w8a8", "w8a32", "f32"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,223 @@
+/*
+ * tenzor_cuda.h -- C ABI of libtenzor_cuda.so, the sm_100a (B200) backend for the Arctic-embed-xs
+ * encoder hot path of tenzor.
+ *
+ * The reference (mattneel/tenzor) is Zig; its host code binds this header with `extern fn`
+ * (see INTEGRATION.md).  Every entry point names the reference function it replaces
+ * (path:line inside the reference project).  Conventions, mirroring the reference kernels:
+ *   - caller-owned, contiguous, row-major buffers plus explicit dimensions;
+ *   - Linear weights in PyTorch layout [out, in];
+ *   - int8 weights carry one IEEE-half scale per output row (quantize_arctic_xs.zig:94-115);
+ *   - every call returns a tz_status; tz_get_last_error() gives the message of the last failing
+ *     call on the calling thread (the reference's error unions, arctic.zig:194-201, become codes).
+ * Op-level entry points (tz_layernorm_last_dim ... tz_gather_rows) take DEVICE pointers and a
+ * stream and are asynchronous; the model entry points take HOST pointers and are synchronous
+ * unless noted.  There is no CPU fallback: without a usable sm_100 device every call fails with
+ * TZ_ECUDA or TZ_EUNSUPPORTED.
+ */
+#ifndef TENZOR_CUDA_H
+#define TENZOR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ------------------------------------------------------------------------------- */
+typedef enum {
+    TZ_OK = 0,
+    TZ_EINVAL = 1,       /* bad argument (shape, null pointer, id out of range)              */
+    TZ_ENOMEM = 2,       /* device allocation failed                                          */
+    TZ_ECUDA = 3,        /* CUDA runtime/driver error                                         */
+    TZ_ETIMEOUT = 4,     /* a bounded device-side wait expired; the kernel returned early     */
+    TZ_EUNSUPPORTED = 5, /* not supported on this device / combination                        */
+    TZ_EMISSING = 6      /* a required weight is missing (arctic.zig:194-196 MissingWeight)   */
+} tz_status;
+
+typedef struct tz_ctx_s* tz_ctx_t;     /* one device + one default stream + scratch arena */
+typedef struct tz_model_s* tz_model_t; /* device-resident Arctic-embed-xs weights + workspace */
+typedef void* tz_stream_t;             /* a cudaStream_t; NULL = the context's stream */
+
+/* Message of the last failing call on this thread ("" if none).  SPEC.md:876 tz_get_last_error. */
+const char* tz_get_last_error(void);
+/* Library version string and build flags. */
+const char* tz_version(void);
+
+/* ---- context ------------------------------------------------------------------------------ */
+/* Creates a context on CUDA device `device`.  Fails with TZ_EUNSUPPORTED unless the device is
+ * compute capability 10.0 (B200).  Replaces the CPU ThreadPool.create of main.zig:787-789. */
+int tz_cuda_create(int device, tz_ctx_t* out);
+int tz_cuda_destroy(tz_ctx_t ctx);
+int tz_cuda_synchronize(tz_ctx_t ctx);
+/* Device status word: non-zero when a kernel's bounded wait expired (bit 0) or a kernel bounds
+ * check fired (bit 1) since the last call.  Reading clears it. */
+int tz_cuda_check_status(tz_ctx_t ctx);
+int tz_cuda_sm_count(tz_ctx_t ctx);
+
+/* ---- device memory (SPEC.md:834-845 tz_tensor_from_data / copy_to_host) ------------------- */
+int tz_alloc(tz_ctx_t ctx, size_t bytes, void** dptr);
+int tz_free(tz_ctx_t ctx, void* dptr);
+int tz_upload(tz_ctx_t ctx, void* dst_device, const void* src_host, size_t bytes);
+int tz_download(tz_ctx_t ctx, void* dst_host, const void* src_device, size_t bytes);
+
+/* ---- Arctic-embed-xs model ---------------------------------------------------------------- */
+typedef enum {
+    TZ_QUANT_F32 = 0,   /* f32 checkpoint; GEMMs on tcgen05 kind::f16 (f16 operands, f32 acc) */
+    TZ_QUANT_W8A32 = 1, /* int8 checkpoint, f32 activations: the reference's int8 path        */
+    TZ_QUANT_W8A8 = 2   /* int8 checkpoint, per-token int8 activations, int32 accumulators    */
+} tz_quant_mode;
+
+/* MatWeight (arctic.zig:47-58): either f32 [rows, cols] or int8 [rows, cols] + half scale [rows].
+ * Exactly one of `f32` and `q8` is non-NULL. */
+typedef struct {
+    const float* f32;
+    const int8_t* q8;
+    const uint16_t* scale_f16;
+} tz_mat_weight;
+
+/* LayerWeights (arctic.zig:64-89). */
+typedef struct {
+    tz_mat_weight query, key, value, attn_output, intermediate, output;
+    const float *query_bias, *key_bias, *value_bias, *attn_output_bias, *intermediate_bias,
+        *output_bias;
+    const float *attn_ln_gamma, *attn_ln_beta, *output_ln_gamma, *output_ln_beta;
+} tz_arctic_layer;
+
+/* ModelWeights (arctic.zig:92-110), config arctic.zig:29-42 (6 layers fixed). */
+typedef struct {
+    tz_mat_weight word_embeddings, position_embeddings, token_type_embeddings;
+    const float *ln_gamma, *ln_beta;
+    tz_arctic_layer layers[6];
+} tz_arctic_weights;
+
+/* Copies the host weights to the device in the layout the kernels want (QKV concatenated,
+ * f16 or int8 operands, f32 scales).  `mode` must agree with the weights: TZ_QUANT_F32 needs
+ * f32 Linear weights; the int8 modes need q8 Linear weights (embedding tables may be either).
+ * Replaces ModelWeights.fromSafeTensors, arctic.zig:113-166 / getMatWeightAlloc 258-287. */
+int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_t* out);
+/* Same, reading a safetensors checkpoint (f32, or I8 + '<name>.scale' F16 as written by
+ * quantize_arctic_xs.zig), with or without the "bert." prefix.  safetensors.zig:275-295. */
+int tz_arctic_load_safetensors(tz_ctx_t ctx, const char* path, int mode, tz_model_t* out);
+int tz_arctic_free(tz_model_t model);
+/* Reserves device workspace for up to max_batch sequences and max_tokens packed tokens
+ * (InferenceContext.init, arctic.zig:424-460).  Forward calls grow it on demand otherwise. */
+int tz_arctic_reserve(tz_model_t model, int max_batch, int64_t max_tokens);
+
+/* Batch forward over ragged sequences (forwardBatchParallel, arctic.zig:959-1013, and forward,
+ * arctic.zig:874-898): ids_packed holds the B sequences back to back, cu_seqlens[B+1] their
+ * offsets (cu_seqlens[0] = 0, 1 <= length <= 512, ids < 30522).  Writes the L2-normalised CLS
+ * embedding of each sequence to out[B, 384].  HOST pointers; synchronous. */
+int tz_arctic_forward(tz_model_t model, const uint32_t* ids_packed, const int32_t* cu_seqlens,
+                      int batch, float* out);
+/* Padded batch: ids[B, S] row-major, lengths[B] (the masked-batch form; tokens at positions
+ * >= length are ignored).  HOST pointers; synchronous. */
+int tz_arctic_forward_padded(tz_model_t model, const uint32_t* ids, const int32_t* lengths,
+                             int batch, int seq, float* out);
+/* Device-resident variant: all pointers on the device, asynchronous on `stream`.  total_tokens =
+ * cu_seqlens[B] and max_len = max length must be passed by the caller (no host read-back). */
+int tz_arctic_forward_device(tz_model_t model, const uint32_t* d_ids_packed,
+                             const int32_t* d_cu_seqlens, int batch, int64_t total_tokens,
+                             int max_len, float* d_out, tz_stream_t stream);
+/* Debug/parity hook: copies the device hidden state [T, 384] after stage `stage` (0 = after the
+ * embeddings, l+1 = after layer l) of the LAST forward into host `out`.  Capture is switched on
+ * by a first call (which returns TZ_EINVAL) and applies from the next forward. */
+int tz_arctic_debug_hidden(tz_model_t model, int stage, float* out, int64_t total_tokens);
+/* Debug/parity hook (W8A8): copies an int8 GEMM operand of layer 0 captured in the LAST forward
+ * (which: 0 = QKV input, 1 = attention-output-projection input, 2 = FFN1 input, 3 = FFN2 input;
+ * int8 [T, K] with K = 384, or 1536 for which = 3, plus its per-row f32 scale [T]).  Capture is
+ * switched on by a first call (which returns TZ_EINVAL) and applies from the next forward. */
+int tz_arctic_debug_operand(tz_model_t model, int which, int8_t* q_out, float* scale_out,
+                            int64_t total_tokens);
+
+/* Kernel timing of the forward: when enabled, CUDA events are recorded on the launching stream
+ * between consecutive launches (inside the captured graph too).  tz_arctic_profile_read returns,
+ * for the LAST forward, the summed milliseconds and the launch count per kernel class:
+ * 0 embedding+LN, 1 QKV GEMM, 2 attention, 3 attention-output GEMM, 4 LayerNorm, 5 FFN1 GEMM,
+ * 6 FFN1 requantisation (W8A8), 7 FFN2 GEMM, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
+#define TZ_PROF_CLASSES 9
+int tz_arctic_profile(tz_model_t model, int enable);
+int tz_arctic_profile_read(tz_model_t model, float* ms, int* launches);
+
+/* ---- op-level kernels (device pointers, async on `stream`) ------------------------------- */
+/* Epilogue / unary op codes (OpTag subset of expr.zig:19-135 used by codegen.zig:228-244). */
+typedef enum {
+    TZ_OP_ADD = 1, /* bias add (matmul epilogue) */
+    TZ_OP_RELU = 2,
+    TZ_OP_GELU = 3, /* simd.zig gelu: tanh(x) = 2*sigmoid(2x)-1 */
+    TZ_OP_SIGMOID = 4,
+    TZ_OP_TANH = 5,
+    TZ_OP_EXP = 6,
+    TZ_OP_NEG = 7,
+    TZ_OP_ABS = 8,
+    TZ_OP_SILU = 9,
+    TZ_OP_LOG = 10,
+    TZ_OP_SQRT = 11,
+    TZ_OP_RSQRT = 12,
+    TZ_OP_SIN = 13,
+    TZ_OP_COS = 14
+} tz_op;
+
+typedef enum { TZ_RED_SUM = 0, TZ_RED_MEAN = 1, TZ_RED_PROD = 2, TZ_RED_MAX = 3, TZ_RED_MIN = 4 } tz_reduce_op;
+
+/* layerNormLastDim, layernorm.zig:26-116 (two-pass mean/variance).  x and y may alias. */
+int tz_layernorm_last_dim(tz_ctx_t ctx, const float* x, const float* gamma, const float* beta,
+                          float* y, int64_t rows, int cols, float eps, tz_stream_t stream);
+/* softmaxLastAxis with optional additive mask [rows, cols] (softmax.zig:20-155); mask may be
+ * NULL.  x and y may alias. */
+int tz_softmax_last_axis(tz_ctx_t ctx, const float* x, const float* mask, float* y, int64_t rows,
+                         int cols, tz_stream_t stream);
+/* Attention-shaped masked softmax: x [groups, rows_per_group, cols]; in group g only the first
+ * key_len[g] columns are valid (others get probability 0), the additive-mask form of
+ * softmax.zig:423-440 with mask = -inf beyond the valid length. */
+int tz_softmax_keylen(tz_ctx_t ctx, const float* x, const int32_t* key_len, float* y,
+                      int64_t groups, int rows_per_group, int cols, tz_stream_t stream);
+/* linearProjection f32 arm, arctic.zig:599-620 (matmulTransposeB matmul.zig:54-77 + bias):
+ * y[m,n] = x[m,k] w[n,k]^T (+ bias) [+ residual].  tcgen05 kind::tf32. */
+int tz_linear_f32(tz_ctx_t ctx, const float* x, const float* w, const float* bias,
+                  const float* residual, float* y, int m, int k, int n, tz_stream_t stream);
+/* matmulTransposeB_f32_i8_rowScale_bias, matmul_w8a32.zig:14-58:
+ * y = (x w_q^T) * f32(scale[j]) + bias[j].  Needs scratch from the context arena. */
+int tz_linear_w8a32(tz_ctx_t ctx, const float* x, const int8_t* wq, const uint16_t* scale_f16,
+                    const float* bias, float* y, int m, int k, int n, tz_stream_t stream);
+/* W8A8 linear: per-token int8 quantisation of x, int8 x int8 -> int32 on tcgen05 kind::i8,
+ * y = float(acc) * (sx[i] * f32(scale[j])) + bias[j].  No reference counterpart (the reference
+ * int8 path is W8A32); scratch from the context arena. */
+int tz_linear_w8a8(tz_ctx_t ctx, const float* x, const int8_t* wq, const uint16_t* scale_f16,
+                   const float* bias, float* y, int m, int k, int n, tz_stream_t stream);
+/* Raw int8 GEMM: c[m,n] = a[m,k] w[n,k]^T in int32 (bit-exact accumulators).  k % 16 == 0. */
+int tz_gemm_i8_i32(tz_ctx_t ctx, const int8_t* a, const int8_t* w, int32_t* c, int m, int k,
+                   int n, tz_stream_t stream);
+/* Per-row symmetric weight quantiser of quantize_arctic_xs.zig:94-115 (f16 scales). */
+int tz_quantize_weight_rows(tz_ctx_t ctx, const float* w, int8_t* q, uint16_t* scale_f16,
+                            int64_t rows, int cols, tz_stream_t stream);
+/* Per-token activation quantiser used by the W8A8 path: s = max|x|/127 (1 if 0),
+ * q = clamp(round(x * (1/s)), -127, 127). */
+int tz_quantize_act_rows(tz_ctx_t ctx, const float* x, int8_t* q, float* scale, int64_t rows,
+                         int cols, tz_stream_t stream);
+/* FusedMatmulEpilogueKernel, codegen.zig:78-147: c = ops(a @ b) with b [k,n] (trans_b = 0) or
+ * [n,k] (trans_b = 1); ops applied in order, TZ_OP_ADD adds bias[j].  n_ops <= 8.
+ * tcgen05 kind::tf32; a trans_b = 0 operand is transposed through context scratch first. */
+int tz_matmul_epilogue(tz_ctx_t ctx, const float* a, const float* b, int trans_b,
+                       const float* bias, const int* ops, int n_ops, float* c, int m, int k, int n,
+                       tz_stream_t stream);
+/* Elementwise chain exp((a + b) * c), b broadcast along rows ([cols]); executor.zig:114-197
+ * evaluation of UnaryExpr(exp, BinaryExpr(mul, BinaryExpr(add, a, b), c)) in one pass. */
+int tz_ew_add_mul_exp(tz_ctx_t ctx, const float* a, const float* b_row, const float* c, float* out,
+                      int64_t rows, int cols, tz_stream_t stream);
+/* General fused elementwise chain (FusedElementwiseKernel, codegen.zig:15-74): out = ops(x). */
+int tz_ew_unary_chain(tz_ctx_t ctx, const float* x, float* out, int64_t n, const int* ops,
+                      int n_ops, tz_stream_t stream);
+/* FusedReduceKernel, codegen.zig:151-205: *out (device) = reduce(pre_ops(x)). */
+int tz_reduce(tz_ctx_t ctx, int reduce_op, const int* pre_ops, int n_pre, const float* x,
+              int64_t n, float* out, tz_stream_t stream);
+/* gather, gather.zig:15-57: out[i,:] = table[ids[i],:]; ids out of range -> TZ_EINVAL via the
+ * device status word (the row is zero-filled). */
+int tz_gather_rows(tz_ctx_t ctx, const float* table, int64_t table_rows, const uint32_t* ids,
+                   int64_t n_ids, int cols, float* out, tz_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TENZOR_CUDA_H */

@@ -1,0 +1,115 @@
+"""ctypes bindings of include/tenzor_cuda.h (libtenzor_cuda.so, built in-tree).
+
+There is no fallback: if the library is missing or cannot load, importing a compute entry point
+raises.  Build it with ``python -m tenzor_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libtenzor_cuda.so")
+
+TZ_OK, TZ_EINVAL, TZ_ENOMEM, TZ_ECUDA, TZ_ETIMEOUT, TZ_EUNSUPPORTED, TZ_EMISSING = range(7)
+QUANT_F32, QUANT_W8A32, QUANT_W8A8 = 0, 1, 2
+OP = {"add": 1, "relu": 2, "gelu": 3, "sigmoid": 4, "tanh": 5, "exp": 6, "neg": 7, "abs": 8,
+      "silu": 9, "log": 10, "sqrt": 11, "rsqrt": 12, "sin": 13, "cos": 14}
+RED = {"sum": 0, "mean": 1, "prod": 2, "max": 3, "min": 4}
+
+# Every symbol include/tenzor_cuda.h declares (checked by tests/test_abi.py).
+EXPORTS = [
+    "tz_get_last_error", "tz_version", "tz_cuda_create", "tz_cuda_destroy", "tz_cuda_synchronize",
+    "tz_cuda_check_status", "tz_cuda_sm_count", "tz_alloc", "tz_free", "tz_upload", "tz_download",
+    "tz_arctic_load", "tz_arctic_load_safetensors", "tz_arctic_free", "tz_arctic_reserve",
+    "tz_arctic_forward", "tz_arctic_forward_padded", "tz_arctic_forward_device",
+    "tz_arctic_debug_hidden", "tz_arctic_debug_operand", "tz_arctic_profile", "tz_arctic_profile_read", "tz_layernorm_last_dim",
+    "tz_softmax_last_axis", "tz_softmax_keylen", "tz_linear_f32", "tz_linear_w8a32",
+    "tz_linear_w8a8", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
+    "tz_matmul_epilogue", "tz_ew_add_mul_exp", "tz_ew_unary_chain", "tz_reduce", "tz_gather_rows",
+]
+
+
+class TenzorError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[tz status {code}] {msg}")
+        self.code = code
+
+
+P = C.c_void_p
+
+
+class MatWeight(C.Structure):
+    _fields_ = [("f32", P), ("q8", P), ("scale_f16", P)]
+
+
+class ArcticLayer(C.Structure):
+    _fields_ = [(n, MatWeight) for n in ("query", "key", "value", "attn_output", "intermediate", "output")]
+    _fields_ += [(n, P) for n in ("query_bias", "key_bias", "value_bias", "attn_output_bias",
+                                  "intermediate_bias", "output_bias", "attn_ln_gamma", "attn_ln_beta",
+                                  "output_ln_gamma", "output_ln_beta")]
+
+
+class ArcticWeights(C.Structure):
+    _fields_ = [("word_embeddings", MatWeight), ("position_embeddings", MatWeight),
+                ("token_type_embeddings", MatWeight), ("ln_gamma", P), ("ln_beta", P),
+                ("layers", ArcticLayer * 6)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `python -m tenzor_b200.build` "
+                              "(there is no CPU fallback)")
+        _lib = C.CDLL(LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def _declare(L):
+    i, i64, u = C.c_int, C.c_int64, C.c_size_t
+    L.tz_get_last_error.restype = C.c_char_p
+    L.tz_version.restype = C.c_char_p
+    sig = {
+        "tz_cuda_create": [i, C.POINTER(P)],
+        "tz_cuda_destroy": [P], "tz_cuda_synchronize": [P], "tz_cuda_check_status": [P],
+        "tz_cuda_sm_count": [P],
+        "tz_alloc": [P, u, C.POINTER(P)], "tz_free": [P, P],
+        "tz_upload": [P, P, P, u], "tz_download": [P, P, P, u],
+        "tz_arctic_load": [P, C.POINTER(ArcticWeights), i, C.POINTER(P)],
+        "tz_arctic_load_safetensors": [P, C.c_char_p, i, C.POINTER(P)],
+        "tz_arctic_free": [P], "tz_arctic_reserve": [P, i, i64],
+        "tz_arctic_forward": [P, P, P, i, P],
+        "tz_arctic_forward_padded": [P, P, P, i, i, P],
+        "tz_arctic_forward_device": [P, P, P, i, i64, i, P, P],
+        "tz_arctic_debug_hidden": [P, i, P, i64],
+        "tz_arctic_debug_operand": [P, i, P, P, i64],
+        "tz_arctic_profile": [P, i], "tz_arctic_profile_read": [P, P, P],
+        "tz_layernorm_last_dim": [P, P, P, P, P, i64, i, C.c_float, P],
+        "tz_softmax_last_axis": [P, P, P, P, i64, i, P],
+        "tz_softmax_keylen": [P, P, P, P, i64, i, i, P],
+        "tz_linear_f32": [P, P, P, P, P, P, i, i, i, P],
+        "tz_linear_w8a32": [P, P, P, P, P, P, i, i, i, P],
+        "tz_linear_w8a8": [P, P, P, P, P, P, i, i, i, P],
+        "tz_gemm_i8_i32": [P, P, P, P, i, i, i, P],
+        "tz_quantize_weight_rows": [P, P, P, P, i64, i, P],
+        "tz_quantize_act_rows": [P, P, P, P, i64, i, P],
+        "tz_matmul_epilogue": [P, P, P, i, P, P, i, P, i, i, i, P],
+        "tz_ew_add_mul_exp": [P, P, P, P, P, i64, i, P],
+        "tz_ew_unary_chain": [P, P, P, i64, P, i, P],
+        "tz_reduce": [P, i, P, i, P, i64, P, P],
+        "tz_gather_rows": [P, P, i64, P, i64, i, P, P],
+    }
+    for name, args in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = C.c_int
+
+
+def check(rc: int):
+    if rc != TZ_OK:
+        raise TenzorError(rc, lib().tz_get_last_error().decode(errors="replace"))

@@ -1,0 +1,836 @@
+// tz_arctic.cu -- Arctic-embed-xs forward on sm_100a: model kernels (embedding + LayerNorm,
+// LayerNorm with the next GEMM's operand fused, per-token requantisation of the FFN intermediate,
+// CLS pooling + L2 norm) and the host orchestration behind tz_arctic_*.
+//
+// Reference call stack replaced (arctic.zig): forward 874-898 -> embeddingsImpl 543-585 ->
+// encoder 830-848 -> transformerBlock 814-826 -> selfAttention 639-747 / feedForward 760-810 ->
+// l2Normalize 851-863; forwardBatchParallel 959-1013 becomes one packed batch on the device.
+//
+// Data layout in HBM (T = packed tokens, row-major):
+//   X    f32 [T,384]   residual stream (LayerNorm outputs)
+//   XA   f16 [T,384]   GEMM operand copy of X (F32 / W8A32)   | int8 [T,384] + xs f32 [T] (W8A8)
+//   QKV  f16 [T,1152]  Q | K | V, head h at columns h*32 of each third
+//   OA   f16 [T,384]   attention output (F32 / W8A32)        | int8 + os [T] (W8A8)
+//   Y    f32 [T,384]   GEMM + bias + residual, LayerNorm input
+//   H    f16 [T,1536]  GELU(FFN1)                              (+ int8 HQ + hs [T] for W8A8)
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "tz_internal.h"
+#include "tz_ptx.cuh"
+#include "tz_rowops.cuh"
+
+namespace tz {
+int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int batch, int max_len, void* out_h,
+                     int8_t* out_q, float* out_s, cudaStream_t s);
+int launch_f32_to_f16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s);
+int launch_i8_to_f16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s);
+int launch_f16bits_to_f32(tz_ctx_t ctx, const uint16_t* x, float* y, long long n, cudaStream_t s);
+
+namespace {
+
+constexpr int kH = 384, kF = 1536, kV = 30522, kP = 512, kLayers = 6;
+constexpr float kEps = 1e-12f;  // arctic.zig:37
+
+// AUX: 0 = f16 copy, 1 = int8 + per-token scale.
+template <int AUX>
+__device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __restrict__ g, const float* __restrict__ b,
+                                              float* xo, void* aux, float* aux_s, long long row, int lane) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 12; ++i) s += v[i];
+    const float mean = warp_sum(s) / 384.0f;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+        const float d = v[i] - mean;
+        q += d * d;
+    }
+    const float inv_std = 1.0f / sqrtf(warp_sum(q) / 384.0f + kEps);
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int col = c * 128 + lane * 4;
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(g + col));
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(b + col));
+        v[4 * c + 0] = (v[4 * c + 0] - mean) * inv_std * gg.x + bb.x;
+        v[4 * c + 1] = (v[4 * c + 1] - mean) * inv_std * gg.y + bb.y;
+        v[4 * c + 2] = (v[4 * c + 2] - mean) * inv_std * gg.z + bb.z;
+        v[4 * c + 3] = (v[4 * c + 3] - mean) * inv_std * gg.w + bb.w;
+        *reinterpret_cast<float4*>(xo + row * kH + col) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[4 * c]), fabsf(v[4 * c + 1])), fmaxf(fabsf(v[4 * c + 2]), fabsf(v[4 * c + 3]))));
+    }
+    if constexpr (AUX == 0) {
+        __half* a = static_cast<__half*>(aux) + row * kH;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const int col = c * 128 + lane * 4;
+            uint2 pk;
+            pk.x = tzp::pack_half2(v[4 * c], v[4 * c + 1]);
+            pk.y = tzp::pack_half2(v[4 * c + 2], v[4 * c + 3]);
+            *reinterpret_cast<uint2*>(a + col) = pk;
+        }
+    } else {
+        amax = warp_max(amax);
+        const float sc = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+        const float inv = __fdiv_rn(1.0f, sc);
+        int8_t* a = static_cast<int8_t*>(aux) + row * kH;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const int col = c * 128 + lane * 4;
+            uint32_t w = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(v[4 * c + i], inv))) << (8 * i);
+            *reinterpret_cast<uint32_t*>(a + col) = w;
+        }
+        if (lane == 0) aux_s[row] = sc;
+    }
+}
+
+// LayerNorm of Y (GEMM output incl. bias + residual) -> X and the next GEMM's operand.
+template <int AUX>
+__global__ void ln_model_kernel(const float* __restrict__ y, const float* __restrict__ g, const float* __restrict__ b,
+                                float* __restrict__ xo, void* aux, float* aux_s, long long rows) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float v[12];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float4 t = *reinterpret_cast<const float4*>(y + row * kH + c * 128 + lane * 4);
+        v[4 * c] = t.x;
+        v[4 * c + 1] = t.y;
+        v[4 * c + 2] = t.z;
+        v[4 * c + 3] = t.w;
+    }
+    ln_finish_row<AUX>(v, g, b, xo, aux, aux_s, row, lane);
+}
+
+struct EmbTables {
+    const float* word_f;
+    const int8_t* word_q;
+    const float* word_s;
+    const float* pos_f;
+    const int8_t* pos_q;
+    const float* pos_s;
+    const float* type_f;  // row 0 used (arctic.zig:557)
+};
+
+__device__ __forceinline__ void emb_load(float (&v)[12], const float* f, const int8_t* q, const float* s, int row,
+                                         int lane, bool add) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int col = c * 128 + lane * 4;
+        float4 t;
+        if (f) {
+            t = __ldg(reinterpret_cast<const float4*>(f + static_cast<long long>(row) * kH + col));
+        } else {
+            const char4 qq = __ldg(reinterpret_cast<const char4*>(q + static_cast<long long>(row) * kH + col));
+            const float sc = __ldg(s + row);
+            t = make_float4(__fmul_rn(static_cast<float>(qq.x), sc), __fmul_rn(static_cast<float>(qq.y), sc),
+                            __fmul_rn(static_cast<float>(qq.z), sc), __fmul_rn(static_cast<float>(qq.w), sc));
+        }
+        if (add) {
+            v[4 * c] += t.x;
+            v[4 * c + 1] += t.y;
+            v[4 * c + 2] += t.z;
+            v[4 * c + 3] += t.w;
+        } else {
+            v[4 * c] = t.x;
+            v[4 * c + 1] = t.y;
+            v[4 * c + 2] = t.z;
+            v[4 * c + 3] = t.w;
+        }
+    }
+}
+
+// embeddingsImpl, arctic.zig:543-585: word[id] + pos[p] + type[0], then LayerNorm.  One CTA per
+// sequence, warp per token.  Ids >= vocab raise the bounds bit and embed row 0.
+template <int AUX>
+__global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, EmbTables t,
+                                const float* __restrict__ g, const float* __restrict__ b, float* __restrict__ xo,
+                                void* aux, float* aux_s, int* status) {
+    const int seq = blockIdx.x;
+    const int s0 = cu[seq], L = cu[seq + 1] - s0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int p = warp; p < L; p += nw) {
+        const long long row = s0 + p;
+        uint32_t id = ids[row];
+        if (id >= static_cast<uint32_t>(kV)) {
+            if (lane == 0) atomicOr(status, TZ_DEV_BOUNDS);
+            id = 0;
+        }
+        const int pos = p < kP ? p : kP - 1;
+        float v[12];
+        emb_load(v, t.word_f, t.word_q, t.word_s, static_cast<int>(id), lane, false);
+        emb_load(v, t.pos_f, t.pos_q, t.pos_s, pos, lane, true);
+        emb_load(v, t.type_f, nullptr, nullptr, 0, lane, true);
+        ln_finish_row<AUX>(v, g, b, xo, aux, aux_s, row, lane);
+    }
+}
+
+// W8A8: H f16 [T,1536] with its row max (float bits, from the FFN1 epilogue) -> int8 + scale;
+// resets the row max for the next layer.
+__global__ void quant_h_kernel(const __half* __restrict__ h, unsigned* __restrict__ hmax, int8_t* __restrict__ q,
+                               float* __restrict__ qs, long long rows) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float m = __uint_as_float(hmax[row]);
+    const float sc = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
+    const float inv = __fdiv_rn(1.0f, sc);
+    const __half* hr = h + row * kF;
+    int8_t* qr = q + row * kF;
+#pragma unroll
+    for (int c = 0; c < 6; ++c) {  // 1536 = 6 x 32 lanes x 8
+        const int col = c * 256 + lane * 8;
+        const uint4 raw = *reinterpret_cast<const uint4*>(hr + col);
+        const __half* hv = reinterpret_cast<const __half*>(&raw);
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w0 |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(__half2float(hv[i]), inv))) << (8 * i);
+            w1 |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(__half2float(hv[i + 4]), inv))) << (8 * i);
+        }
+        *reinterpret_cast<uint2*>(qr + col) = make_uint2(w0, w1);
+    }
+    __syncwarp();
+    if (lane == 0) {
+        qs[row] = sc;
+        hmax[row] = 0u;
+    }
+}
+
+// CLS pooling + l2Normalize (arctic.zig:851-863, forward 894-897): warp per sequence.
+__global__ void pool_l2_kernel(const float* __restrict__ x, const int* __restrict__ cu, float* __restrict__ out,
+                               int batch) {
+    const int seq = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (seq >= batch) return;
+    const float* r = x + static_cast<long long>(cu[seq]) * kH;
+    float v[12];
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float4 t = *reinterpret_cast<const float4*>(r + c * 128 + lane * 4);
+        v[4 * c] = t.x;
+        v[4 * c + 1] = t.y;
+        v[4 * c + 2] = t.z;
+        v[4 * c + 3] = t.w;
+        s += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+    }
+    const float norm = sqrtf(warp_sum(s));
+    float* o = out + static_cast<long long>(seq) * kH;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        float4 t = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        if (norm > 1e-12f) {
+            t.x /= norm;
+            t.y /= norm;
+            t.z /= norm;
+            t.w /= norm;
+        }
+        *reinterpret_cast<float4*>(o + c * 128 + lane * 4) = t;
+    }
+}
+
+inline int rows_grid(long long rows) { return static_cast<int>((rows * 32 + 255) / 256); }
+
+}  // namespace
+}  // namespace tz
+
+using namespace tz;
+
+// ------------------------------------------------------------------------------------------------
+// Model object
+// ------------------------------------------------------------------------------------------------
+struct DevLayer {
+    void* wqkv = nullptr;  // [1152,384] f16 or int8
+    void* wo = nullptr;    // [384,384]
+    void* w1 = nullptr;    // [1536,384]
+    void* w2 = nullptr;    // [384,1536]
+    float *bqkv = nullptr, *bo = nullptr, *b1 = nullptr, *b2 = nullptr;
+    float *sqkv = nullptr, *so = nullptr, *s1 = nullptr, *s2 = nullptr;  // column scales (int8 modes)
+    float *ln1g = nullptr, *ln1b = nullptr, *ln2g = nullptr, *ln2b = nullptr;
+};
+
+struct tz_model_s {
+    tz_ctx_t ctx = nullptr;
+    int mode = TZ_QUANT_F32;
+    std::vector<void*> allocs;  // every device allocation owned by the model
+    EmbTables emb{};
+    float *emb_g = nullptr, *emb_b = nullptr;
+    DevLayer layers[kLayers];
+    // workspace
+    int cap_batch = 0;
+    int64_t cap_tokens = 0;
+    std::vector<void*> ws;
+    uint32_t* d_ids = nullptr;
+    int* d_cu = nullptr;
+    float *X = nullptr, *Y = nullptr, *xs = nullptr, *os = nullptr, *hs = nullptr, *out = nullptr;
+    void *XA = nullptr, *QKV = nullptr, *OA = nullptr, *Hh = nullptr, *HQ = nullptr;
+    unsigned* hmax = nullptr;
+    uint32_t* h_ids = nullptr;  // pinned staging
+    int* h_cu = nullptr;
+    float* h_out = nullptr;
+    // padded-input staging
+    uint32_t* d_pad_ids = nullptr;
+    int* d_pad_lens = nullptr;
+    int64_t cap_pad = 0;
+    // debug
+    bool keep_stages = false;
+    float* d_stages = nullptr;  // [7, cap_tokens, 384] when keep_stages
+    int8_t* d_opq[4] = {nullptr, nullptr, nullptr, nullptr};  // W8A8 layer-0 GEMM operands
+    float* d_ops[4] = {nullptr, nullptr, nullptr, nullptr};
+    int64_t last_T = 0;
+    // kernel-class timing: events around every launch of the forward (recorded in graphs too)
+    bool profile = false;
+    std::vector<cudaEvent_t> ev;  // kMaxLaunch + 1
+    int ev_n = 0;                 // events recorded by the last enqueue
+    int ev_cls[64] = {0};         // class of launch i
+    // graph cache for the host-pointer forward
+    cudaGraphExec_t graph = nullptr;
+    int g_batch = -1, g_maxlen = -1;
+    int64_t g_tokens = -1;
+    bool use_graph = true;
+};
+
+namespace {
+
+int dalloc(tz_model_s* m, std::vector<void*>& list, size_t bytes, void** p) {
+    TZ_CUDA(cudaMalloc(p, bytes ? bytes : 16));
+    list.push_back(*p);
+    return TZ_OK;
+}
+
+int upload_raw(tz_model_s* m, const void* src, size_t bytes, void** dst) {
+    int rc = dalloc(m, m->allocs, bytes, dst);
+    if (rc) return rc;
+    TZ_CUDA(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+    return TZ_OK;
+}
+
+int upload_f32(tz_model_s* m, const float* src, size_t n, float** dst, const char* what) {
+    TZ_CHECK(src, TZ_EMISSING, "missing weight: %s", what);
+    return upload_raw(m, src, n * sizeof(float), reinterpret_cast<void**>(dst));
+}
+
+// A Linear weight [rows, cols] into the device operand format of the mode, at row offset `row0` of
+// a (possibly concatenated) destination with `total_rows` rows.
+int upload_linear(tz_model_s* m, const tz_mat_weight& w, int rows, int cols, void* dst, int row0, float* scale_dst,
+                  const char* what) {
+    cudaStream_t s = m->ctx->stream;
+    if (m->mode == TZ_QUANT_F32) {
+        TZ_CHECK(w.f32, TZ_EINVAL, "%s: mode F32 needs f32 weights", what);
+        void* tmp = nullptr;
+        TZ_CUDA(cudaMalloc(&tmp, sizeof(float) * rows * cols));
+        cudaMemcpy(tmp, w.f32, sizeof(float) * rows * cols, cudaMemcpyHostToDevice);
+        int rc = launch_f32_to_f16(m->ctx, static_cast<float*>(tmp), static_cast<__half*>(dst) + static_cast<long long>(row0) * cols,
+                                   static_cast<long long>(rows) * cols, s);
+        cudaStreamSynchronize(s);
+        cudaFree(tmp);
+        return rc;
+    }
+    TZ_CHECK(w.q8 && w.scale_f16, TZ_EINVAL, "%s: int8 modes need int8 weights with a half scale", what);
+    void* tq = nullptr;
+    void* ts = nullptr;
+    TZ_CUDA(cudaMalloc(&tq, static_cast<size_t>(rows) * cols));
+    TZ_CUDA(cudaMalloc(&ts, sizeof(uint16_t) * rows));
+    cudaMemcpy(tq, w.q8, static_cast<size_t>(rows) * cols, cudaMemcpyHostToDevice);
+    cudaMemcpy(ts, w.scale_f16, sizeof(uint16_t) * rows, cudaMemcpyHostToDevice);
+    int rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), scale_dst + row0, rows, s);
+    if (!rc) {
+        if (m->mode == TZ_QUANT_W8A8)
+            TZ_CUDA(cudaMemcpyAsync(static_cast<int8_t*>(dst) + static_cast<long long>(row0) * cols, tq,
+                                    static_cast<size_t>(rows) * cols, cudaMemcpyDeviceToDevice, s));
+        else  // W8A32: int8 values widened exactly to f16; the scale is applied in the epilogue
+            rc = launch_i8_to_f16(m->ctx, static_cast<int8_t*>(tq), static_cast<__half*>(dst) + static_cast<long long>(row0) * cols,
+                                  static_cast<long long>(rows) * cols, s);
+    }
+    cudaStreamSynchronize(s);
+    cudaFree(tq);
+    cudaFree(ts);
+    return rc;
+}
+
+int upload_table(tz_model_s* m, const tz_mat_weight& w, int rows, const float** f, const int8_t** q, const float** s,
+                 const char* what) {
+    *f = nullptr;
+    *q = nullptr;
+    *s = nullptr;
+    if (w.f32) {
+        float* d = nullptr;
+        int rc = upload_f32(m, w.f32, static_cast<size_t>(rows) * kH, &d, what);
+        *f = d;
+        return rc;
+    }
+    TZ_CHECK(w.q8 && w.scale_f16, TZ_EMISSING, "missing weight: %s", what);
+    void* dq = nullptr;
+    int rc = upload_raw(m, w.q8, static_cast<size_t>(rows) * kH, &dq);
+    if (rc) return rc;
+    void* ts = nullptr;
+    float* ds = nullptr;
+    rc = dalloc(m, m->allocs, sizeof(float) * rows, reinterpret_cast<void**>(&ds));
+    if (rc) return rc;
+    TZ_CUDA(cudaMalloc(&ts, sizeof(uint16_t) * rows));
+    cudaMemcpy(ts, w.scale_f16, sizeof(uint16_t) * rows, cudaMemcpyHostToDevice);
+    rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), ds, rows, m->ctx->stream);
+    cudaStreamSynchronize(m->ctx->stream);
+    cudaFree(ts);
+    *q = static_cast<int8_t*>(dq);
+    *s = ds;
+    return rc;
+}
+
+void free_workspace(tz_model_s* m) {
+    if (m->graph) {
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    for (void* p : m->ws) cudaFree(p);
+    m->ws.clear();
+    if (m->h_ids) cudaFreeHost(m->h_ids);
+    if (m->h_cu) cudaFreeHost(m->h_cu);
+    if (m->h_out) cudaFreeHost(m->h_out);
+    m->h_ids = nullptr;
+    m->h_cu = nullptr;
+    m->h_out = nullptr;
+    m->cap_batch = 0;
+    m->cap_tokens = 0;
+    m->d_stages = nullptr;
+    for (int i = 0; i < 4; ++i) {
+        m->d_opq[i] = nullptr;
+        m->d_ops[i] = nullptr;
+    }
+}
+
+int reserve(tz_model_s* m, int batch, int64_t tokens) {
+    if (batch <= m->cap_batch && tokens <= m->cap_tokens && (!m->keep_stages || m->d_stages)) return TZ_OK;
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    const int nb = std::max(batch, m->cap_batch);
+    const int64_t nt = std::max<int64_t>(tokens, m->cap_tokens);
+    free_workspace(m);
+    const size_t T = static_cast<size_t>(nt);
+    int rc = 0;
+    auto A = [&](size_t bytes, void** p) {
+        if (!rc) rc = dalloc(m, m->ws, bytes, p);
+    };
+    A(sizeof(uint32_t) * T, reinterpret_cast<void**>(&m->d_ids));
+    A(sizeof(int) * (nb + 1), reinterpret_cast<void**>(&m->d_cu));
+    A(sizeof(float) * T * kH, reinterpret_cast<void**>(&m->X));
+    A(sizeof(float) * T * kH, reinterpret_cast<void**>(&m->Y));
+    A(sizeof(__half) * T * 3 * kH, &m->QKV);
+    A(sizeof(float) * nb * kH, reinterpret_cast<void**>(&m->out));
+    if (m->mode == TZ_QUANT_W8A8) {
+        A(T * kH, &m->XA);
+        A(T * kH, &m->OA);
+        A(sizeof(float) * T, reinterpret_cast<void**>(&m->xs));
+        A(sizeof(float) * T, reinterpret_cast<void**>(&m->os));
+        A(sizeof(float) * T, reinterpret_cast<void**>(&m->hs));
+        A(sizeof(unsigned) * T, reinterpret_cast<void**>(&m->hmax));
+        A(sizeof(__half) * T * kF, &m->Hh);
+        A(T * kF, &m->HQ);
+    } else {
+        A(sizeof(__half) * T * kH, &m->XA);
+        A(sizeof(__half) * T * kH, &m->OA);
+        A(sizeof(__half) * T * kF, &m->Hh);
+    }
+    if (m->keep_stages) {
+        A(sizeof(float) * 7 * T * kH, reinterpret_cast<void**>(&m->d_stages));
+        if (m->mode == TZ_QUANT_W8A8)
+            for (int i = 0; i < 4; ++i) {
+                A(T * (i == 3 ? kF : kH), reinterpret_cast<void**>(&m->d_opq[i]));
+                A(sizeof(float) * T, reinterpret_cast<void**>(&m->d_ops[i]));
+            }
+    }
+    if (rc) {
+        free_workspace(m);
+        return rc;
+    }
+    if (m->hmax) TZ_CUDA(cudaMemset(m->hmax, 0, sizeof(unsigned) * T));
+    TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_ids), sizeof(uint32_t) * T, cudaHostAllocDefault));
+    TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_cu), sizeof(int) * (nb + 1), cudaHostAllocDefault));
+    TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_out), sizeof(float) * nb * kH, cudaHostAllocDefault));
+    m->cap_batch = nb;
+    m->cap_tokens = nt;
+    return TZ_OK;
+}
+
+enum ProfClass { P_EMBED = 0, P_QKV, P_ATTN, P_OPROJ, P_LN, P_FFN1, P_QUANT, P_FFN2, P_POOL, P_NCLASS };
+
+// Records the event that closes launch (ev_n - 1) and opens the next one.
+int prof_mark(tz_model_s* m, int next_class, cudaStream_t s) {
+    if (!m->profile) return TZ_OK;
+    if (m->ev_n >= static_cast<int>(m->ev.size())) return TZ_OK;
+    TZ_CUDA(cudaEventRecord(m->ev[m->ev_n], s));
+    if (next_class >= 0 && m->ev_n < 64) m->ev_cls[m->ev_n] = next_class;
+    ++m->ev_n;
+    return TZ_OK;
+}
+
+// W8A8 parity hook: keeps a copy of a layer-0 GEMM operand (int8 rows + per-row scales).
+int keep_operand(tz_model_s* m, int which, const void* q, const float* sc, int64_t T, int K, cudaStream_t s) {
+    if (!m->keep_stages || m->mode != TZ_QUANT_W8A8 || !m->d_opq[which]) return TZ_OK;
+    TZ_CUDA(cudaMemcpyAsync(m->d_opq[which], q, static_cast<size_t>(T) * K, cudaMemcpyDeviceToDevice, s));
+    TZ_CUDA(cudaMemcpyAsync(m->d_ops[which], sc, sizeof(float) * T, cudaMemcpyDeviceToDevice, s));
+    return TZ_OK;
+}
+
+// Enqueues the whole forward on `s`: device ids/cu already in place (d_ids/d_cu may be the
+// caller's device buffers).
+int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B, int64_t T, int maxL, float* d_out,
+                    cudaStream_t s) {
+    tz_ctx_t ctx = m->ctx;
+    const bool q8 = m->mode == TZ_QUANT_W8A8;
+    const bool wscale = m->mode != TZ_QUANT_F32;
+    const int M = static_cast<int>(T);
+    int rc;
+    m->ev_n = 0;
+    if ((rc = prof_mark(m, P_EMBED, s))) return rc;
+    if (q8)
+        embed_ln_kernel<1><<<B, 256, 0, s>>>(d_ids, d_cu, m->emb, m->emb_g, m->emb_b, m->X, m->XA, m->xs, ctx->d_status);
+    else
+        embed_ln_kernel<0><<<B, 256, 0, s>>>(d_ids, d_cu, m->emb, m->emb_g, m->emb_b, m->X, m->XA, nullptr, ctx->d_status);
+    TZ_CUDA(cudaGetLastError());
+    if (m->keep_stages) TZ_CUDA(cudaMemcpyAsync(m->d_stages, m->X, sizeof(float) * T * kH, cudaMemcpyDeviceToDevice, s));
+    for (int l = 0; l < kLayers; ++l) {
+        const DevLayer& L = m->layers[l];
+        GemmArgs g;
+        g.kind = q8 ? KIND_I8 : KIND_F16;
+        // QKV projection (3 linearProjection calls of selfAttention fused into one N=1152 GEMM)
+        g.a = m->XA; g.lda = kH; g.b = L.wqkv; g.ldb = kH; g.M = M; g.N = 3 * kH; g.K = kH;
+        g.bias = L.bqkv; g.col_scale = wscale ? L.sqkv : nullptr; g.row_scale = q8 ? m->xs : nullptr;
+        g.out = m->QKV; g.ldo = 3 * kH; g.out_type = OUT_F16;
+        if (l == 0 && (rc = keep_operand(m, 0, m->XA, m->xs, T, kH, s))) return rc;
+        if ((rc = prof_mark(m, P_QKV, s))) return rc;
+        if ((rc = launch_gemm(ctx, g, s))) return rc;
+        if ((rc = prof_mark(m, P_ATTN, s))) return rc;
+        // attention
+        if ((rc = launch_attention(ctx, m->QKV, d_cu, B, maxL, q8 ? nullptr : m->OA, q8 ? static_cast<int8_t*>(m->OA) : nullptr,
+                                   q8 ? m->os : nullptr, s)))
+            return rc;
+        // output projection + bias + residual, then LayerNorm
+        GemmArgs o;
+        o.kind = g.kind;
+        o.a = m->OA; o.lda = kH; o.b = L.wo; o.ldb = kH; o.M = M; o.N = kH; o.K = kH;
+        o.bias = L.bo; o.col_scale = wscale ? L.so : nullptr; o.row_scale = q8 ? m->os : nullptr;
+        o.residual = m->X; o.ldr = kH; o.out = m->Y; o.ldo = kH; o.out_type = OUT_F32;
+        if (l == 0 && (rc = keep_operand(m, 1, m->OA, m->os, T, kH, s))) return rc;
+        if ((rc = prof_mark(m, P_OPROJ, s))) return rc;
+        if ((rc = launch_gemm(ctx, o, s))) return rc;
+        if ((rc = prof_mark(m, P_LN, s))) return rc;
+        if (q8)
+            ln_model_kernel<1><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln1g, L.ln1b, m->X, m->XA, m->xs, T);
+        else
+            ln_model_kernel<0><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln1g, L.ln1b, m->X, m->XA, nullptr, T);
+        TZ_CUDA(cudaGetLastError());
+        // FFN1 + bias + GELU
+        GemmArgs f1;
+        f1.kind = g.kind;
+        f1.a = m->XA; f1.lda = kH; f1.b = L.w1; f1.ldb = kH; f1.M = M; f1.N = kF; f1.K = kH;
+        f1.bias = L.b1; f1.col_scale = wscale ? L.s1 : nullptr; f1.row_scale = q8 ? m->xs : nullptr;
+        f1.gelu = 1; f1.out = m->Hh; f1.ldo = kF; f1.out_type = OUT_F16; f1.row_absmax = q8 ? m->hmax : nullptr;
+        if (l == 0 && (rc = keep_operand(m, 2, m->XA, m->xs, T, kH, s))) return rc;
+        if ((rc = prof_mark(m, P_FFN1, s))) return rc;
+        if ((rc = launch_gemm(ctx, f1, s))) return rc;
+        if (q8) {
+            if ((rc = prof_mark(m, P_QUANT, s))) return rc;
+            quant_h_kernel<<<rows_grid(T), 256, 0, s>>>(static_cast<__half*>(m->Hh), m->hmax, static_cast<int8_t*>(m->HQ), m->hs, T);
+            TZ_CUDA(cudaGetLastError());
+        }
+        // FFN2 + bias + residual, then LayerNorm
+        GemmArgs f2;
+        f2.kind = g.kind;
+        f2.a = q8 ? m->HQ : m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.N = kH; f2.K = kF;
+        f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.row_scale = q8 ? m->hs : nullptr;
+        f2.residual = m->X; f2.ldr = kH; f2.out = m->Y; f2.ldo = kH; f2.out_type = OUT_F32;
+        if (l == 0 && q8 && (rc = keep_operand(m, 3, m->HQ, m->hs, T, kF, s))) return rc;
+        if ((rc = prof_mark(m, P_FFN2, s))) return rc;
+        if ((rc = launch_gemm(ctx, f2, s))) return rc;
+        if ((rc = prof_mark(m, P_LN, s))) return rc;
+        if (q8)
+            ln_model_kernel<1><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln2g, L.ln2b, m->X, m->XA, m->xs, T);
+        else
+            ln_model_kernel<0><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln2g, L.ln2b, m->X, m->XA, nullptr, T);
+        TZ_CUDA(cudaGetLastError());
+        if (m->keep_stages)
+            TZ_CUDA(cudaMemcpyAsync(m->d_stages + static_cast<size_t>(l + 1) * m->cap_tokens * kH, m->X, sizeof(float) * T * kH,
+                                    cudaMemcpyDeviceToDevice, s));
+    }
+    if ((rc = prof_mark(m, P_POOL, s))) return rc;
+    pool_l2_kernel<<<(B * 32 + 255) / 256, 256, 0, s>>>(m->X, d_cu, d_out, B);
+    TZ_CUDA(cudaGetLastError());
+    if ((rc = prof_mark(m, -1, s))) return rc;
+    return TZ_OK;
+}
+
+int check_lengths(const int32_t* cu, int B, int64_t* T, int* maxL) {
+    TZ_CHECK(cu[0] == 0, TZ_EINVAL, "cu_seqlens[0] must be 0");
+    int mx = 0;
+    for (int b = 0; b < B; ++b) {
+        const int L = cu[b + 1] - cu[b];
+        TZ_CHECK(L >= 1 && L <= kP, TZ_EINVAL, "sequence %d has length %d (must be 1..512)", b, L);
+        mx = std::max(mx, L);
+    }
+    *T = cu[B];
+    *maxL = mx;
+    return TZ_OK;
+}
+
+int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, float* out) {
+    int64_t T = 0;
+    int maxL = 0;
+    int rc = check_lengths(cu, B, &T, &maxL);
+    if (rc) return rc;
+    for (int64_t i = 0; i < T; ++i)
+        TZ_CHECK(ids[i] < static_cast<uint32_t>(kV), TZ_EINVAL, "token id %u at %lld is >= vocab %d", ids[i],
+                 static_cast<long long>(i), kV);
+    if ((rc = reserve(m, B, T))) return rc;
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    cudaStream_t s = m->ctx->stream;
+    memcpy(m->h_ids, ids, sizeof(uint32_t) * T);
+    memcpy(m->h_cu, cu, sizeof(int) * (B + 1));
+    const bool graph_ok = m->use_graph && !m->keep_stages;
+    if (graph_ok && !(m->graph && m->g_batch == B && m->g_tokens == T && m->g_maxlen == maxL)) {
+        if (m->graph) {
+            cudaGraphExecDestroy(m->graph);
+            m->graph = nullptr;
+        }
+        cudaGraph_t gr = nullptr;
+        TZ_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        int crc = TZ_OK;
+        cudaError_t ce = cudaMemcpyAsync(m->d_ids, m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s);
+        if (ce == cudaSuccess) ce = cudaMemcpyAsync(m->d_cu, m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s);
+        if (ce == cudaSuccess) crc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
+        if (ce == cudaSuccess && !crc) ce = cudaMemcpyAsync(m->h_out, m->out, sizeof(float) * B * kH, cudaMemcpyDeviceToHost, s);
+        cudaError_t ee = cudaStreamEndCapture(s, &gr);
+        if (ce != cudaSuccess) return cuda_fail(ce, "forward capture");
+        if (crc) {
+            if (gr) cudaGraphDestroy(gr);
+            return crc;
+        }
+        if (ee != cudaSuccess) return cuda_fail(ee, "cudaStreamEndCapture");
+        ce = cudaGraphInstantiate(&m->graph, gr, 0);
+        cudaGraphDestroy(gr);
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+        m->g_batch = B;
+        m->g_tokens = T;
+        m->g_maxlen = maxL;
+    }
+    if (graph_ok) {
+        TZ_CUDA(cudaGraphLaunch(m->graph, s));
+    } else {
+        TZ_CUDA(cudaMemcpyAsync(m->d_ids, m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
+        TZ_CUDA(cudaMemcpyAsync(m->d_cu, m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s));
+        if ((rc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s))) return rc;
+        TZ_CUDA(cudaMemcpyAsync(m->h_out, m->out, sizeof(float) * B * kH, cudaMemcpyDeviceToHost, s));
+    }
+    TZ_CUDA(cudaStreamSynchronize(s));
+    if ((rc = read_status(m->ctx, s))) return rc;
+    memcpy(out, m->h_out, sizeof(float) * B * kH);
+    m->last_T = T;
+    return TZ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_t* out) {
+    TZ_CHECK(ctx && w && out, TZ_EINVAL, "tz_arctic_load: null argument");
+    TZ_CHECK(mode >= TZ_QUANT_F32 && mode <= TZ_QUANT_W8A8, TZ_EINVAL, "tz_arctic_load: bad mode %d", mode);
+    *out = nullptr;
+    TZ_CUDA(cudaSetDevice(ctx->device));
+    auto m = std::make_unique<tz_model_s>();
+    m->ctx = ctx;
+    m->mode = mode;
+    int rc = TZ_OK;
+    auto fail_cleanup = [&](int code) {
+        for (void* p : m->allocs) cudaFree(p);
+        m->allocs.clear();
+        return code;
+    };
+#define TRY(x)                                      \
+    do {                                            \
+        if ((rc = (x))) return fail_cleanup(rc);    \
+    } while (0)
+    TRY(upload_table(m.get(), w->word_embeddings, kV, &m->emb.word_f, &m->emb.word_q, &m->emb.word_s, "embeddings.word_embeddings.weight"));
+    TRY(upload_table(m.get(), w->position_embeddings, kP, &m->emb.pos_f, &m->emb.pos_q, &m->emb.pos_s, "embeddings.position_embeddings.weight"));
+    {
+        const float* tf = nullptr;
+        const int8_t* tq = nullptr;
+        const float* ts = nullptr;
+        TRY(upload_table(m.get(), w->token_type_embeddings, 2, &tf, &tq, &ts, "embeddings.token_type_embeddings.weight"));
+        TRY(tf ? TZ_OK : fail(TZ_EINVAL, "token_type_embeddings must be f32 (768 elements are never quantised)"));
+        m->emb.type_f = tf;
+    }
+    TRY(upload_f32(m.get(), w->ln_gamma, kH, &m->emb_g, "embeddings.LayerNorm.weight"));
+    TRY(upload_f32(m.get(), w->ln_beta, kH, &m->emb_b, "embeddings.LayerNorm.bias"));
+    const size_t el = (mode == TZ_QUANT_W8A8) ? 1 : 2;
+    for (int l = 0; l < kLayers; ++l) {
+        const tz_arctic_layer& s = w->layers[l];
+        DevLayer& d = m->layers[l];
+        char nm[96];
+        TRY(dalloc(m.get(), m->allocs, el * 3 * kH * kH, &d.wqkv));
+        TRY(dalloc(m.get(), m->allocs, el * kH * kH, &d.wo));
+        TRY(dalloc(m.get(), m->allocs, el * kF * kH, &d.w1));
+        TRY(dalloc(m.get(), m->allocs, el * kH * kF, &d.w2));
+        TRY(dalloc(m.get(), m->allocs, sizeof(float) * 3 * kH, reinterpret_cast<void**>(&d.sqkv)));
+        TRY(dalloc(m.get(), m->allocs, sizeof(float) * kH, reinterpret_cast<void**>(&d.so)));
+        TRY(dalloc(m.get(), m->allocs, sizeof(float) * kF, reinterpret_cast<void**>(&d.s1)));
+        TRY(dalloc(m.get(), m->allocs, sizeof(float) * kH, reinterpret_cast<void**>(&d.s2)));
+        snprintf(nm, sizeof nm, "encoder.layer.%d.attention.self.query.weight", l);
+        TRY(upload_linear(m.get(), s.query, kH, kH, d.wqkv, 0, d.sqkv, nm));
+        snprintf(nm, sizeof nm, "encoder.layer.%d.attention.self.key.weight", l);
+        TRY(upload_linear(m.get(), s.key, kH, kH, d.wqkv, kH, d.sqkv, nm));
+        snprintf(nm, sizeof nm, "encoder.layer.%d.attention.self.value.weight", l);
+        TRY(upload_linear(m.get(), s.value, kH, kH, d.wqkv, 2 * kH, d.sqkv, nm));
+        snprintf(nm, sizeof nm, "encoder.layer.%d.attention.output.dense.weight", l);
+        TRY(upload_linear(m.get(), s.attn_output, kH, kH, d.wo, 0, d.so, nm));
+        snprintf(nm, sizeof nm, "encoder.layer.%d.intermediate.dense.weight", l);
+        TRY(upload_linear(m.get(), s.intermediate, kF, kH, d.w1, 0, d.s1, nm));
+        snprintf(nm, sizeof nm, "encoder.layer.%d.output.dense.weight", l);
+        TRY(upload_linear(m.get(), s.output, kH, kF, d.w2, 0, d.s2, nm));
+        TRY(dalloc(m.get(), m->allocs, sizeof(float) * 3 * kH, reinterpret_cast<void**>(&d.bqkv)));
+        TRY(s.query_bias && s.key_bias && s.value_bias ? TZ_OK : fail(TZ_EMISSING, "missing attention bias in layer %d", l));
+        TZ_CUDA(cudaMemcpy(d.bqkv, s.query_bias, sizeof(float) * kH, cudaMemcpyHostToDevice));
+        TZ_CUDA(cudaMemcpy(d.bqkv + kH, s.key_bias, sizeof(float) * kH, cudaMemcpyHostToDevice));
+        TZ_CUDA(cudaMemcpy(d.bqkv + 2 * kH, s.value_bias, sizeof(float) * kH, cudaMemcpyHostToDevice));
+        TRY(upload_f32(m.get(), s.attn_output_bias, kH, &d.bo, "attention.output.dense.bias"));
+        TRY(upload_f32(m.get(), s.intermediate_bias, kF, &d.b1, "intermediate.dense.bias"));
+        TRY(upload_f32(m.get(), s.output_bias, kH, &d.b2, "output.dense.bias"));
+        TRY(upload_f32(m.get(), s.attn_ln_gamma, kH, &d.ln1g, "attention.output.LayerNorm.weight"));
+        TRY(upload_f32(m.get(), s.attn_ln_beta, kH, &d.ln1b, "attention.output.LayerNorm.bias"));
+        TRY(upload_f32(m.get(), s.output_ln_gamma, kH, &d.ln2g, "output.LayerNorm.weight"));
+        TRY(upload_f32(m.get(), s.output_ln_beta, kH, &d.ln2b, "output.LayerNorm.bias"));
+    }
+#undef TRY
+    TZ_CUDA(cudaDeviceSynchronize());
+    *out = m.release();
+    return TZ_OK;
+}
+
+int tz_arctic_free(tz_model_t m) {
+    if (!m) return TZ_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    free_workspace(m);
+    for (void* p : m->allocs) cudaFree(p);
+    for (auto& e : m->ev) cudaEventDestroy(e);
+    delete m;
+    return TZ_OK;
+}
+
+int tz_arctic_reserve(tz_model_t m, int max_batch, int64_t max_tokens) {
+    TZ_CHECK(m && max_batch > 0 && max_tokens > 0, TZ_EINVAL, "tz_arctic_reserve: bad arguments");
+    return reserve(m, max_batch, max_tokens);
+}
+
+int tz_arctic_forward(tz_model_t m, const uint32_t* ids, const int32_t* cu, int batch, float* out) {
+    TZ_CHECK(m && batch >= 0 && (batch == 0 || (ids && cu && out)), TZ_EINVAL, "tz_arctic_forward: bad arguments");
+    if (batch == 0) return TZ_OK;
+    return forward_host(m, ids, cu, batch, out);
+}
+
+int tz_arctic_forward_padded(tz_model_t m, const uint32_t* ids, const int32_t* lengths, int batch, int seq, float* out) {
+    TZ_CHECK(m && batch >= 0 && seq > 0 && (batch == 0 || (ids && lengths && out)), TZ_EINVAL,
+             "tz_arctic_forward_padded: bad arguments");
+    if (batch == 0) return TZ_OK;
+    std::vector<int32_t> cu(batch + 1, 0);
+    int64_t T = 0;
+    for (int b = 0; b < batch; ++b) {
+        TZ_CHECK(lengths[b] >= 1 && lengths[b] <= seq, TZ_EINVAL, "length %d of row %d outside [1, %d]", lengths[b], b, seq);
+        cu[b + 1] = cu[b] + lengths[b];
+    }
+    T = cu[batch];
+    std::vector<uint32_t> packed(static_cast<size_t>(T));
+    for (int b = 0; b < batch; ++b) memcpy(&packed[cu[b]], ids + static_cast<int64_t>(b) * seq, sizeof(uint32_t) * lengths[b]);
+    return forward_host(m, packed.data(), cu.data(), batch, out);
+}
+
+int tz_arctic_forward_device(tz_model_t m, const uint32_t* d_ids, const int32_t* d_cu, int batch, int64_t T, int max_len,
+                             float* d_out, tz_stream_t stream) {
+    TZ_CHECK(m && batch >= 0 && T >= 0 && max_len >= 1 && max_len <= kP, TZ_EINVAL, "tz_arctic_forward_device: bad arguments");
+    if (batch == 0) return TZ_OK;
+    TZ_CHECK(d_ids && d_cu && d_out, TZ_EINVAL, "tz_arctic_forward_device: null pointer");
+    int rc = reserve(m, batch, T);
+    if (rc) return rc;
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    rc = enqueue_forward(m, d_ids, d_cu, batch, T, max_len, d_out, pick_stream(m->ctx, stream));
+    m->last_T = T;
+    return rc;
+}
+
+int tz_arctic_debug_hidden(tz_model_t m, int stage, float* out, int64_t T) {
+    TZ_CHECK(m && out && stage >= 0 && stage <= kLayers, TZ_EINVAL, "tz_arctic_debug_hidden: bad arguments");
+    if (!m->keep_stages) {
+        m->keep_stages = true;  // takes effect from the next forward
+        return fail(TZ_EINVAL, "stage capture was off; it is on from the next forward");
+    }
+    TZ_CHECK(m->d_stages && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
+    TZ_CUDA(cudaMemcpy(out, m->d_stages + static_cast<size_t>(stage) * m->cap_tokens * kH, sizeof(float) * T * kH,
+                       cudaMemcpyDeviceToHost));
+    return TZ_OK;
+}
+
+int tz_arctic_profile(tz_model_t m, int enable) {
+    TZ_CHECK(m, TZ_EINVAL, "tz_arctic_profile: null model");
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    if (enable && m->ev.empty()) {
+        m->ev.resize(65);
+        for (auto& e : m->ev) TZ_CUDA(cudaEventCreate(&e));
+    }
+    if (m->graph) {  // the captured graph carries (or lacks) the event nodes: recapture
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    m->profile = enable != 0;
+    m->ev_n = 0;
+    return TZ_OK;
+}
+
+int tz_arctic_profile_read(tz_model_t m, float* ms, int* launches) {
+    TZ_CHECK(m && ms && launches, TZ_EINVAL, "tz_arctic_profile_read: null argument");
+    for (int c = 0; c < P_NCLASS; ++c) {
+        ms[c] = 0.f;
+        launches[c] = 0;
+    }
+    TZ_CHECK(m->profile && m->ev_n >= 2, TZ_EINVAL, "no profiled forward recorded");
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    for (int i = 0; i + 1 < m->ev_n; ++i) {
+        float t = 0.f;
+        TZ_CUDA(cudaEventSynchronize(m->ev[i + 1]));
+        TZ_CUDA(cudaEventElapsedTime(&t, m->ev[i], m->ev[i + 1]));
+        const int c = m->ev_cls[i];
+        ms[c] += t;
+        launches[c] += 1;
+    }
+    return TZ_OK;
+}
+
+int tz_arctic_debug_operand(tz_model_t m, int which, int8_t* q_out, float* scale_out, int64_t T) {
+    TZ_CHECK(m && q_out && scale_out && which >= 0 && which < 4, TZ_EINVAL, "tz_arctic_debug_operand: bad arguments");
+    TZ_CHECK(m->mode == TZ_QUANT_W8A8, TZ_EINVAL, "tz_arctic_debug_operand: W8A8 models only");
+    if (!m->keep_stages) {
+        m->keep_stages = true;
+        return fail(TZ_EINVAL, "operand capture was off; it is on from the next forward");
+    }
+    TZ_CHECK(m->d_opq[which] && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
+    const int K = which == 3 ? kF : kH;
+    TZ_CUDA(cudaMemcpy(q_out, m->d_opq[which], static_cast<size_t>(T) * K, cudaMemcpyDeviceToHost));
+    TZ_CUDA(cudaMemcpy(scale_out, m->d_ops[which], sizeof(float) * T, cudaMemcpyDeviceToHost));
+    return TZ_OK;
+}
+
+}  // extern "C"

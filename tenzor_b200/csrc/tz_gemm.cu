@@ -1,0 +1,504 @@
+// tz_gemm.cu -- persistent warp-specialised tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   Y[M, N] = epilogue( A[M, K] * B[N, K]^T )        (both operands K-major, PyTorch [out,in] B)
+//
+// One CTA per SM (persistent, static round-robin over 128 x BN output tiles, tile index n-fastest
+// so neighbouring CTAs share A rows in L2).  192 threads:
+//   warp 0      TMA producer: 128-byte-wide K blocks of A (128 rows) and B (BN rows) into a
+//               STAGES-deep shared-memory ring, SWIZZLE_128B, completion on `full[s]`;
+//   warp 1      allocates TMEM (2 x BN fp32/int32 columns: double-buffered accumulators); lane 0
+//               issues tcgen05.mma (M=128, N=BN, 32 bytes of K per instruction) and commits to
+//               `empty[s]` (smem slot free) and `tfull[acc]` (accumulator ready);
+//   warps 2..5  epilogue: warp w reads TMEM lane quarter (w % 4), so each thread owns one output
+//               row; 32 columns per tcgen05.ld; scale / bias / GELU / residual / row-absmax fused;
+//               vector stores straight from registers.
+// The epilogue of tile t overlaps the MMAs of tile t+1 (second TMEM buffer).
+//
+// Replaces matmulTransposeB (reference matmul.zig:54-77), linearProjection (arctic.zig:599-635),
+// matmulTransposeB_f32_i8_rowScale_bias (matmul_w8a32.zig:14-58) and FusedMatmulEpilogueKernel
+// (codegen.zig:78-147).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "tz_internal.h"
+#include "tz_ptx.cuh"
+
+namespace tz {
+namespace {
+
+struct EpiParams {
+    const float* bias;
+    const float* col_scale;
+    const float* row_scale;
+    const float* residual;
+    long long ldr;
+    void* out;
+    long long ldo;
+    int out_type;
+    int gelu;
+    unsigned* row_absmax;
+    int n_ops;
+    int ops[8];
+    int vec_ok;  // 16-byte aligned rows for vector stores / residual loads
+};
+
+__device__ __forceinline__ float gelu_model(float x) {
+    // arctic.zig:750-756: 0.5 x (1 + tanh(0.7978845608 (x + 0.044715 x^3))), std.math.tanh.
+    const float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, __fmul_rn(__fmul_rn(0.044715f, x), __fmul_rn(x, x))));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+__device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// Unary op table of codegen.zig:228-244 (simd.zig scalar ops); TZ_OP_* codes.
+__device__ __forceinline__ float apply_op(int op, float x) {
+    switch (op) {
+        case TZ_OP_RELU: return x > 0.0f ? x : 0.0f;
+        case TZ_OP_GELU: {
+            const float x3 = x * x * x;
+            const float inner = 0.7978845608028654f * (x + 0.044715f * x3);
+            const float t = 2.0f * sigmoid_ref(2.0f * inner) - 1.0f;
+            return 0.5f * x * (1.0f + t);
+        }
+        case TZ_OP_SIGMOID: return sigmoid_ref(x);
+        case TZ_OP_TANH: return 2.0f * sigmoid_ref(2.0f * x) - 1.0f;
+        case TZ_OP_EXP: return expf(x);
+        case TZ_OP_NEG: return -x;
+        case TZ_OP_ABS: return fabsf(x);
+        case TZ_OP_SILU: return x * sigmoid_ref(x);
+        case TZ_OP_LOG: return logf(x);
+        case TZ_OP_SQRT: return sqrtf(x);
+        case TZ_OP_RSQRT: return 1.0f / sqrtf(x);
+        case TZ_OP_SIN: return sinf(x);
+        case TZ_OP_COS: return cosf(x);
+        default: return x;
+    }
+}
+
+template <int KIND>
+struct KindTraits;
+template <>
+struct KindTraits<KIND_F16> {
+    static constexpr int elem = 2;
+    static constexpr uint32_t c_fmt = 1, ab_fmt = 0;
+};
+template <>
+struct KindTraits<KIND_BF16> {
+    static constexpr int elem = 2;
+    static constexpr uint32_t c_fmt = 1, ab_fmt = 1;
+};
+template <>
+struct KindTraits<KIND_TF32> {
+    static constexpr int elem = 4;
+    static constexpr uint32_t c_fmt = 1, ab_fmt = 2;
+};
+template <>
+struct KindTraits<KIND_I8> {
+    static constexpr int elem = 1;
+    static constexpr uint32_t c_fmt = 2, ab_fmt = 1;
+};
+
+template <int KIND, int BN, int STAGES>
+struct Cfg {
+    static constexpr int BM = 128;
+    static constexpr int ELEM = KindTraits<KIND>::elem;
+    static constexpr int BK = 128 / ELEM;  // elements per 128-byte K block
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+    static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+};
+
+// Epilogue for one 32-column chunk of one row held in registers.
+template <int KIND>
+__device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, const uint32_t (&r)[32],
+                                               int row, int col0, int N, float rs, float& amax) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if constexpr (KIND == KIND_I8)
+            v[j] = __int2float_rn(static_cast<int>(r[j]));
+        else
+            v[j] = __uint_as_float(r[j]);
+    }
+    const bool full = (col0 + 32 <= N);
+    if (ep.out_type == OUT_I32) {
+        int* o = reinterpret_cast<int*>(ep.out) + static_cast<long long>(row) * ep.ldo + col0;
+        if (full && ep.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<int4*>(o + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
+                                                            static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
+        } else {
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) o[j] = static_cast<int>(r[j]);
+        }
+        return;
+    }
+    if (ep.n_ops >= 0) {
+        // Generic chain (codegen.zig:101-145): TZ_OP_ADD adds bias[col], others are unary.
+        for (int j = 0; j < 32; ++j) {
+            const int col = col0 + j;
+            if (col >= N) break;
+            float x = v[j];
+            for (int o = 0; o < ep.n_ops; ++o) {
+                const int op = ep.ops[o];
+                if (op == TZ_OP_ADD) {
+                    if (ep.bias) x = x + __ldg(ep.bias + col);
+                } else {
+                    x = apply_op(op, x);
+                }
+            }
+            v[j] = x;
+        }
+    } else {
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                const int col = col0 + j;
+                if (ep.row_scale) {
+                    const float4 cs = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col));
+                    v[j] = __fmul_rn(v[j], __fmul_rn(rs, cs.x));
+                    v[j + 1] = __fmul_rn(v[j + 1], __fmul_rn(rs, cs.y));
+                    v[j + 2] = __fmul_rn(v[j + 2], __fmul_rn(rs, cs.z));
+                    v[j + 3] = __fmul_rn(v[j + 3], __fmul_rn(rs, cs.w));
+                } else if (ep.col_scale) {
+                    const float4 cs = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col));
+                    v[j] = __fmul_rn(v[j], cs.x);
+                    v[j + 1] = __fmul_rn(v[j + 1], cs.y);
+                    v[j + 2] = __fmul_rn(v[j + 2], cs.z);
+                    v[j + 3] = __fmul_rn(v[j + 3], cs.w);
+                }
+                if (ep.bias) {
+                    const float4 b = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+                    v[j] = __fadd_rn(v[j], b.x);
+                    v[j + 1] = __fadd_rn(v[j + 1], b.y);
+                    v[j + 2] = __fadd_rn(v[j + 2], b.z);
+                    v[j + 3] = __fadd_rn(v[j + 3], b.w);
+                }
+            }
+            if (ep.gelu) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = gelu_model(v[j]);
+            }
+            if (ep.residual) {
+                const float* rp = ep.residual + static_cast<long long>(row) * ep.ldr + col0;
+                if (ep.vec_ok) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 t = *reinterpret_cast<const float4*>(rp + j);
+                        v[j] = __fadd_rn(v[j], t.x);
+                        v[j + 1] = __fadd_rn(v[j + 1], t.y);
+                        v[j + 2] = __fadd_rn(v[j + 2], t.z);
+                        v[j + 3] = __fadd_rn(v[j + 3], t.w);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], rp[j]);
+                }
+            }
+        } else {
+            for (int j = 0; j < 32; ++j) {
+                const int col = col0 + j;
+                if (col >= N) break;
+                float x = v[j];
+                if (ep.row_scale)
+                    x = __fmul_rn(x, __fmul_rn(rs, ep.col_scale[col]));
+                else if (ep.col_scale)
+                    x = __fmul_rn(x, ep.col_scale[col]);
+                if (ep.bias) x = __fadd_rn(x, ep.bias[col]);
+                if (ep.gelu) x = gelu_model(x);
+                if (ep.residual) x = __fadd_rn(x, ep.residual[static_cast<long long>(row) * ep.ldr + col]);
+                v[j] = x;
+            }
+        }
+    }
+    if (ep.out_type == OUT_F16) {
+        __half* o = reinterpret_cast<__half*>(ep.out) + static_cast<long long>(row) * ep.ldo + col0;
+        if (full && ep.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint4 pk;
+                pk.x = tzp::pack_half2(v[j], v[j + 1]);
+                pk.y = tzp::pack_half2(v[j + 2], v[j + 3]);
+                pk.z = tzp::pack_half2(v[j + 4], v[j + 5]);
+                pk.w = tzp::pack_half2(v[j + 6], v[j + 7]);
+                *reinterpret_cast<uint4*>(o + j) = pk;
+            }
+            if (ep.row_absmax) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(__half2float(__float2half_rn(v[j]))));
+            }
+        } else {
+            for (int j = 0; j < 32; ++j) {
+                if (col0 + j >= N) break;
+                const __half h = __float2half_rn(v[j]);
+                o[j] = h;
+                amax = fmaxf(amax, fabsf(__half2float(h)));
+            }
+        }
+    } else {
+        float* o = reinterpret_cast<float*>(ep.out) + static_cast<long long>(row) * ep.ldo + col0;
+        if (full && ep.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if (ep.row_absmax) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+            }
+        } else {
+            for (int j = 0; j < 32; ++j) {
+                if (col0 + j >= N) break;
+                o[j] = v[j];
+                amax = fmaxf(amax, fabsf(v[j]));
+            }
+        }
+    }
+}
+
+template <int KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   int M, int N, int K, EpiParams ep, int* status) {
+    using C = Cfg<KIND, BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = tzp::smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            tzp::mbar_init(&full[s], 1);
+            tzp::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            tzp::mbar_init(&tfull[a], 1);
+            tzp::mbar_init(&tempty[a], 4);
+        }
+        tzp::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tzp::fence_mbar_init();
+        tzp::tma_prefetch_desc(&tmA);
+        tzp::tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tzp::tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tzp::tmem_relinquish();
+    }
+    tzp::tc_fence_before();
+    __syncthreads();
+    tzp::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = ((M + 127) / 128) * n_tiles;
+    const int kblocks = (K + C::BK - 1) / C::BK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer ----
+            int stage = 0;
+            uint32_t phase = 0, armed = 0, armed_par = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int m0 = (tile / n_tiles) * 128;
+                const int n0 = (tile % n_tiles) * BN;
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!tzp::mbar_wait(&empty[stage], phase ^ 1u, status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tzp::tma_load_2d(sa, &tmA, kb * C::BK, m0, &full[stage]);
+                    tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, n0, &full[stage]);
+                    armed |= 1u << stage;
+                    armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+            }
+            // Let every copy this thread issued land before the CTA can exit (bounded).
+            for (int s = 0; s < STAGES; ++s)
+                if (armed & (1u << s)) tzp::mbar_wait(&full[s], (armed_par >> s) & 1u, status, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer ----
+            constexpr uint32_t idesc =
+                tzp::make_idesc(KindTraits<KIND>::c_fmt, KindTraits<KIND>::ab_fmt, 128, BN);
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                if (!tzp::mbar_wait(&tempty[acc], acc_phase ^ 1u, status, abort_flag)) break;
+                tzp::tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!tzp::mbar_wait(&full[stage], phase, status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tzp::tc_fence_after();
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    const uint64_t ad = tzp::sdesc_k128(tzp::smem_u32(sa));
+                    const uint64_t bd = tzp::sdesc_k128(tzp::smem_u32(sa + C::A_BYTES));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)  // 4 x 32 bytes of K per 128-byte block
+                        tzp::umma<KIND>(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    tzp::umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tzp::umma_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // Drain: every MMA this thread issued has completed before TMEM is released.
+            tzp::umma_commit(drain);
+            tzp::mbar_wait(drain, 0, status, nullptr);
+        }
+    } else {
+        // ---- epilogue warps 2..5 ----
+        const int q = warp & 3;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int m0 = (tile / n_tiles) * 128;
+            const int n0 = (tile % n_tiles) * BN;
+            if (!tzp::mbar_wait(&tfull[acc], acc_phase, status, abort_flag)) break;
+            tzp::tc_fence_after();
+            const int row = m0 + q * 32 + lane;
+            const bool row_ok = row < M;
+            const float rs = (ep.row_scale && row_ok) ? ep.row_scale[row] : 1.0f;
+            float amax = 0.0f;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tzp::tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + c),
+                               r);
+                tzp::tmem_ld_wait();
+                if (row_ok && n0 + c < N) epilogue_chunk<KIND>(ep, r, row, n0 + c, N, rs, amax);
+            }
+            tzp::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tzp::mbar_arrive(&tempty[acc]);
+            if (ep.row_absmax && row_ok) atomicMax(ep.row_absmax + row, __float_as_uint(amax));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tzp::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tzp::tc_fence_after();
+        tzp::tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+CUtensorMapDataType tmap_dtype(int kind) {
+    switch (kind) {
+        case KIND_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        case KIND_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        case KIND_TF32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    }
+}
+
+template <int KIND, int BN, int STAGES>
+int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
+    using C = Cfg<KIND, BN, STAGES>;
+    auto kern = gemm_tc_kernel<KIND, BN, STAGES>;
+    static bool attr_set = false;  // per instantiation; set once per process (single device use)
+    if (!attr_set) {
+        TZ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_set = true;
+    }
+    CUtensorMap ta, tb;
+    const uint64_t a_rows = g.a_rows_alloc > 0 ? static_cast<uint64_t>(g.a_rows_alloc) : static_cast<uint64_t>(g.M);
+    int rc = encode_tmap_2d(&ta, tmap_dtype(KIND), C::ELEM, g.a, static_cast<uint64_t>(g.K), a_rows,
+                            static_cast<uint64_t>(g.lda) * C::ELEM, C::BK, 128);
+    if (rc) return rc;
+    rc = encode_tmap_2d(&tb, tmap_dtype(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.K),
+                        static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.ldb) * C::ELEM, C::BK, BN);
+    if (rc) return rc;
+    EpiParams ep{};
+    ep.bias = g.bias;
+    ep.col_scale = g.col_scale;
+    ep.row_scale = g.row_scale;
+    ep.residual = g.residual;
+    ep.ldr = g.ldr;
+    ep.out = g.out;
+    ep.ldo = g.ldo;
+    ep.out_type = g.out_type;
+    ep.gelu = g.gelu;
+    ep.row_absmax = g.row_absmax;
+    ep.n_ops = g.n_ops;
+    for (int i = 0; i < 8; ++i) ep.ops[i] = g.ops[i];
+    const int out_elem = g.out_type == OUT_F16 ? 2 : 4;
+    const bool out_al = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldo * out_elem) % 16 == 0);
+    const bool res_al = !g.residual || ((reinterpret_cast<uintptr_t>(g.residual) % 16 == 0) && ((g.ldr * 4) % 16 == 0));
+    const bool vec_al = (!g.bias || reinterpret_cast<uintptr_t>(g.bias) % 16 == 0) &&
+                        (!g.col_scale || reinterpret_cast<uintptr_t>(g.col_scale) % 16 == 0);
+    TZ_CHECK(vec_al, TZ_EINVAL, "gemm: bias/scale vectors must be 16-byte aligned");
+    ep.vec_ok = (out_al && res_al) ? 1 : 0;
+    const int n_tiles = (g.N + BN - 1) / BN;
+    const int tiles = ((g.M + 127) / 128) * n_tiles;
+    const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+    if (grid <= 0) return TZ_OK;
+    kern<<<grid, 192, C::SMEM, s>>>(ta, tb, g.M, g.N, g.K, ep, ctx->d_status);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+}  // namespace
+
+int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
+    TZ_CHECK(g.M >= 0 && g.N > 0 && g.K > 0, TZ_EINVAL, "gemm: bad shape M=%d N=%d K=%d", g.M, g.N, g.K);
+    if (g.M == 0) return TZ_OK;
+    TZ_CHECK(g.a && g.b && g.out, TZ_EINVAL, "gemm: null operand");
+    const int elem = g.kind == KIND_I8 ? 1 : g.kind == KIND_TF32 ? 4 : 2;
+    TZ_CHECK((g.K * elem) % 16 == 0 && (g.lda * elem) % 16 == 0 && (g.ldb * elem) % 16 == 0, TZ_EINVAL,
+             "gemm: K and leading dimensions must be multiples of 16 bytes (K=%d)", g.K);
+    TZ_CHECK(reinterpret_cast<uintptr_t>(g.a) % 16 == 0 && reinterpret_cast<uintptr_t>(g.b) % 16 == 0,
+             TZ_EINVAL, "gemm: operands must be 16-byte aligned");
+    TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm: row_scale needs col_scale");
+    switch (g.kind) {
+        case KIND_F16: return launch_impl<KIND_F16, 128, 6>(ctx, g, s);
+        case KIND_BF16: return launch_impl<KIND_BF16, 128, 6>(ctx, g, s);
+        case KIND_TF32: return launch_impl<KIND_TF32, 128, 6>(ctx, g, s);
+        case KIND_I8: return launch_impl<KIND_I8, 128, 6>(ctx, g, s);
+        default: return fail(TZ_EINVAL, "gemm: unknown kind %d", g.kind);
+    }
+}
+
+}  // namespace tz

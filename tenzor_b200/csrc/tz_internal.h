@@ -1,0 +1,89 @@
+// tz_internal.h -- host-side internals shared by the translation units of libtenzor_cuda.so.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tenzor_cuda.h"
+
+namespace tz {
+
+// Thread-local last error (tz_get_last_error).
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+void clear_error();
+
+#define TZ_CUDA(call)                                              \
+    do {                                                           \
+        cudaError_t _e = (call);                                   \
+        if (_e != cudaSuccess) return ::tz::cuda_fail(_e, #call);  \
+    } while (0)
+
+#define TZ_CHECK(cond, code, ...)                                  \
+    do {                                                           \
+        if (!(cond)) return ::tz::fail((code), __VA_ARGS__);       \
+    } while (0)
+
+// A growable device scratch arena owned by a context (op-level calls that need temporaries).
+struct Scratch {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+}  // namespace tz
+
+struct tz_ctx_s {
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    int* d_status = nullptr;   // device status word (TZ_DEV_* bits)
+    tz::Scratch scratch;       // op-level temporaries
+    std::mutex mu;             // guards scratch growth
+};
+
+namespace tz {
+
+cudaStream_t pick_stream(tz_ctx_t ctx, tz_stream_t s);
+// Grows the context scratch to at least `bytes` (synchronising the context stream first).
+int scratch_reserve(tz_ctx_t ctx, size_t bytes, void** out);
+// Reads and clears the device status word; TZ_ETIMEOUT / TZ_EINVAL when a bit was set.
+int read_status(tz_ctx_t ctx, cudaStream_t s);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                   uint32_t box_outer);
+
+// ---- kernel launchers (defined in the .cu files) ---------------------------------------------
+enum GemmKind { KIND_F16 = 0, KIND_BF16 = 1, KIND_TF32 = 2, KIND_I8 = 3 };
+enum OutType { OUT_F32 = 0, OUT_F16 = 1, OUT_I32 = 2 };
+
+struct GemmArgs {
+    int kind = KIND_F16;
+    const void* a = nullptr;  // [M, K] row-major, lda elements
+    const void* b = nullptr;  // [N, K] row-major, ldb elements
+    int64_t lda = 0, ldb = 0;
+    int M = 0, N = 0, K = 0;
+    int64_t a_rows_alloc = 0; // rows of A that are addressable (>= M); TMA bound
+    // epilogue
+    const float* bias = nullptr;       // [N]
+    const float* col_scale = nullptr;  // [N]
+    const float* row_scale = nullptr;  // [M]
+    const float* residual = nullptr;   // [M, ldr] f32
+    int64_t ldr = 0;
+    void* out = nullptr;               // [M, ldo]
+    int64_t ldo = 0;
+    int out_type = OUT_F32;
+    int gelu = 0;                      // 1: model GELU (tanhf) after bias, before residual
+    unsigned* row_absmax = nullptr;    // [M] atomicMax of |stored value| (float bits)
+    int n_ops = -1;                    // >= 0: generic op chain instead of the fixed epilogue
+    int ops[8] = {0};
+};
+int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s);
+
+}  // namespace tz

@@ -1,0 +1,456 @@
+// tz_rowops.cu -- HBM-bound row and elementwise kernels: LayerNorm, softmax (additive mask and
+// key-length mask), quantisers, converters, fused elementwise chains, fused reduce, row gather.
+// Each is one pass over its data with 16-byte coalesced accesses: warp-per-row for the row ops
+// (shuffle reductions, the row stays in registers between the passes), grid-stride float4 loops
+// sized to a multiple of the SM count for the elementwise ops.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "tz_internal.h"
+#include "tz_ptx.cuh"
+#include "tz_rowops.cuh"
+
+namespace tz {
+namespace {
+
+// ---- LayerNorm (layernorm.zig:26-116) ----------------------------------------------------------
+// Warp per row; VPL float4 per lane kept in registers (cols == VPL*128).
+template <int VPL>
+__global__ void ln_rows_reg_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                   const float* __restrict__ b, float* y, long long rows, int cols,
+                                   float eps) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+    float4 v[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        v[i] = xr[lane + 32 * i];
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+    s = warp_sum(s);
+    const float mean = s / static_cast<float>(cols);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + bb * bb) + (c * c + d * d);
+    }
+    q = warp_sum(q);
+    const float inv_std = 1.0f / sqrtf(q / static_cast<float>(cols) + eps);
+    float4* yr = reinterpret_cast<float4*>(y + row * cols);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c4 = lane + 32 * i;
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + c4);
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + c4);
+        float4 o;
+        o.x = (v[i].x - mean) * inv_std * gg.x + bb.x;
+        o.y = (v[i].y - mean) * inv_std * gg.y + bb.y;
+        o.z = (v[i].z - mean) * inv_std * gg.z + bb.z;
+        o.w = (v[i].w - mean) * inv_std * gg.w + bb.w;
+        yr[c4] = o;
+    }
+}
+
+// Any width: warp per row, three passes over the (L1/L2-resident) row.
+__global__ void ln_rows_any_kernel(const float* x, const float* __restrict__ g,
+                                   const float* __restrict__ b, float* y, long long rows, int cols,
+                                   float eps) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * cols;
+    float s = 0.f;
+    for (int c = lane; c < cols; c += 32) s += xr[c];
+    const float mean = warp_sum(s) / static_cast<float>(cols);
+    float q = 0.f;
+    for (int c = lane; c < cols; c += 32) {
+        const float d = xr[c] - mean;
+        q += d * d;
+    }
+    const float inv_std = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(cols) + eps);
+    __syncwarp();
+    float* yr = y + row * cols;
+    for (int c = lane; c < cols; c += 32) yr[c] = (xr[c] - mean) * inv_std * g[c] + b[c];
+}
+
+// ---- softmax (softmax.zig:56-155) --------------------------------------------------------------
+// Warp per row; additive mask (may be null); key_len (per group of rows_per_group rows) masks
+// columns >= key_len with probability 0 (the -inf additive mask).
+__global__ void softmax_rows_kernel(const float* x, const float* mask, const int* key_len,
+                                    int rows_per_group, float* y, long long rows, int cols) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * cols;
+    const float* mr = mask ? mask + row * cols : nullptr;
+    const int valid = key_len ? min(max(key_len[row / rows_per_group], 0), cols) : cols;
+    float* yr = y + row * cols;
+    float mx = -INFINITY;
+    for (int c = lane; c < valid; c += 32) mx = fmaxf(mx, mr ? xr[c] + mr[c] : xr[c]);
+    mx = warp_max(mx);
+    float s = 0.f;
+    for (int c = lane; c < valid; c += 32) s += expf((mr ? xr[c] + mr[c] : xr[c]) - mx);
+    s = warp_sum(s);
+    const float inv = 1.0f / s;
+    __syncwarp();
+    for (int c = lane; c < cols; c += 32)
+        yr[c] = (c < valid) ? expf((mr ? xr[c] + mr[c] : xr[c]) - mx) * inv : 0.0f;
+}
+
+// Fast path for cols == 128 (the Arctic attention shape at S=128): a row is one float4 per lane.
+__global__ void softmax_rows128_kernel(const float* x, const float* mask, const int* key_len,
+                                       int rows_per_group, float* y, long long rows) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float4 v = reinterpret_cast<const float4*>(x + row * 128)[lane];
+    if (mask) {
+        const float4 m = reinterpret_cast<const float4*>(mask + row * 128)[lane];
+        v.x += m.x; v.y += m.y; v.z += m.z; v.w += m.w;
+    }
+    const int valid = key_len ? min(max(key_len[row / rows_per_group], 0), 128) : 128;
+    const int c = lane * 4;
+    if (c + 0 >= valid) v.x = -INFINITY;
+    if (c + 1 >= valid) v.y = -INFINITY;
+    if (c + 2 >= valid) v.z = -INFINITY;
+    if (c + 3 >= valid) v.w = -INFINITY;
+    const float mx = warp_max(fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    float4 e;
+    e.x = (c + 0 < valid) ? expf(v.x - mx) : 0.f;
+    e.y = (c + 1 < valid) ? expf(v.y - mx) : 0.f;
+    e.z = (c + 2 < valid) ? expf(v.z - mx) : 0.f;
+    e.w = (c + 3 < valid) ? expf(v.w - mx) : 0.f;
+    const float inv = 1.0f / warp_sum((e.x + e.y) + (e.z + e.w));
+    e.x *= inv; e.y *= inv; e.z *= inv; e.w *= inv;
+    reinterpret_cast<float4*>(y + row * 128)[lane] = e;
+}
+
+// ---- quantisers ---------------------------------------------------------------------------------
+// quantize_arctic_xs.zig:94-115 (f16 scale) when F16SCALE, else the per-token activation rule.
+template <bool F16SCALE>
+__global__ void quant_rows_kernel(const float* x, int8_t* q, void* scale, long long rows, int cols) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * cols;
+    float m = 0.f;
+    for (int c = lane; c < cols; c += 32) m = fmaxf(m, fabsf(xr[c]));
+    m = warp_max(m);
+    float s = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
+    if constexpr (F16SCALE) {
+        const __half h = __float2half_rn(s);
+        if (lane == 0) reinterpret_cast<__half*>(scale)[row] = h;
+        s = __half2float(h);
+    } else {
+        if (lane == 0) reinterpret_cast<float*>(scale)[row] = s;
+    }
+    const float inv = __fdiv_rn(1.0f, s);
+    int8_t* qr = q + row * cols;
+    for (int c = lane; c < cols; c += 32) qr[c] = quant1(xr[c], inv);
+}
+
+// ---- converters ---------------------------------------------------------------------------------
+__global__ void f32_to_f16_kernel(const float* x, __half* y, long long n) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        y[i] = __float2half_rn(x[i]);
+}
+__global__ void i8_to_f16_kernel(const int8_t* x, __half* y, long long n) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        y[i] = __int2half_rn(static_cast<int>(x[i]));
+}
+__global__ void f16bits_to_f32_kernel(const uint16_t* x, float* y, long long n) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        y[i] = __half2float(__ushort_as_half(x[i]));
+}
+__global__ void transpose_kernel(const float* x, float* y, int rows, int cols) {
+    __shared__ float tile[32][33];
+    const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int r = by + j, c = bx + threadIdx.x;
+        if (r < rows && c < cols) tile[j][threadIdx.x] = x[static_cast<long long>(r) * cols + c];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int r = bx + j, c = by + threadIdx.x;  // y is [cols, rows]
+        if (r < cols && c < rows) y[static_cast<long long>(r) * rows + c] = tile[threadIdx.x][j];
+    }
+}
+
+// ---- elementwise chains -------------------------------------------------------------------------
+// exp((a + b) * c), b broadcast along rows: the executor's three passes fused into one.
+__global__ void ew_add_mul_exp_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
+                                      const float4* __restrict__ c, float4* __restrict__ out,
+                                      long long n4, int cols4) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const float4 av = __ldcs(a + i);
+        const float4 cv = __ldcs(c + i);
+        const float4 bv = __ldg(b + (i % cols4));
+        float4 o;
+        o.x = expf((av.x + bv.x) * cv.x);
+        o.y = expf((av.y + bv.y) * cv.y);
+        o.z = expf((av.z + bv.z) * cv.z);
+        o.w = expf((av.w + bv.w) * cv.w);
+        __stcs(out + i, o);
+    }
+}
+__global__ void ew_add_mul_exp_any_kernel(const float* a, const float* b, const float* c, float* out,
+                                          long long n, int cols) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        out[i] = expf((a[i] + b[i % cols]) * c[i]);
+}
+
+struct OpList {
+    int n;
+    int op[8];
+};
+
+__global__ void ew_unary_chain_kernel(const float* x, float* out, long long n, OpList ops) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        float v = x[i];
+        for (int o = 0; o < ops.n; ++o) v = unary_op(ops.op[o], v);
+        out[i] = v;
+    }
+}
+
+// Fused pre-ops + reduction.  Stage 1: per-block partials (f64 for sum/mean); stage 2: one block.
+__global__ void reduce_stage1_kernel(const float* x, long long n, int red, OpList pre, double* part) {
+    double acc = (red == TZ_RED_PROD) ? 1.0 : (red == TZ_RED_MAX) ? -INFINITY : (red == TZ_RED_MIN) ? INFINITY : 0.0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        float v = x[i];
+        for (int o = 0; o < pre.n; ++o) v = unary_op(pre.op[o], v);
+        acc = red_combine(red, acc, static_cast<double>(v));
+    }
+    __shared__ double sh[32];
+    acc = block_reduce(red, acc, sh);
+    if (threadIdx.x == 0) part[blockIdx.x] = acc;
+}
+__global__ void reduce_stage2_kernel(const double* part, int nparts, long long n, int red, float* out) {
+    double acc = (red == TZ_RED_PROD) ? 1.0 : (red == TZ_RED_MAX) ? -INFINITY : (red == TZ_RED_MIN) ? INFINITY : 0.0;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) acc = red_combine(red, acc, part[i]);
+    __shared__ double sh[32];
+    acc = block_reduce(red, acc, sh);
+    if (threadIdx.x == 0) {
+        if (red == TZ_RED_MEAN && n > 0) acc /= static_cast<double>(n);
+        *out = static_cast<float>(acc);
+    }
+}
+
+// gather.zig:15-57 with the device status word in place of the safe-build bounds check.
+__global__ void gather_rows_kernel(const float* table, long long table_rows, const uint32_t* ids,
+                                   long long n_ids, int cols, float* out, int* status) {
+    const long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n_ids) return;
+    const uint32_t id = ids[r];
+    const bool ok = id < table_rows;
+    if (!ok && lane == 0) atomicOr(status, TZ_DEV_BOUNDS);
+    const float* src = table + static_cast<long long>(ok ? id : 0) * cols;
+    float* dst = out + r * cols;
+    for (int c = lane; c < cols; c += 32) dst[c] = ok ? src[c] : 0.0f;
+}
+
+inline int ew_grid(tz_ctx_t ctx, long long work, int threads) {
+    long long blocks = (work + threads - 1) / threads;
+    const long long cap = static_cast<long long>(ctx->sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+inline int warp_rows_grid(long long rows) { return static_cast<int>((rows * 32 + 255) / 256); }
+
+}  // namespace
+
+// ---- launchers shared with the model -----------------------------------------------------------
+int launch_f32_to_f16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s) {
+    f32_to_f16_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(x, static_cast<__half*>(y), n);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+int launch_i8_to_f16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s) {
+    i8_to_f16_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(x, static_cast<__half*>(y), n);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+int launch_f16bits_to_f32(tz_ctx_t ctx, const uint16_t* x, float* y, long long n, cudaStream_t s) {
+    f16bits_to_f32_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(x, y, n);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+int launch_quant_act(tz_ctx_t ctx, const float* x, int8_t* q, float* scale, long long rows, int cols,
+                     cudaStream_t s) {
+    if (rows == 0) return TZ_OK;
+    quant_rows_kernel<false><<<warp_rows_grid(rows), 256, 0, s>>>(x, q, scale, rows, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+}  // namespace tz
+
+using namespace tz;
+
+extern "C" {
+
+int tz_layernorm_last_dim(tz_ctx_t ctx, const float* x, const float* gamma, const float* beta,
+                          float* y, int64_t rows, int cols, float eps, tz_stream_t stream) {
+    TZ_CHECK(ctx && x && gamma && beta && y && rows >= 0 && cols > 0, TZ_EINVAL,
+             "tz_layernorm_last_dim: bad arguments");
+    if (rows == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    const bool al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(gamma) % 16 == 0 && reinterpret_cast<uintptr_t>(beta) % 16 == 0;
+    const int g = warp_rows_grid(rows);
+    if (al && cols == 384)
+        ln_rows_reg_kernel<3><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+    else if (al && cols == 128)
+        ln_rows_reg_kernel<1><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+    else if (al && cols == 256)
+        ln_rows_reg_kernel<2><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+    else if (al && cols == 512)
+        ln_rows_reg_kernel<4><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+    else if (al && cols == 768)
+        ln_rows_reg_kernel<6><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+    else if (al && cols == 1024)
+        ln_rows_reg_kernel<8><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+    else
+        ln_rows_any_kernel<<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_softmax_last_axis(tz_ctx_t ctx, const float* x, const float* mask, float* y, int64_t rows,
+                         int cols, tz_stream_t stream) {
+    TZ_CHECK(ctx && x && y && rows >= 0 && cols >= 0, TZ_EINVAL, "tz_softmax_last_axis: bad arguments");
+    if (rows == 0 || cols == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    const bool al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
+                    (!mask || reinterpret_cast<uintptr_t>(mask) % 16 == 0);
+    if (cols == 128 && al)
+        softmax_rows128_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, mask, nullptr, 1, y, rows);
+    else
+        softmax_rows_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, mask, nullptr, 1, y, rows, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_softmax_keylen(tz_ctx_t ctx, const float* x, const int32_t* key_len, float* y, int64_t groups,
+                      int rows_per_group, int cols, tz_stream_t stream) {
+    TZ_CHECK(ctx && x && y && key_len && groups >= 0 && rows_per_group > 0 && cols > 0, TZ_EINVAL,
+             "tz_softmax_keylen: bad arguments");
+    const long long rows = groups * static_cast<long long>(rows_per_group);
+    if (rows == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    const bool al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+    if (cols == 128 && al)
+        softmax_rows128_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows);
+    else
+        softmax_rows_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_quantize_weight_rows(tz_ctx_t ctx, const float* w, int8_t* q, uint16_t* scale_f16, int64_t rows,
+                            int cols, tz_stream_t stream) {
+    TZ_CHECK(ctx && w && q && scale_f16 && rows >= 0 && cols > 0, TZ_EINVAL,
+             "tz_quantize_weight_rows: bad arguments");
+    if (rows == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    quant_rows_kernel<true><<<warp_rows_grid(rows), 256, 0, s>>>(w, q, scale_f16, rows, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_quantize_act_rows(tz_ctx_t ctx, const float* x, int8_t* q, float* scale, int64_t rows, int cols,
+                         tz_stream_t stream) {
+    TZ_CHECK(ctx && x && q && scale && rows >= 0 && cols > 0, TZ_EINVAL, "tz_quantize_act_rows: bad arguments");
+    return launch_quant_act(ctx, x, q, scale, rows, cols, pick_stream(ctx, stream));
+}
+
+int tz_ew_add_mul_exp(tz_ctx_t ctx, const float* a, const float* b_row, const float* c, float* out,
+                      int64_t rows, int cols, tz_stream_t stream) {
+    TZ_CHECK(ctx && a && b_row && c && out && rows >= 0 && cols > 0, TZ_EINVAL, "tz_ew_add_mul_exp: bad arguments");
+    const long long n = rows * static_cast<long long>(cols);
+    if (n == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    const bool al = cols % 4 == 0 && reinterpret_cast<uintptr_t>(a) % 16 == 0 && reinterpret_cast<uintptr_t>(c) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(out) % 16 == 0 && reinterpret_cast<uintptr_t>(b_row) % 16 == 0;
+    if (al)
+        ew_add_mul_exp_kernel<<<ew_grid(ctx, n / 4, 256), 256, 0, s>>>(
+            reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b_row),
+            reinterpret_cast<const float4*>(c), reinterpret_cast<float4*>(out), n / 4, cols / 4);
+    else
+        ew_add_mul_exp_any_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(a, b_row, c, out, n, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_ew_unary_chain(tz_ctx_t ctx, const float* x, float* out, int64_t n, const int* ops, int n_ops,
+                      tz_stream_t stream) {
+    TZ_CHECK(ctx && x && out && n >= 0 && n_ops >= 0 && n_ops <= 8 && (n_ops == 0 || ops), TZ_EINVAL,
+             "tz_ew_unary_chain: bad arguments");
+    if (n == 0) return TZ_OK;
+    OpList l{};
+    l.n = n_ops;
+    for (int i = 0; i < n_ops; ++i) {
+        TZ_CHECK(ops[i] >= TZ_OP_RELU && ops[i] <= TZ_OP_COS, TZ_EINVAL, "tz_ew_unary_chain: op %d is not unary", ops[i]);
+        l.op[i] = ops[i];
+    }
+    cudaStream_t s = pick_stream(ctx, stream);
+    ew_unary_chain_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(x, out, n, l);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_reduce(tz_ctx_t ctx, int reduce_op, const int* pre_ops, int n_pre, const float* x, int64_t n,
+              float* out, tz_stream_t stream) {
+    TZ_CHECK(ctx && out && (n == 0 || x) && n >= 0 && reduce_op >= 0 && reduce_op <= 4 && n_pre >= 0 && n_pre <= 8 &&
+                 (n_pre == 0 || pre_ops),
+             TZ_EINVAL, "tz_reduce: bad arguments");
+    OpList l{};
+    l.n = n_pre;
+    for (int i = 0; i < n_pre; ++i) {
+        TZ_CHECK(pre_ops[i] >= TZ_OP_RELU && pre_ops[i] <= TZ_OP_COS, TZ_EINVAL, "tz_reduce: op %d is not unary", pre_ops[i]);
+        l.op[i] = pre_ops[i];
+    }
+    cudaStream_t s = pick_stream(ctx, stream);
+    const int parts = ew_grid(ctx, n > 0 ? n : 1, 256);
+    void* scratch = nullptr;
+    int rc = scratch_reserve(ctx, sizeof(double) * parts, &scratch);
+    if (rc) return rc;
+    double* part = static_cast<double*>(scratch);
+    reduce_stage1_kernel<<<parts, 256, 0, s>>>(x, n, reduce_op, l, part);
+    reduce_stage2_kernel<<<1, 256, 0, s>>>(part, parts, n, reduce_op, out);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_gather_rows(tz_ctx_t ctx, const float* table, int64_t table_rows, const uint32_t* ids, int64_t n_ids,
+                   int cols, float* out, tz_stream_t stream) {
+    TZ_CHECK(ctx && table && ids && out && n_ids >= 0 && cols > 0, TZ_EINVAL, "tz_gather_rows: bad arguments");
+    if (n_ids == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    gather_rows_kernel<<<warp_rows_grid(n_ids), 256, 0, s>>>(table, table_rows, ids, n_ids, cols, out, ctx->d_status);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+}  // extern "C"
+
+namespace tz {
+int launch_transpose(const float* x, float* y, int rows, int cols, cudaStream_t s) {
+    dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+    transpose_kernel<<<grid, block, 0, s>>>(x, y, rows, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+}  // namespace tz

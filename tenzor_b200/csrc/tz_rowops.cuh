@@ -1,0 +1,81 @@
+// tz_rowops.cuh -- device helpers shared by the row kernels and the model kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "../../include/tenzor_cuda.h"
+
+namespace tz {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// q = clamp(round(x * inv), -127, 127), round half away from zero (Zig @round / C roundf).
+__device__ __forceinline__ int8_t quant1(float x, float inv) {
+    float r = roundf(__fmul_rn(x, inv));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return static_cast<int8_t>(static_cast<int>(r));
+}
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// Unary op table of the reference fusion codegen (codegen.zig:228-244); TZ_OP_* codes.
+__device__ __forceinline__ float unary_op(int op, float x) {
+    switch (op) {
+        case TZ_OP_RELU: return x > 0.0f ? x : 0.0f;
+        case TZ_OP_GELU: {
+            const float x3 = x * x * x;
+            const float inner = 0.7978845608028654f * (x + 0.044715f * x3);
+            return 0.5f * x * (1.0f + (2.0f * sigmoid_f(2.0f * inner) - 1.0f));
+        }
+        case TZ_OP_SIGMOID: return sigmoid_f(x);
+        case TZ_OP_TANH: return 2.0f * sigmoid_f(2.0f * x) - 1.0f;
+        case TZ_OP_EXP: return expf(x);
+        case TZ_OP_NEG: return -x;
+        case TZ_OP_ABS: return fabsf(x);
+        case TZ_OP_SILU: return x * sigmoid_f(x);
+        case TZ_OP_LOG: return logf(x);
+        case TZ_OP_SQRT: return sqrtf(x);
+        case TZ_OP_RSQRT: return 1.0f / sqrtf(x);
+        case TZ_OP_SIN: return sinf(x);
+        case TZ_OP_COS: return cosf(x);
+        default: return x;
+    }
+}
+
+__device__ __forceinline__ double red_combine(int red, double a, double b) {
+    switch (red) {
+        case TZ_RED_PROD: return a * b;
+        case TZ_RED_MAX: return a > b ? a : b;
+        case TZ_RED_MIN: return a < b ? a : b;
+        default: return a + b;
+    }
+}
+
+__device__ __forceinline__ double block_reduce(int red, double v, double* sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = red_combine(red, v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    if (w == 0) {
+        double t = (lane < nw) ? sh[lane] : ((red == TZ_RED_PROD) ? 1.0 : (red == TZ_RED_MAX) ? -INFINITY : (red == TZ_RED_MIN) ? INFINITY : 0.0);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t = red_combine(red, t, __shfl_xor_sync(0xffffffffu, t, o));
+        v = t;
+    }
+    return v;
+}
+
+}  // namespace tz

@@ -1,0 +1,147 @@
+"""Op-level entry points on device tensors (torch CUDA tensors are used only as device memory;
+every computation runs in libtenzor_cuda.so).  Names follow the reference kernels they replace:
+
+  layer_norm_last_dim   layernorm.zig:26-116          softmax_last_axis   softmax.zig:20-155
+  linear (f32)          arctic.zig:599-620 / matmul.zig:54-77 (tcgen05 kind::tf32)
+  linear_w8a32          matmul_w8a32.zig:14-58        linear_w8a8         (W8A8, no counterpart)
+  gemm_i8_i32           exact int32 accumulators      quantize_weight_rows  quantize_arctic_xs.zig:94-115
+  matmul_epilogue       codegen.zig:78-147            ew_add_mul_exp      executor.zig:114-197
+  ew_unary_chain        codegen.zig:15-74             reduce              codegen.zig:151-205
+  gather_rows           gather.zig:15-57
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib as L
+from .runtime import Context
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(s=None):
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream if s is None else s)
+
+
+def _dev(t, dtype):
+    assert t.is_cuda and t.is_contiguous() and t.dtype == dtype, (t.device, t.dtype, t.is_contiguous())
+    return t
+
+
+def layer_norm_last_dim(ctx: Context, x, gamma, beta, eps: float, out=None):
+    _dev(x, torch.float32)
+    out = torch.empty_like(x) if out is None else out
+    cols = x.shape[-1]
+    L.check(L.lib().tz_layernorm_last_dim(ctx.handle, _p(x), _p(gamma), _p(beta), _p(out), x.numel() // cols,
+                                          cols, eps, _stream()))
+    return out
+
+
+def softmax_last_axis(ctx: Context, x, mask=None, out=None):
+    _dev(x, torch.float32)
+    out = torch.empty_like(x) if out is None else out
+    cols = x.shape[-1]
+    L.check(L.lib().tz_softmax_last_axis(ctx.handle, _p(x), _p(mask), _p(out), x.numel() // cols, cols, _stream()))
+    return out
+
+
+def softmax_keylen(ctx: Context, x, key_len, out=None):
+    """x [G, R, C]; group g keeps its first key_len[g] columns."""
+    _dev(x, torch.float32)
+    out = torch.empty_like(x) if out is None else out
+    G, R, Cc = x.shape
+    L.check(L.lib().tz_softmax_keylen(ctx.handle, _p(x), _p(key_len), _p(out), G, R, Cc, _stream()))
+    return out
+
+
+def linear(ctx: Context, x, w, bias=None, residual=None, out=None):
+    m, k = x.shape
+    n = w.shape[0]
+    out = torch.empty((m, n), device=x.device, dtype=torch.float32) if out is None else out
+    L.check(L.lib().tz_linear_f32(ctx.handle, _p(x), _p(w), _p(bias), _p(residual), _p(out), m, k, n, _stream()))
+    return out
+
+
+def linear_w8a32(ctx: Context, x, wq, scale_f16, bias, out=None):
+    m, k = x.shape
+    n = wq.shape[0]
+    out = torch.empty((m, n), device=x.device, dtype=torch.float32) if out is None else out
+    L.check(L.lib().tz_linear_w8a32(ctx.handle, _p(x), _p(wq), _p(scale_f16), _p(bias), _p(out), m, k, n, _stream()))
+    return out
+
+
+def linear_w8a8(ctx: Context, x, wq, scale_f16, bias, out=None):
+    m, k = x.shape
+    n = wq.shape[0]
+    out = torch.empty((m, n), device=x.device, dtype=torch.float32) if out is None else out
+    L.check(L.lib().tz_linear_w8a8(ctx.handle, _p(x), _p(wq), _p(scale_f16), _p(bias), _p(out), m, k, n, _stream()))
+    return out
+
+
+def gemm_i8_i32(ctx: Context, a, w, out=None):
+    m, k = a.shape
+    n = w.shape[0]
+    out = torch.empty((m, n), device=a.device, dtype=torch.int32) if out is None else out
+    L.check(L.lib().tz_gemm_i8_i32(ctx.handle, _p(a), _p(w), _p(out), m, k, n, _stream()))
+    return out
+
+
+def quantize_weight_rows(ctx: Context, w):
+    rows, cols = w.shape
+    q = torch.empty((rows, cols), device=w.device, dtype=torch.int8)
+    s = torch.empty(rows, device=w.device, dtype=torch.int16)  # IEEE half bits
+    L.check(L.lib().tz_quantize_weight_rows(ctx.handle, _p(w), _p(q), _p(s), rows, cols, _stream()))
+    return q, s
+
+
+def quantize_act_rows(ctx: Context, x):
+    rows, cols = x.shape
+    q = torch.empty((rows, cols), device=x.device, dtype=torch.int8)
+    s = torch.empty(rows, device=x.device, dtype=torch.float32)
+    L.check(L.lib().tz_quantize_act_rows(ctx.handle, _p(x), _p(q), _p(s), rows, cols, _stream()))
+    return q, s
+
+
+def matmul_epilogue(ctx: Context, a, b, bias, ops, trans_b=False, out=None):
+    m, k = a.shape
+    n = b.shape[0] if trans_b else b.shape[1]
+    out = torch.empty((m, n), device=a.device, dtype=torch.float32) if out is None else out
+    codes = (C.c_int * max(1, len(ops)))(*[L.OP[o] if isinstance(o, str) else int(o) for o in ops])
+    L.check(L.lib().tz_matmul_epilogue(ctx.handle, _p(a), _p(b), int(trans_b), _p(bias), C.addressof(codes),
+                                       len(ops), _p(out), m, k, n, _stream()))
+    return out
+
+
+def ew_add_mul_exp(ctx: Context, a, b_row, c, out=None):
+    out = torch.empty_like(a) if out is None else out
+    cols = b_row.numel()
+    L.check(L.lib().tz_ew_add_mul_exp(ctx.handle, _p(a), _p(b_row), _p(c), _p(out), a.numel() // cols, cols,
+                                      _stream()))
+    return out
+
+
+def ew_unary_chain(ctx: Context, x, ops, out=None):
+    out = torch.empty_like(x) if out is None else out
+    codes = (C.c_int * max(1, len(ops)))(*[L.OP[o] for o in ops])
+    L.check(L.lib().tz_ew_unary_chain(ctx.handle, _p(x), _p(out), x.numel(), C.addressof(codes), len(ops),
+                                      _stream()))
+    return out
+
+
+def reduce(ctx: Context, op: str, pre_ops, x):
+    out = torch.empty(1, device=x.device, dtype=torch.float32)
+    codes = (C.c_int * max(1, len(pre_ops)))(*[L.OP[o] for o in pre_ops])
+    L.check(L.lib().tz_reduce(ctx.handle, L.RED[op], C.addressof(codes), len(pre_ops), _p(x), x.numel(), _p(out),
+                              _stream()))
+    return out
+
+
+def gather_rows(ctx: Context, table, ids, out=None):
+    rows, cols = table.shape
+    out = torch.empty((ids.numel(), cols), device=table.device, dtype=torch.float32) if out is None else out
+    L.check(L.lib().tz_gather_rows(ctx.handle, _p(table), rows, _p(ids), ids.numel(), cols, _p(out), _stream()))
+    return out

@@ -1,0 +1,64 @@
+"""Sequence-batch sharding across GPUs (one process per GPU).
+
+The forward has no cross-sequence dependency, so the batch is split by sequence with no collective
+on the hot path; only the final [B, 384] embeddings travel to rank 0.  Sequences are dealt
+longest-first to the rank with the least work, work(L) = L + L^2/2304, which is proportional to the
+forward's FLOPs 6*(3,538,944*L + 1,536*L^2), so every rank gets a near-equal share of them.
+"""
+from __future__ import annotations
+
+import heapq
+
+import numpy as np
+
+
+def work(L: np.ndarray) -> np.ndarray:
+    L = np.asarray(L, np.float64)
+    # FLOP(L) = 6*(3,538,944*L + 1,536*L^2) -> proportional to L + L^2/2304
+    return L + L * L / 2304.0
+
+
+def shard_by_tokens(lengths, world: int):
+    """Returns `world` sorted index arrays that partition range(len(lengths))."""
+    lengths = np.asarray(lengths)
+    order = np.argsort(-work(lengths), kind="stable")
+    heap = [(0.0, r) for r in range(world)]
+    buckets = [[] for _ in range(world)]
+    w = work(lengths)
+    for i in order:
+        load, r = heapq.heappop(heap)
+        buckets[r].append(int(i))
+        heapq.heappush(heap, (load + float(w[i]), r))
+    return [np.array(sorted(b), dtype=np.int64) for b in buckets]
+
+
+def gather_to_rank0(local: "torch.Tensor", index: np.ndarray, total: int, group=None):
+    """Gathers each rank's [n_r, D] embeddings to rank 0 and reorders them into the global batch
+    order (`index` = this rank's global row ids).  Returns the [total, D] tensor on rank 0, None
+    elsewhere.  One torch.distributed.gather of padded buffers (NCCL or gloo)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n = torch.tensor([local.shape[0]], device=local.device, dtype=torch.int64)
+    ns = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(ns, n, group=group)
+    cap = int(max(int(x.item()) for x in ns))
+    pad = torch.zeros((cap, local.shape[1]), device=local.device, dtype=local.dtype)
+    pad[: local.shape[0]] = local
+    idx = torch.full((cap,), -1, device=local.device, dtype=torch.int64)
+    idx[: local.shape[0]] = torch.as_tensor(index, device=local.device)
+    if rank == 0:
+        bufs = [torch.empty_like(pad) for _ in range(world)]
+        ibufs = [torch.empty_like(idx) for _ in range(world)]
+    else:
+        bufs = ibufs = None
+    dist.gather(pad, bufs, dst=0, group=group)
+    dist.gather(idx, ibufs, dst=0, group=group)
+    if rank != 0:
+        return None
+    out = torch.empty((total, local.shape[1]), device=local.device, dtype=local.dtype)
+    for b, ib in zip(bufs, ibufs):
+        keep = ib >= 0
+        out[ib[keep]] = b[keep]
+    return out
