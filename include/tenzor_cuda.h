@@ -131,9 +131,10 @@ int tz_arctic_debug_hidden(tz_model_t model, int stage, float* out, int64_t tota
 int tz_arctic_debug_operand(tz_model_t model, int which, int8_t* q_out, float* scale_out,
                             int64_t total_tokens);
 
-/* Kernel timing of the forward: when enabled, CUDA events are recorded on the launching stream
- * between consecutive launches (inside the captured graph too).  tz_arctic_profile_read returns,
- * for the LAST forward, the summed milliseconds and the launch count per kernel class:
+/* Kernel timing of the forward: when enabled (enable = number of forwards to keep, 0 = off), CUDA
+ * events are recorded on the launching stream between consecutive launches (inside a captured
+ * graph too).  tz_arctic_profile_read returns, summed over the kept forwards since enabling, the
+ * milliseconds and the launch count per kernel class:
  * 0 embedding+LN, 1 QKV GEMM, 2 attention, 3 attention-output GEMM, 4 LayerNorm, 5 FFN1 GEMM,
  * 6 FFN1 requantisation (W8A8), 7 FFN2 GEMM, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
 #define TZ_PROF_CLASSES 9

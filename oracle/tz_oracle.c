@@ -97,11 +97,60 @@ float tzo_bf16_to_f32(uint16_t h) {
 /* ------------------------------------------------------------------------------------------ */
 /* Optional CBLAS, loaded at run time like blas.zig:140-260 (env TENZOR_BLAS_LIB).              */
 /* ------------------------------------------------------------------------------------------ */
+static void* dlopen_with_siblings(const char* path, int depth);
+static void* dlopen_with_siblings_global(const char* path, int depth) {
+    void* h = dlopen(path, RTLD_NOW | RTLD_GLOBAL);
+    if (h || depth > 6) return h;
+    const char* err = dlerror();
+    if (!err || !strstr(err, "cannot open shared object file")) return NULL;
+    const char* colon = strchr(err, ':');
+    char dep[256];
+    size_t n = colon ? (size_t)(colon - err) : 0;
+    if (n == 0 || n >= sizeof dep) return NULL;
+    memcpy(dep, err, n);
+    dep[n] = 0;
+    char dir[512];
+    snprintf(dir, sizeof dir, "%s", path);
+    char* slash = strrchr(dir, '/');
+    if (!slash) return NULL;
+    *slash = 0;
+    char full[800];
+    snprintf(full, sizeof full, "%s/%s", dir, dep);
+    if (!dlopen_with_siblings_global(full, depth + 1)) return NULL;
+    return dlopen_with_siblings_global(path, depth + 1);
+}
+
 typedef void (*cblas_sgemm_fn)(int, int, int, int, int, int, float, const float*, int,
                                const float*, int, float, float*, int);
 static cblas_sgemm_fn g_sgemm = NULL;
 static int g_blas_tried = 0;
 static char g_blas_status[512] = "not loaded";
+
+/* dlopen that also resolves sibling dependencies of a bundled library (e.g. an OpenBLAS shipped with
+ * its own libgfortran / libquadmath next to it and no RPATH): on "X: cannot open shared object
+ * file", X is loaded from the library's directory with RTLD_GLOBAL and the open is retried. */
+static void* dlopen_with_siblings(const char* path, int depth) {
+    void* h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+    if (h || depth > 6) return h;
+    const char* err = dlerror();
+    if (!err) return NULL;
+    const char* colon = strchr(err, ':');
+    if (!colon || !strstr(err, "cannot open shared object file")) return NULL;
+    char dep[256];
+    size_t n = (size_t)(colon - err);
+    if (n == 0 || n >= sizeof dep) return NULL;
+    memcpy(dep, err, n);
+    dep[n] = 0;
+    char dir[512];
+    snprintf(dir, sizeof dir, "%s", path);
+    char* slash = strrchr(dir, '/');
+    if (!slash) return NULL;
+    *slash = 0;
+    char full[800];
+    snprintf(full, sizeof full, "%s/%s", dir, dep);
+    if (!dlopen_with_siblings_global(full, depth + 1)) return NULL;
+    return dlopen_with_siblings(path, depth + 1);
+}
 
 static void blas_init(void) {
     if (g_blas_tried) return;
@@ -110,7 +159,7 @@ static void blas_init(void) {
         if (!g_blas_tried) {
             const char* path = getenv("TENZOR_BLAS_LIB");
             if (path && *path) {
-                void* h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+                void* h = dlopen_with_siblings(path, 0);
                 if (h) {
                     g_sgemm = (cblas_sgemm_fn)dlsym(h, "cblas_sgemm");
                     void (*set_threads)(int) = (void (*)(int))dlsym(h, "openblas_set_num_threads");

@@ -118,6 +118,7 @@ class ArcticModel:
         self.handle = handle
         self.mode = mode
         self.config = ARCTIC_EMBED_XS
+        ctx._adopt(self)
 
     @classmethod
     def from_checkpoint(cls, ctx: Context, ckpt: dict, mode: str = "f32") -> "ArcticModel":

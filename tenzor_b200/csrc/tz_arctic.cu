@@ -266,6 +266,7 @@ struct DevLayer {
 
 struct tz_model_s {
     tz_ctx_t ctx = nullptr;
+    int device = 0;
     int mode = TZ_QUANT_F32;
     std::vector<void*> allocs;  // every device allocation owned by the model
     EmbTables emb{};
@@ -295,7 +296,10 @@ struct tz_model_s {
     int64_t last_T = 0;
     // kernel-class timing: events around every launch of the forward (recorded in graphs too)
     bool profile = false;
-    std::vector<cudaEvent_t> ev;  // kMaxLaunch + 1
+    std::vector<cudaEvent_t> ev;  // prof_slots x 65: one set of events per recorded forward
+    int prof_slots = 0;
+    int64_t prof_fwd = 0;         // forwards recorded since profiling was enabled
+    int ev_base = 0;              // first event of the current forward's set
     int ev_n = 0;                 // events recorded by the last enqueue
     int ev_cls[64] = {0};         // class of launch i
     // graph cache for the host-pointer forward
@@ -313,11 +317,19 @@ int dalloc(tz_model_s* m, std::vector<void*>& list, size_t bytes, void** p) {
     return TZ_OK;
 }
 
+// Host -> device copy ordered on the context stream and complete on return.  (A plain cudaMemcpy
+// from pageable memory may return before its DMA lands, and the conversion kernels that consume
+// the copies run on the context's non-blocking stream, so the copy must be stream-ordered.)
+int h2d(tz_model_s* m, void* dst, const void* src, size_t bytes) {
+    TZ_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, m->ctx->stream));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    return TZ_OK;
+}
+
 int upload_raw(tz_model_s* m, const void* src, size_t bytes, void** dst) {
     int rc = dalloc(m, m->allocs, bytes, dst);
     if (rc) return rc;
-    TZ_CUDA(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
-    return TZ_OK;
+    return h2d(m, *dst, src, bytes);
 }
 
 int upload_f32(tz_model_s* m, const float* src, size_t n, float** dst, const char* what) {
@@ -334,8 +346,9 @@ int upload_linear(tz_model_s* m, const tz_mat_weight& w, int rows, int cols, voi
         TZ_CHECK(w.f32, TZ_EINVAL, "%s: mode F32 needs f32 weights", what);
         void* tmp = nullptr;
         TZ_CUDA(cudaMalloc(&tmp, sizeof(float) * rows * cols));
-        cudaMemcpy(tmp, w.f32, sizeof(float) * rows * cols, cudaMemcpyHostToDevice);
-        int rc = launch_f32_to_f16(m->ctx, static_cast<float*>(tmp), static_cast<__half*>(dst) + static_cast<long long>(row0) * cols,
+        int rc = h2d(m, tmp, w.f32, sizeof(float) * rows * cols);
+        if (!rc)
+            rc = launch_f32_to_f16(m->ctx, static_cast<float*>(tmp), static_cast<__half*>(dst) + static_cast<long long>(row0) * cols,
                                    static_cast<long long>(rows) * cols, s);
         cudaStreamSynchronize(s);
         cudaFree(tmp);
@@ -346,9 +359,10 @@ int upload_linear(tz_model_s* m, const tz_mat_weight& w, int rows, int cols, voi
     void* ts = nullptr;
     TZ_CUDA(cudaMalloc(&tq, static_cast<size_t>(rows) * cols));
     TZ_CUDA(cudaMalloc(&ts, sizeof(uint16_t) * rows));
-    cudaMemcpy(tq, w.q8, static_cast<size_t>(rows) * cols, cudaMemcpyHostToDevice);
-    cudaMemcpy(ts, w.scale_f16, sizeof(uint16_t) * rows, cudaMemcpyHostToDevice);
-    int rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), scale_dst + row0, rows, s);
+    int rc = h2d(m, tq, w.q8, static_cast<size_t>(rows) * cols);
+    if (!rc) rc = h2d(m, ts, w.scale_f16, sizeof(uint16_t) * rows);
+    if (!rc)
+        rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), scale_dst + row0, rows, s);
     if (!rc) {
         if (m->mode == TZ_QUANT_W8A8)
             TZ_CUDA(cudaMemcpyAsync(static_cast<int8_t*>(dst) + static_cast<long long>(row0) * cols, tq,
@@ -383,8 +397,8 @@ int upload_table(tz_model_s* m, const tz_mat_weight& w, int rows, const float** 
     rc = dalloc(m, m->allocs, sizeof(float) * rows, reinterpret_cast<void**>(&ds));
     if (rc) return rc;
     TZ_CUDA(cudaMalloc(&ts, sizeof(uint16_t) * rows));
-    cudaMemcpy(ts, w.scale_f16, sizeof(uint16_t) * rows, cudaMemcpyHostToDevice);
-    rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), ds, rows, m->ctx->stream);
+    rc = h2d(m, ts, w.scale_f16, sizeof(uint16_t) * rows);
+    if (!rc) rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), ds, rows, m->ctx->stream);
     cudaStreamSynchronize(m->ctx->stream);
     cudaFree(ts);
     *q = static_cast<int8_t*>(dq);
@@ -472,8 +486,8 @@ enum ProfClass { P_EMBED = 0, P_QKV, P_ATTN, P_OPROJ, P_LN, P_FFN1, P_QUANT, P_F
 // Records the event that closes launch (ev_n - 1) and opens the next one.
 int prof_mark(tz_model_s* m, int next_class, cudaStream_t s) {
     if (!m->profile) return TZ_OK;
-    if (m->ev_n >= static_cast<int>(m->ev.size())) return TZ_OK;
-    TZ_CUDA(cudaEventRecord(m->ev[m->ev_n], s));
+    if (m->ev_n >= 65) return TZ_OK;
+    TZ_CUDA(cudaEventRecord(m->ev[m->ev_base + m->ev_n], s));
     if (next_class >= 0 && m->ev_n < 64) m->ev_cls[m->ev_n] = next_class;
     ++m->ev_n;
     return TZ_OK;
@@ -497,6 +511,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
     const int M = static_cast<int>(T);
     int rc;
     m->ev_n = 0;
+    if (m->profile) m->ev_base = static_cast<int>(m->prof_fwd % m->prof_slots) * 65;
     if ((rc = prof_mark(m, P_EMBED, s))) return rc;
     if (q8)
         embed_ln_kernel<1><<<B, 256, 0, s>>>(d_ids, d_cu, m->emb, m->emb_g, m->emb_b, m->X, m->XA, m->xs, ctx->d_status);
@@ -572,6 +587,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
     pool_l2_kernel<<<(B * 32 + 255) / 256, 256, 0, s>>>(m->X, d_cu, d_out, B);
     TZ_CUDA(cudaGetLastError());
     if ((rc = prof_mark(m, -1, s))) return rc;
+    if (m->profile) ++m->prof_fwd;
     return TZ_OK;
 }
 
@@ -654,6 +670,7 @@ int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_
     TZ_CUDA(cudaSetDevice(ctx->device));
     auto m = std::make_unique<tz_model_s>();
     m->ctx = ctx;
+    m->device = ctx->device;
     m->mode = mode;
     int rc = TZ_OK;
     auto fail_cleanup = [&](int code) {
@@ -704,9 +721,9 @@ int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_
         TRY(upload_linear(m.get(), s.output, kH, kF, d.w2, 0, d.s2, nm));
         TRY(dalloc(m.get(), m->allocs, sizeof(float) * 3 * kH, reinterpret_cast<void**>(&d.bqkv)));
         TRY(s.query_bias && s.key_bias && s.value_bias ? TZ_OK : fail(TZ_EMISSING, "missing attention bias in layer %d", l));
-        TZ_CUDA(cudaMemcpy(d.bqkv, s.query_bias, sizeof(float) * kH, cudaMemcpyHostToDevice));
-        TZ_CUDA(cudaMemcpy(d.bqkv + kH, s.key_bias, sizeof(float) * kH, cudaMemcpyHostToDevice));
-        TZ_CUDA(cudaMemcpy(d.bqkv + 2 * kH, s.value_bias, sizeof(float) * kH, cudaMemcpyHostToDevice));
+        TRY(h2d(m.get(), d.bqkv, s.query_bias, sizeof(float) * kH));
+        TRY(h2d(m.get(), d.bqkv + kH, s.key_bias, sizeof(float) * kH));
+        TRY(h2d(m.get(), d.bqkv + 2 * kH, s.value_bias, sizeof(float) * kH));
         TRY(upload_f32(m.get(), s.attn_output_bias, kH, &d.bo, "attention.output.dense.bias"));
         TRY(upload_f32(m.get(), s.intermediate_bias, kF, &d.b1, "intermediate.dense.bias"));
         TRY(upload_f32(m.get(), s.output_bias, kH, &d.b2, "output.dense.bias"));
@@ -723,8 +740,8 @@ int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_
 
 int tz_arctic_free(tz_model_t m) {
     if (!m) return TZ_OK;
-    cudaSetDevice(m->ctx->device);
-    cudaStreamSynchronize(m->ctx->stream);
+    cudaSetDevice(m->device);  // the context may already be gone: touch only the model
+    cudaDeviceSynchronize();
     free_workspace(m);
     for (void* p : m->allocs) cudaFree(p);
     for (auto& e : m->ev) cudaEventDestroy(e);
@@ -779,23 +796,28 @@ int tz_arctic_debug_hidden(tz_model_t m, int stage, float* out, int64_t T) {
         return fail(TZ_EINVAL, "stage capture was off; it is on from the next forward");
     }
     TZ_CHECK(m->d_stages && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
-    TZ_CUDA(cudaMemcpy(out, m->d_stages + static_cast<size_t>(stage) * m->cap_tokens * kH, sizeof(float) * T * kH,
-                       cudaMemcpyDeviceToHost));
+    TZ_CUDA(cudaMemcpyAsync(out, m->d_stages + static_cast<size_t>(stage) * m->cap_tokens * kH, sizeof(float) * T * kH,
+                            cudaMemcpyDeviceToHost, m->ctx->stream));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
     return TZ_OK;
 }
 
 int tz_arctic_profile(tz_model_t m, int enable) {
-    TZ_CHECK(m, TZ_EINVAL, "tz_arctic_profile: null model");
+    TZ_CHECK(m && enable >= 0, TZ_EINVAL, "tz_arctic_profile: bad arguments");
     TZ_CUDA(cudaSetDevice(m->ctx->device));
-    if (enable && m->ev.empty()) {
-        m->ev.resize(65);
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (enable && enable > m->prof_slots) {
+        for (auto& e : m->ev) cudaEventDestroy(e);
+        m->ev.assign(static_cast<size_t>(enable) * 65, nullptr);
         for (auto& e : m->ev) TZ_CUDA(cudaEventCreate(&e));
+        m->prof_slots = enable;
     }
     if (m->graph) {  // the captured graph carries (or lacks) the event nodes: recapture
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
     }
     m->profile = enable != 0;
+    m->prof_fwd = 0;
     m->ev_n = 0;
     return TZ_OK;
 }
@@ -806,15 +828,19 @@ int tz_arctic_profile_read(tz_model_t m, float* ms, int* launches) {
         ms[c] = 0.f;
         launches[c] = 0;
     }
-    TZ_CHECK(m->profile && m->ev_n >= 2, TZ_EINVAL, "no profiled forward recorded");
+    TZ_CHECK(m->profile && m->prof_fwd > 0 && m->ev_n >= 2, TZ_EINVAL, "no profiled forward recorded");
     TZ_CUDA(cudaSetDevice(m->ctx->device));
-    for (int i = 0; i + 1 < m->ev_n; ++i) {
-        float t = 0.f;
-        TZ_CUDA(cudaEventSynchronize(m->ev[i + 1]));
-        TZ_CUDA(cudaEventElapsedTime(&t, m->ev[i], m->ev[i + 1]));
-        const int c = m->ev_cls[i];
-        ms[c] += t;
-        launches[c] += 1;
+    const int sets = static_cast<int>(std::min<int64_t>(m->prof_fwd, m->prof_slots));
+    for (int k = 0; k < sets; ++k) {
+        const int b = k * 65;
+        for (int i = 0; i + 1 < m->ev_n; ++i) {
+            float t = 0.f;
+            TZ_CUDA(cudaEventSynchronize(m->ev[b + i + 1]));
+            TZ_CUDA(cudaEventElapsedTime(&t, m->ev[b + i], m->ev[b + i + 1]));
+            const int c = m->ev_cls[i];
+            ms[c] += t;
+            launches[c] += 1;
+        }
     }
     return TZ_OK;
 }
@@ -828,8 +854,9 @@ int tz_arctic_debug_operand(tz_model_t m, int which, int8_t* q_out, float* scale
     }
     TZ_CHECK(m->d_opq[which] && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
     const int K = which == 3 ? kF : kH;
-    TZ_CUDA(cudaMemcpy(q_out, m->d_opq[which], static_cast<size_t>(T) * K, cudaMemcpyDeviceToHost));
-    TZ_CUDA(cudaMemcpy(scale_out, m->d_ops[which], sizeof(float) * T, cudaMemcpyDeviceToHost));
+    TZ_CUDA(cudaMemcpyAsync(q_out, m->d_opq[which], static_cast<size_t>(T) * K, cudaMemcpyDeviceToHost, m->ctx->stream));
+    TZ_CUDA(cudaMemcpyAsync(scale_out, m->d_ops[which], sizeof(float) * T, cudaMemcpyDeviceToHost, m->ctx->stream));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
     return TZ_OK;
 }
 

@@ -3,15 +3,16 @@
 //   Y[M, N] = epilogue( A[M, K] * B[N, K]^T )        (both operands K-major, PyTorch [out,in] B)
 //
 // One CTA per SM (persistent, static round-robin over 128 x BN output tiles, tile index n-fastest
-// so neighbouring CTAs share A rows in L2).  192 threads:
+// so neighbouring CTAs share A rows in L2).  64 + 32*EPI_WARPS threads:
 //   warp 0      TMA producer: 128-byte-wide K blocks of A (128 rows) and B (BN rows) into a
 //               STAGES-deep shared-memory ring, SWIZZLE_128B, completion on `full[s]`;
 //   warp 1      allocates TMEM (2 x BN fp32/int32 columns: double-buffered accumulators); lane 0
 //               issues tcgen05.mma (M=128, N=BN, 32 bytes of K per instruction) and commits to
 //               `empty[s]` (smem slot free) and `tfull[acc]` (accumulator ready);
-//   warps 2..5  epilogue: warp w reads TMEM lane quarter (w % 4), so each thread owns one output
-//               row; 32 columns per tcgen05.ld; scale / bias / GELU / residual / row-absmax fused;
-//               vector stores straight from registers.
+//   warps 2..   epilogue: warp w reads TMEM lane quarter (w % 4) and one column slice, so each
+//               thread owns one output row of that slice; 32 columns per tcgen05.ld; scale / bias /
+//               GELU / residual / row-absmax fused in registers; each 32x32 chunk is staged in
+//               swizzled shared memory and written by one TMA bulk-tensor store (double-buffered).
 // The epilogue of tile t overlaps the MMAs of tile t+1 (second TMEM buffer).
 //
 // Replaces matmulTransposeB (reference matmul.zig:54-77), linearProjection (arctic.zig:599-635),
@@ -39,15 +40,9 @@ struct EpiParams {
     int gelu;
     unsigned* row_absmax;
     int n_ops;
-    int ops[8];
+    uint32_t ops;  // op o in bits [4o, 4o+4) (packed: no dynamic indexing of kernel parameters)
     int vec_ok;  // 16-byte aligned rows for vector stores / residual loads
 };
-
-__device__ __forceinline__ float gelu_model(float x) {
-    // arctic.zig:750-756: 0.5 x (1 + tanh(0.7978845608 (x + 0.044715 x^3))), std.math.tanh.
-    const float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, __fmul_rn(__fmul_rn(0.044715f, x), __fmul_rn(x, x))));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
 
@@ -99,7 +94,7 @@ struct KindTraits<KIND_I8> {
     static constexpr uint32_t c_fmt = 2, ab_fmt = 1;
 };
 
-template <int KIND, int BN, int STAGES>
+template <int KIND, int BN, int STAGES, int EPI_WARPS>
 struct Cfg {
     static constexpr int BM = 128;
     static constexpr int ELEM = KindTraits<KIND>::elem;
@@ -108,170 +103,186 @@ struct Cfg {
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+    static constexpr int EPI_BUF = 32 * 128;                // 32 rows x 128 bytes: one store box
+    static constexpr int STAGING = EPI_WARPS * 2 * EPI_BUF;  // double-buffered per epilogue warp
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + BAR_BYTES + 1024;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int SLICES = EPI_WARPS / 4;             // warps sharing one TMEM lane quarter
+    static constexpr int COLS_PER_WARP = BN / SLICES;
     static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
-    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+    static_assert(EPI_WARPS % 4 == 0 && COLS_PER_WARP % 32 == 0, "epilogue split");
+    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "BN");
     static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-// Epilogue for one 32-column chunk of one row held in registers.
+__device__ __forceinline__ float gelu_fast(float x) {
+    // arctic.zig:750-756 formula with the hardware tanh
+    const float inner = 0.7978845608f * (x + 0.044715f * x * x * x);
+    const float hx = 0.5f * x;
+    return fmaf(hx, tzp::tanh_approx(inner), hx);
+}
+
+// Epilogue math for one 32-column chunk of one row: v[] in, v[] out (fp32), amax updated with the
+// value as stored.
 template <int KIND>
-__device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, const uint32_t (&r)[32],
-                                               int row, int col0, int N, float rs, float& amax) {
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        if constexpr (KIND == KIND_I8)
-            v[j] = __int2float_rn(static_cast<int>(r[j]));
-        else
-            v[j] = __uint_as_float(r[j]);
-    }
+__device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32], int row, bool row_ok, int col0,
+                                              int N, float rs) {
     const bool full = (col0 + 32 <= N);
-    if (ep.out_type == OUT_I32) {
-        int* o = reinterpret_cast<int*>(ep.out) + static_cast<long long>(row) * ep.ldo + col0;
-        if (full && ep.vec_ok) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<int4*>(o + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
-                                                            static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
-        } else {
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < N) o[j] = static_cast<int>(r[j]);
-        }
-        return;
-    }
     if (ep.n_ops >= 0) {
         // Generic chain (codegen.zig:101-145): TZ_OP_ADD adds bias[col], others are unary.
+#pragma unroll
         for (int j = 0; j < 32; ++j) {
             const int col = col0 + j;
-            if (col >= N) break;
             float x = v[j];
-            for (int o = 0; o < ep.n_ops; ++o) {
-                const int op = ep.ops[o];
-                if (op == TZ_OP_ADD) {
-                    if (ep.bias) x = x + __ldg(ep.bias + col);
-                } else {
-                    x = apply_op(op, x);
+            if (col < N) {
+                for (int o = 0; o < ep.n_ops; ++o) {
+                    const int op = static_cast<int>((ep.ops >> (4 * o)) & 15u);
+                    if (op == TZ_OP_ADD) {
+                        if (ep.bias) x = x + __ldg(ep.bias + col);
+                    } else {
+                        x = apply_op(op, x);
+                    }
                 }
             }
             v[j] = x;
         }
+        return;
+    }
+    if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const int col = col0 + j;
+            if (ep.row_scale) {
+                const float4 cs = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col));
+                v[j] = __fmul_rn(v[j], __fmul_rn(rs, cs.x));
+                v[j + 1] = __fmul_rn(v[j + 1], __fmul_rn(rs, cs.y));
+                v[j + 2] = __fmul_rn(v[j + 2], __fmul_rn(rs, cs.z));
+                v[j + 3] = __fmul_rn(v[j + 3], __fmul_rn(rs, cs.w));
+            } else if (ep.col_scale) {
+                const float4 cs = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col));
+                v[j] = __fmul_rn(v[j], cs.x);
+                v[j + 1] = __fmul_rn(v[j + 1], cs.y);
+                v[j + 2] = __fmul_rn(v[j + 2], cs.z);
+                v[j + 3] = __fmul_rn(v[j + 3], cs.w);
+            }
+            if (ep.bias) {
+                const float4 b = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+                v[j] = __fadd_rn(v[j], b.x);
+                v[j + 1] = __fadd_rn(v[j + 1], b.y);
+                v[j + 2] = __fadd_rn(v[j + 2], b.z);
+                v[j + 3] = __fadd_rn(v[j + 3], b.w);
+            }
+        }
+        if (ep.gelu) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+        }
+        if (ep.residual && row_ok) {
+            const float* rp = ep.residual + static_cast<long long>(row) * ep.ldr + col0;
+            if (ep.vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 t = *reinterpret_cast<const float4*>(rp + j);
+                    v[j] = __fadd_rn(v[j], t.x);
+                    v[j + 1] = __fadd_rn(v[j + 1], t.y);
+                    v[j + 2] = __fadd_rn(v[j + 2], t.z);
+                    v[j + 3] = __fadd_rn(v[j + 3], t.w);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], rp[j]);
+            }
+        }
     } else {
-        if (full) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const int col = col0 + j;
-                if (ep.row_scale) {
-                    const float4 cs = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col));
-                    v[j] = __fmul_rn(v[j], __fmul_rn(rs, cs.x));
-                    v[j + 1] = __fmul_rn(v[j + 1], __fmul_rn(rs, cs.y));
-                    v[j + 2] = __fmul_rn(v[j + 2], __fmul_rn(rs, cs.z));
-                    v[j + 3] = __fmul_rn(v[j + 3], __fmul_rn(rs, cs.w));
-                } else if (ep.col_scale) {
-                    const float4 cs = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col));
-                    v[j] = __fmul_rn(v[j], cs.x);
-                    v[j + 1] = __fmul_rn(v[j + 1], cs.y);
-                    v[j + 2] = __fmul_rn(v[j + 2], cs.z);
-                    v[j + 3] = __fmul_rn(v[j + 3], cs.w);
-                }
-                if (ep.bias) {
-                    const float4 b = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
-                    v[j] = __fadd_rn(v[j], b.x);
-                    v[j + 1] = __fadd_rn(v[j + 1], b.y);
-                    v[j + 2] = __fadd_rn(v[j + 2], b.z);
-                    v[j + 3] = __fadd_rn(v[j + 3], b.w);
-                }
-            }
-            if (ep.gelu) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = gelu_model(v[j]);
-            }
-            if (ep.residual) {
-                const float* rp = ep.residual + static_cast<long long>(row) * ep.ldr + col0;
-                if (ep.vec_ok) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const float4 t = *reinterpret_cast<const float4*>(rp + j);
-                        v[j] = __fadd_rn(v[j], t.x);
-                        v[j + 1] = __fadd_rn(v[j + 1], t.y);
-                        v[j + 2] = __fadd_rn(v[j + 2], t.z);
-                        v[j + 3] = __fadd_rn(v[j + 3], t.w);
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], rp[j]);
-                }
-            }
-        } else {
-            for (int j = 0; j < 32; ++j) {
-                const int col = col0 + j;
-                if (col >= N) break;
-                float x = v[j];
+        for (int j = 0; j < 32; ++j) {
+            const int col = col0 + j;
+            float x = v[j];
+            if (col < N) {
                 if (ep.row_scale)
                     x = __fmul_rn(x, __fmul_rn(rs, ep.col_scale[col]));
                 else if (ep.col_scale)
                     x = __fmul_rn(x, ep.col_scale[col]);
                 if (ep.bias) x = __fadd_rn(x, ep.bias[col]);
-                if (ep.gelu) x = gelu_model(x);
-                if (ep.residual) x = __fadd_rn(x, ep.residual[static_cast<long long>(row) * ep.ldr + col]);
-                v[j] = x;
+                if (ep.gelu) x = gelu_fast(x);
+                if (ep.residual && row_ok) x = __fadd_rn(x, ep.residual[static_cast<long long>(row) * ep.ldr + col]);
             }
+            v[j] = x;
         }
     }
-    if (ep.out_type == OUT_F16) {
-        __half* o = reinterpret_cast<__half*>(ep.out) + static_cast<long long>(row) * ep.ldo + col0;
-        if (full && ep.vec_ok) {
+}
+
+// Direct (non-TMA) stores of one chunk: used when the output is not 16-byte aligned per row.
+__device__ __forceinline__ void store_direct(const EpiParams& ep, const float (&v)[32], const uint32_t (&r)[32], int row,
+                                             int col0, int N, float& amax) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-                uint4 pk;
-                pk.x = tzp::pack_half2(v[j], v[j + 1]);
-                pk.y = tzp::pack_half2(v[j + 2], v[j + 3]);
-                pk.z = tzp::pack_half2(v[j + 4], v[j + 5]);
-                pk.w = tzp::pack_half2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4*>(o + j) = pk;
-            }
-            if (ep.row_absmax) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(__half2float(__float2half_rn(v[j]))));
-            }
-        } else {
-            for (int j = 0; j < 32; ++j) {
-                if (col0 + j >= N) break;
+    for (int j = 0; j < 32; ++j) {
+        const int col = col0 + j;
+        if (col < N) {
+            const long long o = static_cast<long long>(row) * ep.ldo + col;
+            if (ep.out_type == OUT_I32) {
+                reinterpret_cast<int*>(ep.out)[o] = static_cast<int>(r[j]);
+            } else if (ep.out_type == OUT_F16) {
                 const __half h = __float2half_rn(v[j]);
-                o[j] = h;
+                reinterpret_cast<__half*>(ep.out)[o] = h;
                 amax = fmaxf(amax, fabsf(__half2float(h)));
-            }
-        }
-    } else {
-        float* o = reinterpret_cast<float*>(ep.out) + static_cast<long long>(row) * ep.ldo + col0;
-        if (full && ep.vec_ok) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            if (ep.row_absmax) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-            }
-        } else {
-            for (int j = 0; j < 32; ++j) {
-                if (col0 + j >= N) break;
-                o[j] = v[j];
+            } else {
+                reinterpret_cast<float*>(ep.out)[o] = v[j];
                 amax = fmaxf(amax, fabsf(v[j]));
             }
         }
     }
 }
 
-template <int KIND, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+// Swizzled staging of one 32x32 chunk for a TMA store (thread = row).  32-bit outputs: 128-byte rows,
+// SWIZZLE_128B (16-byte unit c of row r at c ^ (r & 7)); f16 outputs: 64-byte rows, SWIZZLE_64B
+// (unit c at c ^ ((r >> 1) & 3)).
+__device__ __forceinline__ void stage_chunk(const EpiParams& ep, uint32_t buf, int lane, const float (&v)[32],
+                                            const uint32_t (&r)[32], float& amax) {
+    if (ep.out_type == OUT_F16) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t a = buf + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4);
+            tzp::st_shared_v4(a, tzp::pack_half2(v[8 * c], v[8 * c + 1]), tzp::pack_half2(v[8 * c + 2], v[8 * c + 3]),
+                              tzp::pack_half2(v[8 * c + 4], v[8 * c + 5]), tzp::pack_half2(v[8 * c + 6], v[8 * c + 7]));
+        }
+        if (ep.row_absmax) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(__half2float(__float2half_rn(v[j]))));
+        }
+    } else if (ep.out_type == OUT_I32) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t a = buf + lane * 128 + ((c ^ (lane & 7)) << 4);
+            tzp::st_shared_v4(a, r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t a = buf + lane * 128 + ((c ^ (lane & 7)) << 4);
+            tzp::st_shared_v4(a, __float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]),
+                              __float_as_uint(v[4 * c + 3]));
+        }
+        if (ep.row_absmax) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        }
+    }
+}
+
+template <int KIND, int BN, int STAGES, int EPI_WARPS>
+__global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, EpiParams ep, int* status) {
-    using C = Cfg<KIND, BN, STAGES>;
+                   const __grid_constant__ CUtensorMap tmOut, int M, int N, int K, EpiParams ep, int use_tma_store,
+                   int* status) {
+    using C = Cfg<KIND, BN, STAGES, EPI_WARPS>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = tzp::smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+    uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -289,13 +300,14 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int a = 0; a < 2; ++a) {
             tzp::mbar_init(&tfull[a], 1);
-            tzp::mbar_init(&tempty[a], 4);
+            tzp::mbar_init(&tempty[a], EPI_WARPS);
         }
         tzp::mbar_init(drain, 1);
         *abort_flag = 0;
         tzp::fence_mbar_init();
         tzp::tma_prefetch_desc(&tmA);
         tzp::tma_prefetch_desc(&tmB);
+        if (use_tma_store) tzp::tma_prefetch_desc(&tmOut);
     }
     if (warp == 1) {
         tzp::tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -383,27 +395,54 @@ __global__ void __launch_bounds__(192, 1)
             tzp::mbar_wait(drain, 0, status, nullptr);
         }
     } else {
-        // ---- epilogue warps 2..5 ----
+        // ---- epilogue warps: warp e reads TMEM lane quarter (warp % 4), column slice e / 4 ----
+        const int e = warp - 2;
         const int q = warp & 3;
-        int acc = 0;
+        const int slice = e >> 2;
+        const uint32_t bufs = tzp::smem_u32(staging) + static_cast<uint32_t>(e * 2 * C::EPI_BUF);
+        int acc = 0, nbuf = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int m0 = (tile / n_tiles) * 128;
             const int n0 = (tile % n_tiles) * BN;
             if (!tzp::mbar_wait(&tfull[acc], acc_phase, status, abort_flag)) break;
             tzp::tc_fence_after();
-            const int row = m0 + q * 32 + lane;
+            const int row0 = m0 + q * 32;
+            const int row = row0 + lane;
             const bool row_ok = row < M;
             const float rs = (ep.row_scale && row_ok) ? ep.row_scale[row] : 1.0f;
             float amax = 0.0f;
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = slice * C::COLS_PER_WARP; c < (slice + 1) * C::COLS_PER_WARP; c += 32) {
                 uint32_t r[32];
-                tzp::tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN + c),
-                               r);
+                tzp::tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c), r);
                 tzp::tmem_ld_wait();
-                if (row_ok && n0 + c < N) epilogue_chunk<KIND>(ep, r, row, n0 + c, N, rs, amax);
+                const int col0 = n0 + c;
+                if (col0 >= N) continue;  // warp-uniform
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if constexpr (KIND == KIND_I8)
+                        v[j] = __int2float_rn(static_cast<int>(r[j]));
+                    else
+                        v[j] = __uint_as_float(r[j]);
+                }
+                if (ep.out_type != OUT_I32) epilogue_math<KIND>(ep, v, row, row_ok, col0, N, rs);
+                if (use_tma_store) {
+                    const uint32_t buf = bufs + static_cast<uint32_t>(nbuf * C::EPI_BUF);
+                    if (lane == 0) tzp::bulk_wait_read<1>();  // this buffer's previous store has read smem
+                    __syncwarp();
+                    stage_chunk(ep, buf, lane, v, r, amax);
+                    tzp::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tzp::tma_store_2d(&tmOut, staging + e * 2 * C::EPI_BUF + nbuf * C::EPI_BUF, col0, row0);
+                        tzp::bulk_commit();
+                    }
+                    nbuf ^= 1;
+                } else if (row_ok) {
+                    store_direct(ep, v, r, row, col0, N, amax);
+                }
             }
             tzp::tc_fence_before();
             __syncwarp();
@@ -414,6 +453,7 @@ __global__ void __launch_bounds__(192, 1)
                 acc_phase ^= 1u;
             }
         }
+        if (use_tma_store && lane == 0) tzp::bulk_wait_all();
     }
 
     tzp::tc_fence_before();
@@ -434,16 +474,18 @@ CUtensorMapDataType tmap_dtype(int kind) {
     }
 }
 
-template <int KIND, int BN, int STAGES>
+template <int KIND, int BN, int STAGES, int EPI_WARPS>
 int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
-    using C = Cfg<KIND, BN, STAGES>;
-    auto kern = gemm_tc_kernel<KIND, BN, STAGES>;
-    static bool attr_set = false;  // per instantiation; set once per process (single device use)
-    if (!attr_set) {
+    using C = Cfg<KIND, BN, STAGES, EPI_WARPS>;
+    auto kern = gemm_tc_kernel<KIND, BN, STAGES, EPI_WARPS>;
+    static unsigned attr_set = 0;  // one bit per device
+    int dev = 0;
+    TZ_CUDA(cudaGetDevice(&dev));
+    if (!(attr_set & (1u << (dev & 31)))) {
         TZ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_set = true;
+        attr_set |= 1u << (dev & 31);
     }
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, to;
     const uint64_t a_rows = g.a_rows_alloc > 0 ? static_cast<uint64_t>(g.a_rows_alloc) : static_cast<uint64_t>(g.M);
     int rc = encode_tmap_2d(&ta, tmap_dtype(KIND), C::ELEM, g.a, static_cast<uint64_t>(g.K), a_rows,
                             static_cast<uint64_t>(g.lda) * C::ELEM, C::BK, 128);
@@ -463,7 +505,8 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     ep.gelu = g.gelu;
     ep.row_absmax = g.row_absmax;
     ep.n_ops = g.n_ops;
-    for (int i = 0; i < 8; ++i) ep.ops[i] = g.ops[i];
+    ep.ops = 0;
+    for (int i = 0; i < 8; ++i) ep.ops |= (static_cast<uint32_t>(g.ops[i]) & 15u) << (4 * i);
     const int out_elem = g.out_type == OUT_F16 ? 2 : 4;
     const bool out_al = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldo * out_elem) % 16 == 0);
     const bool res_al = !g.residual || ((reinterpret_cast<uintptr_t>(g.residual) % 16 == 0) && ((g.ldr * 4) % 16 == 0));
@@ -471,11 +514,23 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
                         (!g.col_scale || reinterpret_cast<uintptr_t>(g.col_scale) % 16 == 0);
     TZ_CHECK(vec_al, TZ_EINVAL, "gemm: bias/scale vectors must be 16-byte aligned");
     ep.vec_ok = (out_al && res_al) ? 1 : 0;
+    int use_tma = (out_al && g.N % 32 == 0) ? 1 : 0;
+    if (use_tma) {
+        const CUtensorMapDataType odt = g.out_type == OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                        : g.out_type == OUT_I32 ? CU_TENSOR_MAP_DATA_TYPE_INT32
+                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        rc = encode_tmap_2d_swz(&to, odt, out_elem, g.out, static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.M),
+                                static_cast<uint64_t>(g.ldo) * out_elem, 32, 32,
+                                g.out_type == OUT_F16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    } else {
+        to = tb;  // unused
+    }
     const int n_tiles = (g.N + BN - 1) / BN;
     const int tiles = ((g.M + 127) / 128) * n_tiles;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
-    kern<<<grid, 192, C::SMEM, s>>>(ta, tb, g.M, g.N, g.K, ep, ctx->d_status);
+    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, to, g.M, g.N, g.K, ep, use_tma, ctx->d_status);
     TZ_CUDA(cudaGetLastError());
     return TZ_OK;
 }
@@ -493,10 +548,10 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
              TZ_EINVAL, "gemm: operands must be 16-byte aligned");
     TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm: row_scale needs col_scale");
     switch (g.kind) {
-        case KIND_F16: return launch_impl<KIND_F16, 128, 6>(ctx, g, s);
-        case KIND_BF16: return launch_impl<KIND_BF16, 128, 6>(ctx, g, s);
-        case KIND_TF32: return launch_impl<KIND_TF32, 128, 6>(ctx, g, s);
-        case KIND_I8: return launch_impl<KIND_I8, 128, 6>(ctx, g, s);
+        case KIND_F16: return launch_impl<KIND_F16, 128, 4, 8>(ctx, g, s);
+        case KIND_BF16: return launch_impl<KIND_BF16, 128, 4, 8>(ctx, g, s);
+        case KIND_TF32: return launch_impl<KIND_TF32, 128, 4, 8>(ctx, g, s);
+        case KIND_I8: return launch_impl<KIND_I8, 128, 4, 8>(ctx, g, s);
         default: return fail(TZ_EINVAL, "gemm: unknown kind %d", g.kind);
     }
 }

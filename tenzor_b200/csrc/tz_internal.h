@@ -58,6 +58,9 @@ int read_status(tz_ctx_t ctx, cudaStream_t s);
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                    uint32_t box_outer);
+int encode_tmap_2d_swz(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                       uint32_t box_outer, CUtensorMapSwizzle swz);
 
 // ---- kernel launchers (defined in the .cu files) ---------------------------------------------
 enum GemmKind { KIND_F16 = 0, KIND_BF16 = 1, KIND_TF32 = 2, KIND_I8 = 3 };

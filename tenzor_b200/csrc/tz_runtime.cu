@@ -80,17 +80,25 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                    uint32_t box_outer) {
+    return encode_tmap_2d_swz(map, dtype, elem_bytes, base, inner, outer, row_stride_bytes, box_inner, box_outer,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int encode_tmap_2d_swz(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                       uint32_t box_outer, CUtensorMapSwizzle swz) {
     auto enc = get_encode();
     TZ_CHECK(enc, TZ_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
     TZ_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, TZ_EINVAL, "TMA base must be 16-byte aligned");
     TZ_CHECK(row_stride_bytes % 16 == 0, TZ_EINVAL, "TMA row stride must be a multiple of 16 bytes");
-    TZ_CHECK(box_inner * static_cast<uint32_t>(elem_bytes) <= 128, TZ_EINVAL, "TMA box too wide for SWIZZLE_128B");
+    const uint32_t span = swz == CU_TENSOR_MAP_SWIZZLE_128B ? 128 : swz == CU_TENSOR_MAP_SWIZZLE_64B ? 64 : 32;
+    TZ_CHECK(box_inner * static_cast<uint32_t>(elem_bytes) <= span, TZ_EINVAL, "TMA box too wide for its swizzle");
     cuuint64_t dims[2] = {inner, outer < 1 ? 1 : outer};
     cuuint64_t strides[1] = {row_stride_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     TZ_CHECK(r == CUDA_SUCCESS, TZ_ECUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return TZ_OK;

@@ -2,6 +2,7 @@
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 from . import _lib as L
 
@@ -15,6 +16,10 @@ class Context:
         L.check(L.lib().tz_cuda_create(device, C.byref(h)))
         self.handle = h
         self.device = device
+        self._owned = weakref.WeakSet()  # models on this context: closed before the context
+
+    def _adopt(self, obj):
+        self._owned.add(obj)
 
     @property
     def sm_count(self) -> int:
@@ -29,6 +34,8 @@ class Context:
 
     def close(self):
         if self.handle:
+            for obj in list(self._owned):
+                obj.close()
             L.lib().tz_cuda_destroy(self.handle)
             self.handle = None
 

@@ -207,13 +207,17 @@ def test_safetensors_loader(ctx, weights, qweights, models, c1):
         p = os.path.join(d, "f32.safetensors")
         st.save(p, alt)
         m = ArcticModel.from_safetensors(ctx, p, "f32")
-        assert np.abs(m.forward_packed(packed, cu) - models["f32"].forward_packed(packed, cu)).max() == 0
-        m.close()
+        try:
+            assert np.abs(m.forward_packed(packed, cu) - models["f32"].forward_packed(packed, cu)).max() == 0
+        finally:
+            m.close()
         p8 = os.path.join(d, "i8.safetensors")
         st.save(p8, qweights)
         m8 = ArcticModel.from_safetensors(ctx, p8, "w8a8")
-        assert np.abs(m8.forward_packed(packed, cu) - models["w8a8"].forward_packed(packed, cu)).max() == 0
-        m8.close()
+        try:
+            assert np.abs(m8.forward_packed(packed, cu) - models["w8a8"].forward_packed(packed, cu)).max() == 0
+        finally:
+            m8.close()
 
 
 def test_gpu_quantizer_matches_oracle_checkpoint(ctx, weights, qweights):
