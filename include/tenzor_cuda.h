@@ -136,7 +136,7 @@ int tz_arctic_debug_operand(tz_model_t model, int which, int8_t* q_out, float* s
  * graph too).  tz_arctic_profile_read returns, summed over the kept forwards since enabling, the
  * milliseconds and the launch count per kernel class:
  * 0 embedding+LN, 1 QKV GEMM, 2 attention, 3 attention-output GEMM, 4 LayerNorm, 5 FFN1 GEMM,
- * 6 FFN1 requantisation (W8A8), 7 FFN2 GEMM, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
+ * 6 per-token requantisation (W8A8: attention output and FFN1 output), 7 FFN2 GEMM, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
 #define TZ_PROF_CLASSES 9
 int tz_arctic_profile(tz_model_t model, int enable);
 int tz_arctic_profile_read(tz_model_t model, float* ms, int* launches);

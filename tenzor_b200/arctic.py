@@ -182,9 +182,10 @@ class ArcticModel:
 
     def forward_device(self, d_ids, d_cu, batch: int, total_tokens: int, max_len: int, d_out,
                        stream=None):
-        """Device-pointer variant (integers or torch tensors' data_ptr()), async on `stream`."""
+        """Device-pointer variant (integers or torch tensors' data_ptr()), async on `stream` (a raw
+        cudaStream_t handle; None = the context's own stream; 0x1 = the legacy default stream)."""
         L.check(L.lib().tz_arctic_forward_device(self.handle, int(d_ids), int(d_cu), batch, total_tokens,
-                                                 max_len, int(d_out), stream))
+                                                 max_len, int(d_out), C.c_void_p(stream) if stream else None))
 
     # ---- parity hooks -----------------------------------------------------------------------
     def debug_hidden(self, stage: int, total_tokens: int) -> np.ndarray:

@@ -31,8 +31,8 @@
 #include "tz_rowops.cuh"
 
 namespace tz {
-int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int batch, int max_len, void* out_h,
-                     int8_t* out_q, float* out_s, cudaStream_t s);
+int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int batch, int max_len, void* out,
+                     unsigned* row_absmax, cudaStream_t s);
 int launch_f32_to_f16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s);
 int launch_i8_to_f16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s);
 int launch_f16bits_to_f32(tz_ctx_t ctx, const uint16_t* x, float* y, long long n, cudaStream_t s);
@@ -179,22 +179,21 @@ __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __r
     }
 }
 
-// W8A8: H f16 [T,1536] with its row max (float bits, from the FFN1 epilogue) -> int8 + scale;
-// resets the row max for the next layer.
-__global__ void quant_h_kernel(const __half* __restrict__ h, unsigned* __restrict__ hmax, int8_t* __restrict__ q,
-                               float* __restrict__ qs, long long rows) {
+// W8A8 per-token requantisation of an f16 activation X [rows, cols] whose row |max| (float bits) was
+// accumulated by its producer (GEMM epilogue or attention): s = max/127 (1 if 0),
+// q = clamp(round(x * (1/s))); the row max is reset to 0 for the next producer.  Warp per row.
+__global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsigned* __restrict__ xmax,
+                                    int8_t* __restrict__ q, float* __restrict__ qs, long long rows) {
     const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const float m = __uint_as_float(hmax[row]);
+    const float m = __uint_as_float(xmax[row]);
     const float sc = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
     const float inv = __fdiv_rn(1.0f, sc);
-    const __half* hr = h + row * kF;
-    int8_t* qr = q + row * kF;
-#pragma unroll
-    for (int c = 0; c < 6; ++c) {  // 1536 = 6 x 32 lanes x 8
-        const int col = c * 256 + lane * 8;
-        const uint4 raw = *reinterpret_cast<const uint4*>(hr + col);
+    const __half* xr = x + row * cols;
+    int8_t* qr = q + row * cols;
+    for (int col = lane * 8; col < cols; col += 256) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(xr + col);
         const __half* hv = reinterpret_cast<const __half*>(&raw);
         uint32_t w0 = 0, w1 = 0;
 #pragma unroll
@@ -207,7 +206,7 @@ __global__ void quant_h_kernel(const __half* __restrict__ h, unsigned* __restric
     __syncwarp();
     if (lane == 0) {
         qs[row] = sc;
-        hmax[row] = 0u;
+        xmax[row] = 0u;
     }
 }
 
@@ -281,6 +280,7 @@ struct tz_model_s {
     float *X = nullptr, *Y = nullptr, *xs = nullptr, *os = nullptr, *hs = nullptr, *out = nullptr;
     void *XA = nullptr, *QKV = nullptr, *OA = nullptr, *Hh = nullptr, *HQ = nullptr;
     unsigned* hmax = nullptr;
+    unsigned* omax = nullptr;
     uint32_t* h_ids = nullptr;  // pinned staging
     int* h_cu = nullptr;
     float* h_out = nullptr;
@@ -453,6 +453,7 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
         A(sizeof(float) * T, reinterpret_cast<void**>(&m->os));
         A(sizeof(float) * T, reinterpret_cast<void**>(&m->hs));
         A(sizeof(unsigned) * T, reinterpret_cast<void**>(&m->hmax));
+        A(sizeof(unsigned) * T, reinterpret_cast<void**>(&m->omax));
         A(sizeof(__half) * T * kF, &m->Hh);
         A(T * kF, &m->HQ);
     } else {
@@ -473,6 +474,7 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
         return rc;
     }
     if (m->hmax) TZ_CUDA(cudaMemset(m->hmax, 0, sizeof(unsigned) * T));
+    if (m->omax) TZ_CUDA(cudaMemset(m->omax, 0, sizeof(unsigned) * T));
     TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_ids), sizeof(uint32_t) * T, cudaHostAllocDefault));
     TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_cu), sizeof(int) * (nb + 1), cudaHostAllocDefault));
     TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_out), sizeof(float) * nb * kH, cudaHostAllocDefault));
@@ -532,9 +534,14 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if ((rc = launch_gemm(ctx, g, s))) return rc;
         if ((rc = prof_mark(m, P_ATTN, s))) return rc;
         // attention
-        if ((rc = launch_attention(ctx, m->QKV, d_cu, B, maxL, q8 ? nullptr : m->OA, q8 ? static_cast<int8_t*>(m->OA) : nullptr,
-                                   q8 ? m->os : nullptr, s)))
-            return rc;
+        // W8A8: the f16 attention output goes through the (still free) H buffer and is requantised
+        if ((rc = launch_attention(ctx, m->QKV, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s))) return rc;
+        if (q8) {
+            if ((rc = prof_mark(m, P_QUANT, s))) return rc;
+            requant_rows_kernel<<<rows_grid(T), 256, 0, s>>>(static_cast<__half*>(m->Hh), kH, m->omax,
+                                                             static_cast<int8_t*>(m->OA), m->os, T);
+            TZ_CUDA(cudaGetLastError());
+        }
         // output projection + bias + residual, then LayerNorm
         GemmArgs o;
         o.kind = g.kind;
@@ -561,7 +568,8 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if ((rc = launch_gemm(ctx, f1, s))) return rc;
         if (q8) {
             if ((rc = prof_mark(m, P_QUANT, s))) return rc;
-            quant_h_kernel<<<rows_grid(T), 256, 0, s>>>(static_cast<__half*>(m->Hh), m->hmax, static_cast<int8_t*>(m->HQ), m->hs, T);
+            requant_rows_kernel<<<rows_grid(T), 256, 0, s>>>(static_cast<__half*>(m->Hh), kF, m->hmax,
+                                                             static_cast<int8_t*>(m->HQ), m->hs, T);
             TZ_CUDA(cudaGetLastError());
         }
         // FFN2 + bias + residual, then LayerNorm

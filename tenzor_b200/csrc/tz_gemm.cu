@@ -94,6 +94,8 @@ struct KindTraits<KIND_I8> {
     static constexpr uint32_t c_fmt = 2, ab_fmt = 1;
 };
 
+constexpr int CW = 16;  // epilogue chunk width (columns per tcgen05.ld / per TMA store box)
+
 template <int KIND, int BN, int STAGES, int EPI_WARPS>
 struct Cfg {
     static constexpr int BM = 128;
@@ -103,7 +105,7 @@ struct Cfg {
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-    static constexpr int EPI_BUF = 32 * 128;                // 32 rows x 128 bytes: one store box
+    static constexpr int EPI_BUF = 32 * CW * 4;              // 32 rows x 16 columns x 4 bytes: one store box
     static constexpr int STAGING = EPI_WARPS * 2 * EPI_BUF;  // double-buffered per epilogue warp
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + BAR_BYTES + 1024;
@@ -111,7 +113,7 @@ struct Cfg {
     static constexpr int SLICES = EPI_WARPS / 4;             // warps sharing one TMEM lane quarter
     static constexpr int COLS_PER_WARP = BN / SLICES;
     static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
-    static_assert(EPI_WARPS % 4 == 0 && COLS_PER_WARP % 32 == 0, "epilogue split");
+    static_assert(EPI_WARPS % 4 == 0 && COLS_PER_WARP % CW == 0, "epilogue split");
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "BN");
     static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
     static_assert(SMEM <= 227 * 1024, "shared memory");
@@ -124,16 +126,15 @@ __device__ __forceinline__ float gelu_fast(float x) {
     return fmaf(hx, tzp::tanh_approx(inner), hx);
 }
 
-// Epilogue math for one 32-column chunk of one row: v[] in, v[] out (fp32), amax updated with the
-// value as stored.
+// Epilogue math for one CW-column chunk of one row (v[] in and out, fp32).
 template <int KIND>
-__device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32], int row, bool row_ok, int col0,
+__device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[CW], int row, bool row_ok, int col0,
                                               int N, float rs) {
-    const bool full = (col0 + 32 <= N);
+    const bool full = (col0 + CW <= N);
     if (ep.n_ops >= 0) {
         // Generic chain (codegen.zig:101-145): TZ_OP_ADD adds bias[col], others are unary.
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < CW; ++j) {
             const int col = col0 + j;
             float x = v[j];
             if (col < N) {
@@ -151,8 +152,19 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32
         return;
     }
     if (full) {
+        float4 res[CW / 4];
+        if (ep.residual && row_ok) {  // issue the residual loads first: their latency overlaps the math
+            const float* rp = ep.residual + static_cast<long long>(row) * ep.ldr + col0;
+            if (ep.vec_ok) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
+                for (int j = 0; j < CW / 4; ++j) res[j] = *reinterpret_cast<const float4*>(rp + 4 * j);
+            } else {
+#pragma unroll
+                for (int j = 0; j < CW / 4; ++j) res[j] = make_float4(rp[4 * j], rp[4 * j + 1], rp[4 * j + 2], rp[4 * j + 3]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < CW; j += 4) {
             const int col = col0 + j;
             if (ep.row_scale) {
                 const float4 cs = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col));
@@ -177,27 +189,20 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32
         }
         if (ep.gelu) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+            for (int j = 0; j < CW; ++j) v[j] = gelu_fast(v[j]);
         }
         if (ep.residual && row_ok) {
-            const float* rp = ep.residual + static_cast<long long>(row) * ep.ldr + col0;
-            if (ep.vec_ok) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    const float4 t = *reinterpret_cast<const float4*>(rp + j);
-                    v[j] = __fadd_rn(v[j], t.x);
-                    v[j + 1] = __fadd_rn(v[j + 1], t.y);
-                    v[j + 2] = __fadd_rn(v[j + 2], t.z);
-                    v[j + 3] = __fadd_rn(v[j + 3], t.w);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], rp[j]);
+            for (int j = 0; j < CW / 4; ++j) {
+                v[4 * j] = __fadd_rn(v[4 * j], res[j].x);
+                v[4 * j + 1] = __fadd_rn(v[4 * j + 1], res[j].y);
+                v[4 * j + 2] = __fadd_rn(v[4 * j + 2], res[j].z);
+                v[4 * j + 3] = __fadd_rn(v[4 * j + 3], res[j].w);
             }
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < CW; ++j) {
             const int col = col0 + j;
             float x = v[j];
             if (col < N) {
@@ -215,10 +220,10 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32
 }
 
 // Direct (non-TMA) stores of one chunk: used when the output is not 16-byte aligned per row.
-__device__ __forceinline__ void store_direct(const EpiParams& ep, const float (&v)[32], const uint32_t (&r)[32], int row,
+__device__ __forceinline__ void store_direct(const EpiParams& ep, const float (&v)[CW], const uint32_t (&r)[CW], int row,
                                              int col0, int N, float& amax) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < CW; ++j) {
         const int col = col0 + j;
         if (col < N) {
             const long long o = static_cast<long long>(row) * ep.ldo + col;
@@ -236,38 +241,38 @@ __device__ __forceinline__ void store_direct(const EpiParams& ep, const float (&
     }
 }
 
-// Swizzled staging of one 32x32 chunk for a TMA store (thread = row).  32-bit outputs: 128-byte rows,
-// SWIZZLE_128B (16-byte unit c of row r at c ^ (r & 7)); f16 outputs: 64-byte rows, SWIZZLE_64B
-// (unit c at c ^ ((r >> 1) & 3)).
-__device__ __forceinline__ void stage_chunk(const EpiParams& ep, uint32_t buf, int lane, const float (&v)[32],
-                                            const uint32_t (&r)[32], float& amax) {
+// Swizzled staging of one 32 x 16 chunk for a TMA store (thread = row).  32-bit outputs: 64-byte
+// rows, SWIZZLE_64B (16-byte unit c of row r at c ^ ((r >> 1) & 3)); f16 outputs: 32-byte rows,
+// SWIZZLE_32B (unit c at c ^ ((r >> 2) & 1)).
+__device__ __forceinline__ void stage_chunk(const EpiParams& ep, uint32_t buf, int lane, const float (&v)[CW],
+                                            const uint32_t (&r)[CW], float& amax) {
     if (ep.out_type == OUT_F16) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint32_t a = buf + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4);
+        for (int c = 0; c < 2; ++c) {
+            const uint32_t a = buf + lane * 32 + ((c ^ ((lane >> 2) & 1)) << 4);
             tzp::st_shared_v4(a, tzp::pack_half2(v[8 * c], v[8 * c + 1]), tzp::pack_half2(v[8 * c + 2], v[8 * c + 3]),
                               tzp::pack_half2(v[8 * c + 4], v[8 * c + 5]), tzp::pack_half2(v[8 * c + 6], v[8 * c + 7]));
         }
         if (ep.row_absmax) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(__half2float(__float2half_rn(v[j]))));
+            for (int j = 0; j < CW; ++j) amax = fmaxf(amax, fabsf(__half2float(__float2half_rn(v[j]))));
         }
     } else if (ep.out_type == OUT_I32) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint32_t a = buf + lane * 128 + ((c ^ (lane & 7)) << 4);
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t a = buf + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4);
             tzp::st_shared_v4(a, r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
         }
     } else {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint32_t a = buf + lane * 128 + ((c ^ (lane & 7)) << 4);
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t a = buf + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4);
             tzp::st_shared_v4(a, __float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]),
                               __float_as_uint(v[4 * c + 3]));
         }
         if (ep.row_absmax) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+            for (int j = 0; j < CW; ++j) amax = fmaxf(amax, fabsf(v[j]));
         }
     }
 }
@@ -413,15 +418,15 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             const float rs = (ep.row_scale && row_ok) ? ep.row_scale[row] : 1.0f;
             float amax = 0.0f;
 #pragma unroll 1
-            for (int c = slice * C::COLS_PER_WARP; c < (slice + 1) * C::COLS_PER_WARP; c += 32) {
-                uint32_t r[32];
-                tzp::tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c), r);
+            for (int c = slice * C::COLS_PER_WARP; c < (slice + 1) * C::COLS_PER_WARP; c += CW) {
+                uint32_t r[CW];
+                tzp::tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c), r);
                 tzp::tmem_ld_wait();
                 const int col0 = n0 + c;
                 if (col0 >= N) continue;  // warp-uniform
-                float v[32];
+                float v[CW];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
+                for (int j = 0; j < CW; ++j) {
                     if constexpr (KIND == KIND_I8)
                         v[j] = __int2float_rn(static_cast<int>(r[j]));
                     else
@@ -514,14 +519,14 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
                         (!g.col_scale || reinterpret_cast<uintptr_t>(g.col_scale) % 16 == 0);
     TZ_CHECK(vec_al, TZ_EINVAL, "gemm: bias/scale vectors must be 16-byte aligned");
     ep.vec_ok = (out_al && res_al) ? 1 : 0;
-    int use_tma = (out_al && g.N % 32 == 0) ? 1 : 0;
+    int use_tma = (out_al && g.N % CW == 0) ? 1 : 0;
     if (use_tma) {
         const CUtensorMapDataType odt = g.out_type == OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                         : g.out_type == OUT_I32 ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
         rc = encode_tmap_2d_swz(&to, odt, out_elem, g.out, static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.M),
-                                static_cast<uint64_t>(g.ldo) * out_elem, 32, 32,
-                                g.out_type == OUT_F16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+                                static_cast<uint64_t>(g.ldo) * out_elem, CW, 32,
+                                g.out_type == OUT_F16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
         if (rc) return rc;
     } else {
         to = tb;  // unused
@@ -548,10 +553,12 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
              TZ_EINVAL, "gemm: operands must be 16-byte aligned");
     TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm: row_scale needs col_scale");
     switch (g.kind) {
-        case KIND_F16: return launch_impl<KIND_F16, 128, 4, 8>(ctx, g, s);
-        case KIND_BF16: return launch_impl<KIND_BF16, 128, 4, 8>(ctx, g, s);
-        case KIND_TF32: return launch_impl<KIND_TF32, 128, 4, 8>(ctx, g, s);
-        case KIND_I8: return launch_impl<KIND_I8, 128, 4, 8>(ctx, g, s);
+        // BN = 192 when it divides N (every Arctic projection: 384, 1152, 1536): 25% more output per
+        // byte of A staged than BN = 128, and no partial tiles.
+        case KIND_F16: return g.N % 192 == 0 ? launch_impl<KIND_F16, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_F16, 128, 4, 16>(ctx, g, s);
+        case KIND_BF16: return launch_impl<KIND_BF16, 128, 4, 16>(ctx, g, s);
+        case KIND_TF32: return g.N % 192 == 0 ? launch_impl<KIND_TF32, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_TF32, 128, 4, 16>(ctx, g, s);
+        case KIND_I8: return g.N % 192 == 0 ? launch_impl<KIND_I8, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_I8, 128, 4, 16>(ctx, g, s);
         default: return fail(TZ_EINVAL, "gemm: unknown kind %d", g.kind);
     }
 }

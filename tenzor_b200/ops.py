@@ -23,8 +23,14 @@ def _p(t):
     return None if t is None else t.data_ptr()
 
 
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the handle torch's default stream (0) stands for
+
+
 def _stream(s=None):
-    return C.c_void_p(torch.cuda.current_stream().cuda_stream if s is None else s)
+    """The stream to launch on: torch's current stream.  Its default stream has handle 0, which the C
+    ABI reads as 'the context's own stream', so it is passed as cudaStreamLegacy instead."""
+    h = torch.cuda.current_stream().cuda_stream if s is None else s
+    return C.c_void_p(h if h else CUDA_STREAM_LEGACY)
 
 
 def _dev(t, dtype):

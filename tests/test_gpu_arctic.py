@@ -226,3 +226,21 @@ def test_gpu_quantizer_matches_oracle_checkpoint(ctx, weights, qweights):
     assert set(g) == set(qweights)
     for k in g:
         assert g[k].dtype == qweights[k].dtype and (g[k] == qweights[k]).all(), k
+
+
+def test_device_forward_on_user_stream(models, c1):
+    """tz_arctic_forward_device on a caller's stream gives the host-API result bit for bit."""
+    import torch
+    ids, lens, packed, cu = c1
+    m = models["w8a8"]
+    ref = m.forward_packed(packed, cu)
+    s = torch.cuda.Stream()
+    d_ids = torch.from_numpy(packed.view(np.int32)).cuda()
+    d_cu = torch.from_numpy(cu).cuda()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        out = torch.empty((len(lens), 384), device="cuda")
+        m.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), len(lens), int(cu[-1]), int(lens.max()), out.data_ptr(),
+                         s.cuda_stream)
+    s.synchronize()
+    assert (out.cpu().numpy() == ref).all()
