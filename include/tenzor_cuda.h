@@ -116,7 +116,9 @@ int tz_arctic_forward(tz_model_t model, const uint32_t* ids_packed, const int32_
 int tz_arctic_forward_padded(tz_model_t model, const uint32_t* ids, const int32_t* lengths,
                              int batch, int seq, float* out);
 /* Device-resident variant: all pointers on the device, asynchronous on `stream`.  total_tokens =
- * cu_seqlens[B] and max_len = max length must be passed by the caller (no host read-back). */
+ * cu_seqlens[B] and max_len = max length must be passed by the caller (no host read-back).  The
+ * launch sequence is captured into a CUDA graph on first use and replayed while the buffers, the
+ * shape and the stream repeat (the legacy default stream is never captured). */
 int tz_arctic_forward_device(tz_model_t model, const uint32_t* d_ids_packed,
                              const int32_t* d_cu_seqlens, int batch, int64_t total_tokens,
                              int max_len, float* d_out, tz_stream_t stream);
@@ -135,8 +137,9 @@ int tz_arctic_debug_operand(tz_model_t model, int which, int8_t* q_out, float* s
  * events are recorded on the launching stream between consecutive launches (inside a captured
  * graph too).  tz_arctic_profile_read returns, summed over the kept forwards since enabling, the
  * milliseconds and the launch count per kernel class:
- * 0 embedding+LN, 1 QKV GEMM, 2 attention, 3 attention-output GEMM, 4 LayerNorm, 5 FFN1 GEMM,
- * 6 per-token requantisation (W8A8: attention output and FFN1 output), 7 FFN2 GEMM, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
+ * 0 embedding+LN, 1 QKV GEMM, 2 attention, 3 attention-output GEMM + residual + LayerNorm,
+ * 4 (unused: LayerNorm is fused into 3 and 7), 5 FFN1 GEMM,
+ * 6 per-token requantisation (W8A8: attention output and FFN1 output), 7 FFN2 GEMM + residual + LayerNorm, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
 #define TZ_PROF_CLASSES 9
 int tz_arctic_profile(tz_model_t model, int enable);
 int tz_arctic_profile_read(tz_model_t model, float* ms, int* launches);

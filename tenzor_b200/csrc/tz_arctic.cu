@@ -1,6 +1,8 @@
-// tz_arctic.cu -- Arctic-embed-xs forward on sm_100a: model kernels (embedding + LayerNorm,
-// LayerNorm with the next GEMM's operand fused, per-token requantisation of the FFN intermediate,
-// CLS pooling + L2 norm) and the host orchestration behind tz_arctic_*.
+// tz_arctic.cu -- Arctic-embed-xs forward on sm_100a: model kernels (embedding + LayerNorm, per-token
+// requantisation of f16 activations for the W8A8 path, CLS pooling + L2 norm) and the host
+// orchestration behind tz_arctic_*.  Per layer: QKV GEMM (tz_gemm.cu) -> attention
+// (tz_attention.cu) -> [requant] -> output projection + residual + LayerNorm (tz_gemm_ln.cu) ->
+// FFN1 + GELU (tz_gemm.cu) -> [requant] -> FFN2 + residual + LayerNorm (tz_gemm_ln.cu).
 //
 // Reference call stack replaced (arctic.zig): forward 874-898 -> embeddingsImpl 543-585 ->
 // encoder 830-848 -> transformerBlock 814-826 -> selfAttention 639-747 / feedForward 760-810 ->
@@ -11,7 +13,6 @@
 //   XA   f16 [T,384]   GEMM operand copy of X (F32 / W8A32)   | int8 [T,384] + xs f32 [T] (W8A8)
 //   QKV  f16 [T,1152]  Q | K | V, head h at columns h*32 of each third
 //   OA   f16 [T,384]   attention output (F32 / W8A32)        | int8 + os [T] (W8A8)
-//   Y    f32 [T,384]   GEMM + bias + residual, LayerNorm input
 //   H    f16 [T,1536]  GELU(FFN1)                              (+ int8 HQ + hs [T] for W8A8)
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -32,7 +33,7 @@
 
 namespace tz {
 int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int batch, int max_len, void* out,
-                     unsigned* row_absmax, cudaStream_t s);
+                     unsigned* row_absmax, cudaStream_t s, bool pdl);
 int launch_f32_to_f16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s);
 int launch_i8_to_f16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s);
 int launch_f16bits_to_f32(tz_ctx_t ctx, const uint16_t* x, float* y, long long n, cudaStream_t s);
@@ -97,25 +98,6 @@ __device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __res
     }
 }
 
-// LayerNorm of Y (GEMM output incl. bias + residual) -> X and the next GEMM's operand.
-template <int AUX>
-__global__ void ln_model_kernel(const float* __restrict__ y, const float* __restrict__ g, const float* __restrict__ b,
-                                float* __restrict__ xo, void* aux, float* aux_s, long long rows) {
-    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    float v[12];
-#pragma unroll
-    for (int c = 0; c < 3; ++c) {
-        const float4 t = *reinterpret_cast<const float4*>(y + row * kH + c * 128 + lane * 4);
-        v[4 * c] = t.x;
-        v[4 * c + 1] = t.y;
-        v[4 * c + 2] = t.z;
-        v[4 * c + 3] = t.w;
-    }
-    ln_finish_row<AUX>(v, g, b, xo, aux, aux_s, row, lane);
-}
-
 struct EmbTables {
     const float* word_f;
     const int8_t* word_q;
@@ -160,6 +142,8 @@ template <int AUX>
 __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, EmbTables t,
                                 const float* __restrict__ g, const float* __restrict__ b, float* __restrict__ xo,
                                 void* aux, float* aux_s, int* status) {
+    tzp::pdl_wait();
+    tzp::pdl_trigger();
     const int seq = blockIdx.x;
     const int s0 = cu[seq], L = cu[seq + 1] - s0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -184,6 +168,8 @@ __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __r
 // q = clamp(round(x * (1/s))); the row max is reset to 0 for the next producer.  Warp per row.
 __global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsigned* __restrict__ xmax,
                                     int8_t* __restrict__ q, float* __restrict__ qs, long long rows) {
+    tzp::pdl_wait();
+    tzp::pdl_trigger();
     const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -213,6 +199,8 @@ __global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsi
 // CLS pooling + l2Normalize (arctic.zig:851-863, forward 894-897): warp per sequence.
 __global__ void pool_l2_kernel(const float* __restrict__ x, const int* __restrict__ cu, float* __restrict__ out,
                                int batch) {
+    tzp::pdl_wait();
+    tzp::pdl_trigger();
     const int seq = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (seq >= batch) return;
@@ -277,7 +265,7 @@ struct tz_model_s {
     std::vector<void*> ws;
     uint32_t* d_ids = nullptr;
     int* d_cu = nullptr;
-    float *X = nullptr, *Y = nullptr, *xs = nullptr, *os = nullptr, *hs = nullptr, *out = nullptr;
+    float *X = nullptr, *xs = nullptr, *os = nullptr, *hs = nullptr, *out = nullptr;
     void *XA = nullptr, *QKV = nullptr, *OA = nullptr, *Hh = nullptr, *HQ = nullptr;
     unsigned* hmax = nullptr;
     unsigned* omax = nullptr;
@@ -307,6 +295,10 @@ struct tz_model_s {
     int g_batch = -1, g_maxlen = -1;
     int64_t g_tokens = -1;
     bool use_graph = true;
+    // graph cache for the device-pointer forward (keyed by buffers, shape and stream)
+    cudaGraphExec_t dgraph = nullptr;
+    const void* dkey[4] = {nullptr, nullptr, nullptr, nullptr};
+    int64_t dkey_shape[3] = {-1, -1, -1};
 };
 
 namespace {
@@ -406,11 +398,20 @@ int upload_table(tz_model_s* m, const tz_mat_weight& w, int rows, const float** 
     return rc;
 }
 
-void free_workspace(tz_model_s* m) {
+void drop_graphs(tz_model_s* m) {
     if (m->graph) {
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
     }
+    if (m->dgraph) {
+        cudaGraphExecDestroy(m->dgraph);
+        m->dgraph = nullptr;
+    }
+    m->dkey[0] = m->dkey[1] = m->dkey[2] = m->dkey[3] = nullptr;
+}
+
+void free_workspace(tz_model_s* m) {
+    drop_graphs(m);
     for (void* p : m->ws) cudaFree(p);
     m->ws.clear();
     if (m->h_ids) cudaFreeHost(m->h_ids);
@@ -443,7 +444,6 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
     A(sizeof(uint32_t) * T, reinterpret_cast<void**>(&m->d_ids));
     A(sizeof(int) * (nb + 1), reinterpret_cast<void**>(&m->d_cu));
     A(sizeof(float) * T * kH, reinterpret_cast<void**>(&m->X));
-    A(sizeof(float) * T * kH, reinterpret_cast<void**>(&m->Y));
     A(sizeof(__half) * T * 3 * kH, &m->QKV);
     A(sizeof(float) * nb * kH, reinterpret_cast<void**>(&m->out));
     if (m->mode == TZ_QUANT_W8A8) {
@@ -489,7 +489,12 @@ enum ProfClass { P_EMBED = 0, P_QKV, P_ATTN, P_OPROJ, P_LN, P_FFN1, P_QUANT, P_F
 int prof_mark(tz_model_s* m, int next_class, cudaStream_t s) {
     if (!m->profile) return TZ_OK;
     if (m->ev_n >= 65) return TZ_OK;
-    TZ_CUDA(cudaEventRecord(m->ev[m->ev_base + m->ev_n], s));
+    // Inside a stream capture the record must become an external event node so that every graph
+    // replay records it (a plain record only orders the captured work).
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    TZ_CUDA(cudaStreamIsCapturing(s, &cs));
+    TZ_CUDA(cudaEventRecordWithFlags(m->ev[m->ev_base + m->ev_n], s,
+                                     cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault));
     if (next_class >= 0 && m->ev_n < 64) m->ev_cls[m->ev_n] = next_class;
     ++m->ev_n;
     return TZ_OK;
@@ -515,15 +520,19 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
     m->ev_n = 0;
     if (m->profile) m->ev_base = static_cast<int>(m->prof_fwd % m->prof_slots) * 65;
     if ((rc = prof_mark(m, P_EMBED, s))) return rc;
+    const bool pdl = !m->profile;  // events between launches would break the programmatic edges anyway
     if (q8)
-        embed_ln_kernel<1><<<B, 256, 0, s>>>(d_ids, d_cu, m->emb, m->emb_g, m->emb_b, m->X, m->XA, m->xs, ctx->d_status);
+        rc = launch_kernel(embed_ln_kernel<1>, dim3(B), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
+                           (const float*)m->emb_b, m->X, m->XA, m->xs, ctx->d_status);
     else
-        embed_ln_kernel<0><<<B, 256, 0, s>>>(d_ids, d_cu, m->emb, m->emb_g, m->emb_b, m->X, m->XA, nullptr, ctx->d_status);
-    TZ_CUDA(cudaGetLastError());
+        rc = launch_kernel(embed_ln_kernel<0>, dim3(B), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
+                           (const float*)m->emb_b, m->X, m->XA, (float*)nullptr, ctx->d_status);
+    if (rc) return rc;
     if (m->keep_stages) TZ_CUDA(cudaMemcpyAsync(m->d_stages, m->X, sizeof(float) * T * kH, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < kLayers; ++l) {
         const DevLayer& L = m->layers[l];
         GemmArgs g;
+        g.pdl = pdl;
         g.kind = q8 ? KIND_I8 : KIND_F16;
         // QKV projection (3 linearProjection calls of selfAttention fused into one N=1152 GEMM)
         g.a = m->XA; g.lda = kH; g.b = L.wqkv; g.ldb = kH; g.M = M; g.N = 3 * kH; g.K = kH;
@@ -535,30 +544,28 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if ((rc = prof_mark(m, P_ATTN, s))) return rc;
         // attention
         // W8A8: the f16 attention output goes through the (still free) H buffer and is requantised
-        if ((rc = launch_attention(ctx, m->QKV, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s))) return rc;
+        if ((rc = launch_attention(ctx, m->QKV, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s, pdl)))
+            return rc;
         if (q8) {
             if ((rc = prof_mark(m, P_QUANT, s))) return rc;
-            requant_rows_kernel<<<rows_grid(T), 256, 0, s>>>(static_cast<__half*>(m->Hh), kH, m->omax,
-                                                             static_cast<int8_t*>(m->OA), m->os, T);
-            TZ_CUDA(cudaGetLastError());
+            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, pdl,
+                                    static_cast<const __half*>(m->Hh), kH, m->omax, static_cast<int8_t*>(m->OA), m->os, T)))
+                return rc;
         }
-        // output projection + bias + residual, then LayerNorm
-        GemmArgs o;
+        // output projection + bias + residual + LayerNorm in one kernel (arctic.zig:716-746)
+        GemmLnArgs o;
+        o.pdl = pdl;
         o.kind = g.kind;
-        o.a = m->OA; o.lda = kH; o.b = L.wo; o.ldb = kH; o.M = M; o.N = kH; o.K = kH;
+        o.a = m->OA; o.lda = kH; o.b = L.wo; o.ldb = kH; o.M = M; o.K = kH;
         o.bias = L.bo; o.col_scale = wscale ? L.so : nullptr; o.row_scale = q8 ? m->os : nullptr;
-        o.residual = m->X; o.ldr = kH; o.out = m->Y; o.ldo = kH; o.out_type = OUT_F32;
+        o.residual = m->X; o.gamma = L.ln1g; o.beta = L.ln1b; o.eps = kEps;
+        o.x_out = m->X; o.aux = m->XA; o.aux_scale = q8 ? m->xs : nullptr; o.aux_int8 = q8;
         if (l == 0 && (rc = keep_operand(m, 1, m->OA, m->os, T, kH, s))) return rc;
         if ((rc = prof_mark(m, P_OPROJ, s))) return rc;
-        if ((rc = launch_gemm(ctx, o, s))) return rc;
-        if ((rc = prof_mark(m, P_LN, s))) return rc;
-        if (q8)
-            ln_model_kernel<1><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln1g, L.ln1b, m->X, m->XA, m->xs, T);
-        else
-            ln_model_kernel<0><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln1g, L.ln1b, m->X, m->XA, nullptr, T);
-        TZ_CUDA(cudaGetLastError());
+        if ((rc = launch_gemm_ln(ctx, o, s))) return rc;
         // FFN1 + bias + GELU
         GemmArgs f1;
+        f1.pdl = pdl;
         f1.kind = g.kind;
         f1.a = m->XA; f1.lda = kH; f1.b = L.w1; f1.ldb = kH; f1.M = M; f1.N = kF; f1.K = kH;
         f1.bias = L.b1; f1.col_scale = wscale ? L.s1 : nullptr; f1.row_scale = q8 ? m->xs : nullptr;
@@ -568,32 +575,29 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if ((rc = launch_gemm(ctx, f1, s))) return rc;
         if (q8) {
             if ((rc = prof_mark(m, P_QUANT, s))) return rc;
-            requant_rows_kernel<<<rows_grid(T), 256, 0, s>>>(static_cast<__half*>(m->Hh), kF, m->hmax,
-                                                             static_cast<int8_t*>(m->HQ), m->hs, T);
-            TZ_CUDA(cudaGetLastError());
+            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, pdl,
+                                    static_cast<const __half*>(m->Hh), kF, m->hmax, static_cast<int8_t*>(m->HQ), m->hs, T)))
+                return rc;
         }
-        // FFN2 + bias + residual, then LayerNorm
-        GemmArgs f2;
+        // FFN2 + bias + residual + LayerNorm in one kernel (arctic.zig:779-807)
+        GemmLnArgs f2;
+        f2.pdl = pdl;
         f2.kind = g.kind;
-        f2.a = q8 ? m->HQ : m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.N = kH; f2.K = kF;
+        f2.a = q8 ? m->HQ : m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.K = kF;
         f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.row_scale = q8 ? m->hs : nullptr;
-        f2.residual = m->X; f2.ldr = kH; f2.out = m->Y; f2.ldo = kH; f2.out_type = OUT_F32;
+        f2.residual = m->X; f2.gamma = L.ln2g; f2.beta = L.ln2b; f2.eps = kEps;
+        f2.x_out = m->X; f2.aux = m->XA; f2.aux_scale = q8 ? m->xs : nullptr; f2.aux_int8 = q8;
         if (l == 0 && q8 && (rc = keep_operand(m, 3, m->HQ, m->hs, T, kF, s))) return rc;
         if ((rc = prof_mark(m, P_FFN2, s))) return rc;
-        if ((rc = launch_gemm(ctx, f2, s))) return rc;
-        if ((rc = prof_mark(m, P_LN, s))) return rc;
-        if (q8)
-            ln_model_kernel<1><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln2g, L.ln2b, m->X, m->XA, m->xs, T);
-        else
-            ln_model_kernel<0><<<rows_grid(T), 256, 0, s>>>(m->Y, L.ln2g, L.ln2b, m->X, m->XA, nullptr, T);
-        TZ_CUDA(cudaGetLastError());
+        if ((rc = launch_gemm_ln(ctx, f2, s))) return rc;
         if (m->keep_stages)
             TZ_CUDA(cudaMemcpyAsync(m->d_stages + static_cast<size_t>(l + 1) * m->cap_tokens * kH, m->X, sizeof(float) * T * kH,
                                     cudaMemcpyDeviceToDevice, s));
     }
     if ((rc = prof_mark(m, P_POOL, s))) return rc;
-    pool_l2_kernel<<<(B * 32 + 255) / 256, 256, 0, s>>>(m->X, d_cu, d_out, B);
-    TZ_CUDA(cudaGetLastError());
+    if ((rc = launch_kernel(pool_l2_kernel, dim3((B * 32 + 255) / 256), dim3(256), 0, s, pdl, (const float*)m->X, d_cu,
+                            d_out, B)))
+        return rc;
     if ((rc = prof_mark(m, -1, s))) return rc;
     if (m->profile) ++m->prof_fwd;
     return TZ_OK;
@@ -792,9 +796,41 @@ int tz_arctic_forward_device(tz_model_t m, const uint32_t* d_ids, const int32_t*
     int rc = reserve(m, batch, T);
     if (rc) return rc;
     TZ_CUDA(cudaSetDevice(m->ctx->device));
-    rc = enqueue_forward(m, d_ids, d_cu, batch, T, max_len, d_out, pick_stream(m->ctx, stream));
+    cudaStream_t s = pick_stream(m->ctx, stream);
     m->last_T = T;
-    return rc;
+    // The legacy / per-thread default streams cannot be captured: launch directly there.
+    const bool capturable = m->use_graph && !m->keep_stages && s != cudaStreamLegacy && s != cudaStreamPerThread;
+    if (!capturable) return enqueue_forward(m, d_ids, d_cu, batch, T, max_len, d_out, s);
+    const bool hit = m->dgraph && m->dkey[0] == d_ids && m->dkey[1] == d_cu && m->dkey[2] == d_out &&
+                     m->dkey[3] == static_cast<const void*>(s) && m->dkey_shape[0] == batch && m->dkey_shape[1] == T &&
+                     m->dkey_shape[2] == max_len;
+    if (!hit) {
+        if (m->dgraph) {
+            cudaGraphExecDestroy(m->dgraph);
+            m->dgraph = nullptr;
+        }
+        cudaGraph_t gr = nullptr;
+        TZ_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        const int crc = enqueue_forward(m, d_ids, d_cu, batch, T, max_len, d_out, s);
+        const cudaError_t ee = cudaStreamEndCapture(s, &gr);
+        if (crc) {
+            if (gr) cudaGraphDestroy(gr);
+            return crc;
+        }
+        if (ee != cudaSuccess) return cuda_fail(ee, "cudaStreamEndCapture");
+        const cudaError_t ie = cudaGraphInstantiate(&m->dgraph, gr, 0);
+        cudaGraphDestroy(gr);
+        if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
+        m->dkey[0] = d_ids;
+        m->dkey[1] = d_cu;
+        m->dkey[2] = d_out;
+        m->dkey[3] = s;
+        m->dkey_shape[0] = batch;
+        m->dkey_shape[1] = T;
+        m->dkey_shape[2] = max_len;
+    }
+    TZ_CUDA(cudaGraphLaunch(m->dgraph, s));
+    return TZ_OK;
 }
 
 int tz_arctic_debug_hidden(tz_model_t m, int stage, float* out, int64_t T) {
@@ -820,10 +856,7 @@ int tz_arctic_profile(tz_model_t m, int enable) {
         for (auto& e : m->ev) TZ_CUDA(cudaEventCreate(&e));
         m->prof_slots = enable;
     }
-    if (m->graph) {  // the captured graph carries (or lacks) the event nodes: recapture
-        cudaGraphExecDestroy(m->graph);
-        m->graph = nullptr;
-    }
+    drop_graphs(m);  // the captured graphs carry (or lack) the event nodes: recapture
     m->profile = enable != 0;
     m->prof_fwd = 0;
     m->ev_n = 0;

@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(128)
     attention_kernel(const __half* __restrict__ qkv, const int* __restrict__ cu_seqlens, int lpad,
                      __half* __restrict__ out, unsigned* __restrict__ row_absmax) {
     extern __shared__ __align__(128) uint8_t sm[];
+    tzp::pdl_wait();
     const int b = blockIdx.z;
     const int h = blockIdx.y;
     const int seq0 = cu_seqlens[b];
@@ -63,6 +64,7 @@ __global__ void __launch_bounds__(128)
     tzp::cp_async_commit();
     tzp::cp_async_wait<0>();
     __syncthreads();
+    tzp::pdl_trigger();
     if (q0 + warp * 16 >= L) return;  // no further block-wide synchronisation below
 
     const uint32_t kaddr = tzp::smem_u32(ks), vaddr = tzp::smem_u32(vs), qaddr = tzp::smem_u32(qs);
@@ -187,7 +189,7 @@ size_t attention_smem_bytes(int max_len) {
 // qkv f16 [T, 1152]; cu_seqlens device [B+1]; out f16 [T, 384]; row_absmax (optional) [T] float
 // bits, accumulated with atomicMax (must start at zero).
 int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int batch, int max_len, void* out,
-                     unsigned* row_absmax, cudaStream_t s) {
+                     unsigned* row_absmax, cudaStream_t s, bool pdl) {
     TZ_CHECK(max_len >= 1 && max_len <= 512, TZ_EINVAL, "attention: max_len %d outside [1, 512]", max_len);
     if (batch == 0) return TZ_OK;
     const int lpad = (max_len + 63) / 64 * 64;
@@ -201,10 +203,8 @@ int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int b
         set |= 1u << (dev & 31);
     }
     dim3 grid((max_len + kQTile - 1) / kQTile, kHeads, batch);
-    attention_kernel<<<grid, 128, smem, s>>>(static_cast<const __half*>(qkv), cu_seqlens, lpad,
-                                             static_cast<__half*>(out), row_absmax);
-    TZ_CUDA(cudaGetLastError());
-    return TZ_OK;
+    return launch_kernel(attention_kernel, grid, dim3(128), smem, s, pdl, static_cast<const __half*>(qkv), cu_seqlens, lpad,
+                         static_cast<__half*>(out), row_absmax);
 }
 
 }  // namespace tz

@@ -322,6 +322,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     __syncthreads();
     tzp::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    tzp::pdl_wait();  // everything above is independent of the previous kernel's output
 
     const int n_tiles = (N + BN - 1) / BN;
     const int num_tiles = ((M + 127) / 128) * n_tiles;
@@ -461,6 +462,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         if (use_tma_store && lane == 0) tzp::bulk_wait_all();
     }
 
+    tzp::pdl_trigger();
     tzp::tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -535,9 +537,8 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     const int tiles = ((g.M + 127) / 128) * n_tiles;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
-    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, to, g.M, g.N, g.K, ep, use_tma, ctx->d_status);
-    TZ_CUDA(cudaGetLastError());
-    return TZ_OK;
+    return launch_kernel(kern, dim3(grid), dim3(C::THREADS), C::SMEM, s, g.pdl, ta, tb, to, g.M, g.N, g.K, ep, use_tma,
+                         ctx->d_status);
 }
 
 }  // namespace

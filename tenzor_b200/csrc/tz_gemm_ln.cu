@@ -1,0 +1,409 @@
+// tz_gemm_ln.cu -- tcgen05 GEMM whose epilogue finishes a post-LN transformer sub-block:
+//
+//   x_out[M, 384] = LayerNorm( dequant(A[M, K] * W[384, K]^T) + bias + residual )
+//   aux[M, 384]   = f16(x_out)                          (AUX = 0: the next GEMM's f16 operand)
+//                 | int8(x_out) with per-row scale       (AUX = 1: the next GEMM's W8A8 operand)
+//
+// Reference: selfAttention's output projection + residual + LayerNorm (arctic.zig:716-746) and
+// feedForward's second projection + residual + LayerNorm (arctic.zig:779-807); layerNormLastDim
+// numerics of layernorm.zig:26-116 (mean, then the mean of squared deviations, 1/sqrt(var+eps)).
+//
+// One CTA owns whole 128-row blocks (persistent over row blocks): the full 384-column accumulator
+// lives in TMEM (two N=192 MMAs per K step).  192 + 16*32 threads: warp 0 TMA producer (A block and
+// the two 192-row halves of W per 128-byte K block, 3-stage ring), warp 1 TMEM owner + MMA issuer,
+// warps 2..17 epilogue: warp w reads TMEM lane quarter (w % 4) and a 96-column slice.  Per row:
+// pass A dequantises, adds bias and residual, writes x back into TMEM and sums; pass B sums squared
+// deviations; pass C normalises and stores x_out (+ f16 aux, or y back to TMEM and |max|); pass D
+// (AUX = 1) quantises.  The four slices of a row combine their partial sums through shared memory
+// at mbarriers (bounded waits, one phase per tile).  No separate LayerNorm launch and no round trip
+// of the pre-LN activations.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "tz_internal.h"
+#include "tz_ptx.cuh"
+#include "tz_rowops.cuh"
+
+namespace tz {
+namespace {
+
+constexpr int kN = 384, kHalf = 192, kStages = 3, kEpiWarps = 16, kThreads = 64 + 32 * kEpiWarps;
+constexpr int kSlice = kN / 4;  // 96 columns per epilogue warp
+
+struct LnParams {
+    const float* bias;
+    const float* col_scale;
+    const float* row_scale;
+    const float* residual;
+    const float* gamma;
+    const float* beta;
+    float eps;
+    float* x_out;
+    void* aux;
+    float* aux_scale;
+};
+
+template <int KIND>
+struct LnCfg {
+    static constexpr int ELEM = KIND == KIND_I8 ? 1 : (KIND == KIND_TF32 ? 4 : 2);
+    static constexpr int BK = 128 / ELEM;
+    static constexpr int A_BYTES = 128 * 128;
+    static constexpr int B_BYTES = kN * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int RED_BYTES = 3 * 4 * 128 * 4;
+    static constexpr int SMEM = kStages * STAGE_BYTES + RED_BYTES + 256 + 1024;  // + barriers, alignment
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+// All epilogue warps meet here (one arrival per warp after its shared-memory writes); bounded wait on
+// the barrier's phase `parity` (one phase per tile).  False when the wait expired.
+__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t parity, int lane, int* status) {
+    __syncwarp();
+    if (lane == 0) tzp::mbar_arrive(bar);
+    return tzp::mbar_wait(bar, parity, status, nullptr);
+}
+
+template <int KIND>
+__device__ __forceinline__ float acc_to_f(uint32_t r) {
+    if constexpr (KIND == KIND_I8)
+        return __int2float_rn(static_cast<int>(r));
+    else
+        return __uint_as_float(r);
+}
+
+template <int KIND, int AUX>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
+                   LnParams p, int* status) {
+    using C = LnCfg<KIND>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = tzp::smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    float* red_sum = reinterpret_cast<float*>(smem + kStages * C::STAGE_BYTES);  // [4 slices][128 rows]
+    float* red_ssq = red_sum + 4 * 128;
+    float* red_max = red_ssq + 4 * 128;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::STAGE_BYTES + C::RED_BYTES);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;
+    uint64_t* tempty = tfull + 1;
+    uint64_t* drain = tempty + 1;
+    uint64_t* red_bar = drain + 1;  // [3]: the epilogue warps' row reductions (sum, ssq, max)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 3);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            tzp::mbar_init(&full[s], 1);
+            tzp::mbar_init(&empty[s], 1);
+        }
+        tzp::mbar_init(tfull, 1);
+        tzp::mbar_init(tempty, kEpiWarps);
+        tzp::mbar_init(drain, 1);
+        for (int i = 0; i < 3; ++i) tzp::mbar_init(&red_bar[i], kEpiWarps);
+        *abort_flag = 0;
+        tzp::fence_mbar_init();
+        tzp::tma_prefetch_desc(&tmA);
+        tzp::tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tzp::tmem_alloc(tmem_slot, 512);
+        tzp::tmem_relinquish();
+    }
+    tzp::tc_fence_before();
+    __syncthreads();
+    tzp::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    tzp::pdl_wait();
+
+    const int num_tiles = (M + 127) / 128;
+    const int kblocks = (K + C::BK - 1) / C::BK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0, armed = 0, armed_par = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!tzp::mbar_wait(&empty[stage], phase ^ 1u, status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tzp::tma_load_2d(sa, &tmA, kb * C::BK, tile * 128, &full[stage]);
+                    tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, 0, &full[stage]);
+                    tzp::tma_load_2d(sa + C::A_BYTES + kHalf * 128, &tmB, kb * C::BK, kHalf, &full[stage]);
+                    armed |= 1u << stage;
+                    armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+            }
+            for (int s = 0; s < kStages; ++s)
+                if (armed & (1u << s)) tzp::mbar_wait(&full[s], (armed_par >> s) & 1u, status, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t c_fmt = KIND == KIND_I8 ? 2u : 1u;
+            constexpr uint32_t ab_fmt = KIND == KIND_I8 ? 1u : (KIND == KIND_TF32 ? 2u : (KIND == KIND_BF16 ? 1u : 0u));
+            constexpr uint32_t idesc = tzp::make_idesc(c_fmt, ab_fmt, 128, kHalf);
+            int stage = 0;
+            uint32_t phase = 0, tphase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                if (!tzp::mbar_wait(tempty, tphase ^ 1u, status, abort_flag)) break;
+                tzp::tc_fence_after();
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!tzp::mbar_wait(&full[stage], phase, status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tzp::tc_fence_after();
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    const uint64_t ad = tzp::sdesc_k128(tzp::smem_u32(sa));
+                    const uint64_t bd0 = tzp::sdesc_k128(tzp::smem_u32(sa + C::A_BYTES));
+                    const uint64_t bd1 = tzp::sdesc_k128(tzp::smem_u32(sa + C::A_BYTES + kHalf * 128));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+                        tzp::umma<KIND>(tmem_base, ad + 2u * k, bd0 + 2u * k, idesc, acc);
+                        tzp::umma<KIND>(tmem_base + kHalf, ad + 2u * k, bd1 + 2u * k, idesc, acc);
+                    }
+                    tzp::umma_commit(&empty[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tzp::umma_commit(tfull);
+                tphase ^= 1u;
+            }
+            tzp::umma_commit(drain);
+            tzp::mbar_wait(drain, 0, status, nullptr);
+        }
+    } else {
+        const int e = warp - 2;
+        const int q = warp & 3;
+        const int slice = e >> 2;
+        const int rloc = q * 32 + lane;
+        const int c0 = slice * kSlice;
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0);
+        uint32_t tphase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            if (!tzp::mbar_wait(tfull, tphase, status, abort_flag)) break;
+            tzp::tc_fence_after();
+            const int row = tile * 128 + rloc;
+            const bool ok = row < M;
+            const float rs = (p.row_scale && ok) ? p.row_scale[row] : 1.0f;
+            const float* res = p.residual + static_cast<long long>(ok ? row : 0) * kN + c0;
+
+            // ---- pass A: x = dequant(acc) + bias + residual -> TMEM; row sum ----
+            float sum = 0.f;
+            float4 rb[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) rb[j] = ok ? *reinterpret_cast<const float4*>(res + 4 * j) : make_float4(0, 0, 0, 0);
+#pragma unroll
+            for (int c = 0; c < kSlice / 16; ++c) {
+                uint32_t r[16];
+                tzp::tmem_ld16(tbase + 16 * c, r);
+                float4 cur[4] = {rb[0], rb[1], rb[2], rb[3]};
+                if (c + 1 < kSlice / 16) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        rb[j] = ok ? *reinterpret_cast<const float4*>(res + 16 * (c + 1) + 4 * j) : make_float4(0, 0, 0, 0);
+                }
+                tzp::tmem_ld_wait();
+                const int col = c0 + 16 * c;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float v[4] = {acc_to_f<KIND>(r[4 * j]), acc_to_f<KIND>(r[4 * j + 1]), acc_to_f<KIND>(r[4 * j + 2]),
+                                  acc_to_f<KIND>(r[4 * j + 3])};
+                    if (p.row_scale) {
+                        const float4 cs = __ldg(reinterpret_cast<const float4*>(p.col_scale + col + 4 * j));
+                        v[0] = __fmul_rn(v[0], __fmul_rn(rs, cs.x));
+                        v[1] = __fmul_rn(v[1], __fmul_rn(rs, cs.y));
+                        v[2] = __fmul_rn(v[2], __fmul_rn(rs, cs.z));
+                        v[3] = __fmul_rn(v[3], __fmul_rn(rs, cs.w));
+                    } else if (p.col_scale) {
+                        const float4 cs = __ldg(reinterpret_cast<const float4*>(p.col_scale + col + 4 * j));
+                        v[0] = __fmul_rn(v[0], cs.x);
+                        v[1] = __fmul_rn(v[1], cs.y);
+                        v[2] = __fmul_rn(v[2], cs.z);
+                        v[3] = __fmul_rn(v[3], cs.w);
+                    }
+                    const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col + 4 * j));
+                    v[0] = __fadd_rn(__fadd_rn(v[0], b.x), cur[j].x);
+                    v[1] = __fadd_rn(__fadd_rn(v[1], b.y), cur[j].y);
+                    v[2] = __fadd_rn(__fadd_rn(v[2], b.z), cur[j].z);
+                    v[3] = __fadd_rn(__fadd_rn(v[3], b.w), cur[j].w);
+                    sum += (v[0] + v[1]) + (v[2] + v[3]);
+                    r[4 * j] = __float_as_uint(v[0]);
+                    r[4 * j + 1] = __float_as_uint(v[1]);
+                    r[4 * j + 2] = __float_as_uint(v[2]);
+                    r[4 * j + 3] = __float_as_uint(v[3]);
+                }
+                tzp::tmem_st16(tbase + 16 * c, r);
+            }
+            tzp::tmem_st_wait();
+            red_sum[slice * 128 + rloc] = sum;
+            if (!epi_sync(&red_bar[0], tphase, lane, status)) break;
+            const float mean =
+                ((red_sum[rloc] + red_sum[128 + rloc]) + (red_sum[256 + rloc] + red_sum[384 + rloc])) / static_cast<float>(kN);
+
+            // ---- pass B: sum of squared deviations ----
+            float ssq = 0.f;
+#pragma unroll
+            for (int c = 0; c < kSlice / 16; ++c) {
+                uint32_t r[16];
+                tzp::tmem_ld16(tbase + 16 * c, r);
+                tzp::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float d = __uint_as_float(r[j]) - mean;
+                    ssq += d * d;
+                }
+            }
+            red_ssq[slice * 128 + rloc] = ssq;
+            if (!epi_sync(&red_bar[1], tphase, lane, status)) break;
+            const float var =
+                ((red_ssq[rloc] + red_ssq[128 + rloc]) + (red_ssq[256 + rloc] + red_ssq[384 + rloc])) / static_cast<float>(kN);
+            const float inv_std = 1.0f / sqrtf(var + p.eps);
+
+            // ---- pass C: normalise, store x_out (+ f16 aux, or y -> TMEM and |max|) ----
+            float amax = 0.f;
+            float* xo = p.x_out + static_cast<long long>(row) * kN + c0;
+#pragma unroll
+            for (int c = 0; c < kSlice / 16; ++c) {
+                uint32_t r[16];
+                tzp::tmem_ld16(tbase + 16 * c, r);
+                tzp::tmem_ld_wait();
+                const int col = c0 + 16 * c;
+                float y[16];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 g = __ldg(reinterpret_cast<const float4*>(p.gamma + col + 4 * j));
+                    const float4 bb = __ldg(reinterpret_cast<const float4*>(p.beta + col + 4 * j));
+                    y[4 * j] = (__uint_as_float(r[4 * j]) - mean) * inv_std * g.x + bb.x;
+                    y[4 * j + 1] = (__uint_as_float(r[4 * j + 1]) - mean) * inv_std * g.y + bb.y;
+                    y[4 * j + 2] = (__uint_as_float(r[4 * j + 2]) - mean) * inv_std * g.z + bb.z;
+                    y[4 * j + 3] = (__uint_as_float(r[4 * j + 3]) - mean) * inv_std * g.w + bb.w;
+                }
+                if (ok) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        *reinterpret_cast<float4*>(xo + 16 * c + 4 * j) = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+                }
+                if constexpr (AUX == 0) {
+                    if (ok) {
+                        __half* a = static_cast<__half*>(p.aux) + static_cast<long long>(row) * kN + col;
+                        *reinterpret_cast<uint4*>(a) = make_uint4(tzp::pack_half2(y[0], y[1]), tzp::pack_half2(y[2], y[3]),
+                                                                  tzp::pack_half2(y[4], y[5]), tzp::pack_half2(y[6], y[7]));
+                        *reinterpret_cast<uint4*>(a + 8) = make_uint4(tzp::pack_half2(y[8], y[9]), tzp::pack_half2(y[10], y[11]),
+                                                                      tzp::pack_half2(y[12], y[13]), tzp::pack_half2(y[14], y[15]));
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        amax = fmaxf(amax, fabsf(y[j]));
+                        r[j] = __float_as_uint(y[j]);
+                    }
+                    tzp::tmem_st16(tbase + 16 * c, r);
+                }
+            }
+            if constexpr (AUX == 1) {
+                // ---- pass D: per-token int8 quantisation of the LayerNorm output ----
+                tzp::tmem_st_wait();
+                red_max[slice * 128 + rloc] = amax;
+                if (!epi_sync(&red_bar[2], tphase, lane, status)) break;
+                const float m = fmaxf(fmaxf(red_max[rloc], red_max[128 + rloc]), fmaxf(red_max[256 + rloc], red_max[384 + rloc]));
+                const float sc = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
+                const float inv = __fdiv_rn(1.0f, sc);
+                int8_t* a = static_cast<int8_t*>(p.aux) + static_cast<long long>(row) * kN + c0;
+#pragma unroll
+                for (int c = 0; c < kSlice / 16; ++c) {
+                    uint32_t r[16];
+                    tzp::tmem_ld16(tbase + 16 * c, r);
+                    tzp::tmem_ld_wait();
+                    uint32_t w[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        w[j] = 0;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            w[j] |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(__uint_as_float(r[4 * j + i]), inv))) << (8 * i);
+                    }
+                    if (ok) *reinterpret_cast<uint4*>(a + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                if (ok && slice == 0) p.aux_scale[row] = sc;
+            }
+            tzp::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tzp::mbar_arrive(tempty);
+            tphase ^= 1u;
+        }
+    }
+
+    tzp::pdl_trigger();
+    tzp::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tzp::tc_fence_after();
+        tzp::tmem_dealloc(tmem_base, 512);
+    }
+}
+
+CUtensorMapDataType dtype_of(int kind) {
+    return kind == KIND_I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                           : kind == KIND_TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                               : kind == KIND_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+template <int KIND, int AUX>
+int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
+    using C = LnCfg<KIND>;
+    auto kern = gemm_ln_kernel<KIND, AUX>;
+    static unsigned attr_set = 0;
+    int dev = 0;
+    TZ_CUDA(cudaGetDevice(&dev));
+    if (!(attr_set & (1u << (dev & 31)))) {
+        TZ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_set |= 1u << (dev & 31);
+    }
+    CUtensorMap ta, tb;
+    int rc = encode_tmap_2d(&ta, dtype_of(KIND), C::ELEM, g.a, static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M),
+                            static_cast<uint64_t>(g.lda) * C::ELEM, C::BK, 128);
+    if (rc) return rc;
+    rc = encode_tmap_2d(&tb, dtype_of(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.K), kN,
+                        static_cast<uint64_t>(g.ldb) * C::ELEM, C::BK, kHalf);
+    if (rc) return rc;
+    LnParams p{g.bias, g.col_scale, g.row_scale, g.residual, g.gamma, g.beta, g.eps, g.x_out, g.aux, g.aux_scale};
+    const int tiles = (g.M + 127) / 128;
+    const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+    if (grid <= 0) return TZ_OK;
+    return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, g.M, g.K, p, ctx->d_status);
+}
+
+}  // namespace
+
+int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
+    TZ_CHECK(g.M >= 0 && g.K > 0, TZ_EINVAL, "gemm_ln: bad shape");
+    if (g.M == 0) return TZ_OK;
+    TZ_CHECK(g.a && g.b && g.bias && g.residual && g.gamma && g.beta && g.x_out && g.aux, TZ_EINVAL, "gemm_ln: null operand");
+    TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm_ln: row_scale needs col_scale");
+    TZ_CHECK(g.aux_int8 == (g.aux_scale != nullptr), TZ_EINVAL, "gemm_ln: int8 aux needs its scale vector");
+    if (g.kind == KIND_I8) return g.aux_int8 ? launch_ln_impl<KIND_I8, 1>(ctx, g, s) : launch_ln_impl<KIND_I8, 0>(ctx, g, s);
+    if (g.kind == KIND_F16) return g.aux_int8 ? launch_ln_impl<KIND_F16, 1>(ctx, g, s) : launch_ln_impl<KIND_F16, 0>(ctx, g, s);
+    return fail(TZ_EUNSUPPORTED, "gemm_ln: kind %d", g.kind);
+}
+
+}  // namespace tz

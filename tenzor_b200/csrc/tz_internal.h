@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/tenzor_cuda.h"
@@ -62,6 +63,26 @@ int encode_tmap_2d_swz(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
                        uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                        uint32_t box_outer, CUtensorMapSwizzle swz);
 
+// Kernel launch through cudaLaunchKernelEx; with `pdl` the launch may begin while the previous
+// kernel in the stream is finishing (the kernel calls griddepcontrol.wait before reading inputs).
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                  Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+    return TZ_OK;
+}
+
 // ---- kernel launchers (defined in the .cu files) ---------------------------------------------
 enum GemmKind { KIND_F16 = 0, KIND_BF16 = 1, KIND_TF32 = 2, KIND_I8 = 3 };
 enum OutType { OUT_F32 = 0, OUT_F16 = 1, OUT_I32 = 2 };
@@ -86,7 +107,30 @@ struct GemmArgs {
     unsigned* row_absmax = nullptr;    // [M] atomicMax of |stored value| (float bits)
     int n_ops = -1;                    // >= 0: generic op chain instead of the fixed epilogue
     int ops[8] = {0};
+    bool pdl = false;                  // programmatic dependent launch (inside the model forward)
 };
 int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s);
+
+// GEMM with N = 384 whose epilogue adds bias + residual and applies LayerNorm (tz_gemm_ln.cu).
+struct GemmLnArgs {
+    int kind = KIND_F16;
+    const void* a = nullptr;  // [M, K]
+    const void* b = nullptr;  // [384, K]
+    int64_t lda = 0, ldb = 0;
+    int M = 0, K = 0;
+    const float* bias = nullptr;       // [384]
+    const float* col_scale = nullptr;  // [384]
+    const float* row_scale = nullptr;  // [M]
+    const float* residual = nullptr;   // [M, 384] f32 (may alias x_out)
+    const float* gamma = nullptr;
+    const float* beta = nullptr;
+    float eps = 1e-12f;
+    float* x_out = nullptr;            // [M, 384] f32
+    void* aux = nullptr;               // [M, 384] f16 or int8
+    float* aux_scale = nullptr;        // [M] when aux is int8
+    bool aux_int8 = false;
+    bool pdl = false;
+};
+int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s);
 
 }  // namespace tz
