@@ -384,6 +384,88 @@ def run_ours(a):
     return 0
 
 
+def run_micro(a):
+    """the fused-op microbenchmarks, one JSON line each (not the headline metric).
+    Inputs are seeded U[-1, 1]; each timed region is K launches with the L2 flushed before each."""
+    import torch
+    from tenzor_b200 import expr as E
+    from tenzor_b200 import ops
+    from tenzor_b200 import synthetic as S
+    from tenzor_b200.runtime import Context
+    ctx = Context(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    hbm, bf16, bf16_sus, src = peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
+
+    def timed(fn):
+        for _ in range(a.warmup):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(a.steps):
+            flush.zero_()
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record(stream)
+            fn()
+            e_.record(stream)
+            e_.synchronize()
+            tot += s_.elapsed_time(e_)
+        return tot / a.steps
+
+    def u(seed, shape):
+        return torch.from_numpy(S.uniform(seed, shape, -1.0, 1.0)).cuda()
+
+    lines = []
+    # (a) [8192,384] x [384,1536] + bias + GELU (B not transposed), tf32 tensor cores
+    A, B, bias = u(1, (8192, 384)), u(2, (384, 1536)), u(3, (1536,))
+    e = E.matmul(A, B).add(bias).gelu()
+    ms = timed(lambda: e.eval(ctx))
+    fl = 2.0 * 8192 * 384 * 1536
+    lines.append({"metric": "fused matmul+bias+GELU [8192,384]x[384,1536] TFLOP/s (f32 in, tf32 tensor cores)",
+                  "value": fl / ms / 1e9, "unit": "TFLOP/s", "ms": ms, "plan": E.analyze(e),
+                  "roofline": {"bound": "tensor", "peak": bf16_sus / 2, "frac": fl / ms / 1e9 / (bf16_sus / 2),
+                               "peak_source": f"tf32 = half of {src} bf16 sustained (nominal ratio)"}})
+    # (b) exp((a + b) * c), a, c [16384, 4096], b [4096]
+    a_, b_, c_ = u(4, (16384, 4096)), u(5, (4096,)), u(6, (16384, 4096))
+    e = E.tensor(a_).add(b_).mul(c_).exp()
+    out = torch.empty_like(a_)
+    ms = timed(lambda: ops.ew_add_mul_exp(ctx, a_, b_, c_, out=out))
+    byts = 3 * 64 * 2 ** 20 * 4 + 4096 * 4
+    lines.append({"metric": "elementwise chain a.add(b).mul(c).exp() 64M elems GB/s", "value": byts / ms / 1e6,
+                  "unit": "GB/s", "ms": ms, "plan": E.analyze(e),
+                  "roofline": {"bound": "hbm", "peak": hbm, "frac": byts / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy"}})
+    del a_, c_, out
+    # (c) LayerNorm [32768, 384]
+    x, g, bb = u(7, (32768, 384)), torch.ones(384, device="cuda"), torch.zeros(384, device="cuda")
+    y = torch.empty_like(x)
+    ms = timed(lambda: ops.layer_norm_last_dim(ctx, x, g, bb, 1e-5, out=y))
+    byts = 2 * 32768 * 384 * 4 + 2 * 384 * 4
+    lines.append({"metric": "LayerNorm [32768,384] GB/s", "value": byts / ms / 1e6, "unit": "GB/s", "ms": ms,
+                  "roofline": {"bound": "hbm", "peak": hbm, "frac": byts / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy"}})
+    # (c) masked softmax [96, 128, 128], key lengths U{16..128}; 32 distinct buffers round-robin (> L2)
+    nb = 32
+    xs = [u(100 + i, (96, 128, 128)) for i in range(nb)]
+    ys = [torch.empty_like(t) for t in xs]
+    kl = torch.from_numpy(S.randint(9, 96, 16, 128).astype(np.int32)).cuda()
+    it = [0]
+
+    def sm():
+        i = it[0] % nb
+        it[0] += 1
+        ops.softmax_keylen(ctx, xs[i], kl, out=ys[i])
+    ms = timed(sm)
+    byts = 2 * 96 * 128 * 128 * 4
+    lines.append({"metric": "masked softmax [96,128,128] GB/s", "value": byts / ms / 1e6, "unit": "GB/s", "ms": ms,
+                  "roofline": {"bound": "hbm", "peak": hbm, "frac": byts / ms / 1e6 / hbm,
+                               "peak_source": f"{src} HBM copy; 32 distinct 6.3 MB buffers round-robin"}})
+    for ln in lines:
+        ln.update({"steps": a.steps, "warmup": a.warmup, "data": "synthetic U[-1,1]", "config": {"workload": "configs[2]"}})
+        print(json.dumps(ln), flush=True)
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -393,11 +475,14 @@ def main():
     ap.add_argument("--config", default="c2", choices=list(CONFIGS))
     ap.add_argument("--mode", default="w8a8", choices=["w8a8", "w8a32", "f32"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--micro", action="store_true", help="configs[2] fused-op microbenchmarks (one line each)")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
     if a.impl == "reference":
         return run_reference(a)
+    if a.micro:
+        return run_micro(a)
     return run_ours(a)
 
 

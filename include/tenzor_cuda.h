@@ -160,7 +160,16 @@ typedef enum {
     TZ_OP_SQRT = 11,
     TZ_OP_RSQRT = 12,
     TZ_OP_SIN = 13,
-    TZ_OP_COS = 14
+    TZ_OP_COS = 14,
+    TZ_OP_ERF = 15,      /* ONNX Erf */
+    TZ_OP_GELU_ERF = 16, /* ONNX Gelu (default): 0.5 x (1 + erf(x / sqrt 2)) */
+    /* binary ops of an elementwise program (BinaryExpr, expr.zig:352-513) */
+    TZ_EW_ADD = 20,
+    TZ_EW_SUB = 21,
+    TZ_EW_MUL = 22,
+    TZ_EW_DIV = 23,
+    TZ_EW_MAX = 24,
+    TZ_EW_MIN = 25
 } tz_op;
 
 typedef enum { TZ_RED_SUM = 0, TZ_RED_MEAN = 1, TZ_RED_PROD = 2, TZ_RED_MAX = 3, TZ_RED_MIN = 4 } tz_reduce_op;
@@ -210,6 +219,29 @@ int tz_matmul_epilogue(tz_ctx_t ctx, const float* a, const float* b, int trans_b
  * evaluation of UnaryExpr(exp, BinaryExpr(mul, BinaryExpr(add, a, b), c)) in one pass. */
 int tz_ew_add_mul_exp(tz_ctx_t ctx, const float* a, const float* b_row, const float* c, float* out,
                       int64_t rows, int cols, tz_stream_t stream);
+/* A fused elementwise expression over up to 4 broadcast inputs, evaluated in one pass (the launch
+ * that an elementwise_chain FusionPlan, analyzer.zig:106-153, lowers to).  Input k is read at
+ * in[k][r * row_stride[k] + c * col_stride[k]] for output element (r, c) of [rows, cols] (stride 0 =
+ * broadcast, executor.zig:152-197).  Instruction i computes reg[dst] = op(reg[a], reg[b]); registers
+ * 0..3 hold the inputs, 4..11 temporaries, 12..15 the constants consts[0..3]; unary ops
+ * (TZ_OP_RELU..TZ_OP_GELU_ERF) ignore b.  The output is reg[result]. */
+#define TZ_EW_MAX_INPUTS 4
+#define TZ_EW_MAX_INSTR 16
+typedef struct {
+    int op, dst, a, b;
+} tz_ew_instr;
+typedef struct {
+    int n_inputs;
+    const float* in[TZ_EW_MAX_INPUTS];
+    int64_t row_stride[TZ_EW_MAX_INPUTS];
+    int64_t col_stride[TZ_EW_MAX_INPUTS];
+    int n_instr;
+    tz_ew_instr instr[TZ_EW_MAX_INSTR];
+    int result;
+    float consts[4];
+} tz_ew_program;
+int tz_ew_program_run(tz_ctx_t ctx, const tz_ew_program* prog, float* out, int64_t rows, int cols,
+                      tz_stream_t stream);
 /* General fused elementwise chain (FusedElementwiseKernel, codegen.zig:15-74): out = ops(x). */
 int tz_ew_unary_chain(tz_ctx_t ctx, const float* x, float* out, int64_t n, const int* ops,
                       int n_ops, tz_stream_t stream);

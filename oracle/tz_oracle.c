@@ -437,6 +437,8 @@ float tzo_unary(int op, float x) {
         case 12: return 1.0f / sqrtf(x);                      /* rsqrt */
         case 13: return sinf(x);                              /* sin */
         case 14: return cosf(x);                              /* cos */
+        case 15: return erff(x);                              /* erf (ONNX Erf) */
+        case 16: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); /* ONNX Gelu */
         default: return x;
     }
 }

@@ -14,7 +14,8 @@ LIB_PATH = os.path.join(PKG, "libtenzor_cuda.so")
 TZ_OK, TZ_EINVAL, TZ_ENOMEM, TZ_ECUDA, TZ_ETIMEOUT, TZ_EUNSUPPORTED, TZ_EMISSING = range(7)
 QUANT_F32, QUANT_W8A32, QUANT_W8A8 = 0, 1, 2
 OP = {"add": 1, "relu": 2, "gelu": 3, "sigmoid": 4, "tanh": 5, "exp": 6, "neg": 7, "abs": 8,
-      "silu": 9, "log": 10, "sqrt": 11, "rsqrt": 12, "sin": 13, "cos": 14}
+      "silu": 9, "log": 10, "sqrt": 11, "rsqrt": 12, "sin": 13, "cos": 14, "erf": 15, "gelu_erf": 16}
+EW_BINARY = {"add": 20, "sub": 21, "mul": 22, "div": 23, "max": 24, "min": 25}
 RED = {"sum": 0, "mean": 1, "prod": 2, "max": 3, "min": 4}
 
 # Every symbol include/tenzor_cuda.h declares (checked by tests/test_abi.py).
@@ -26,7 +27,8 @@ EXPORTS = [
     "tz_arctic_debug_hidden", "tz_arctic_debug_operand", "tz_arctic_profile", "tz_arctic_profile_read", "tz_layernorm_last_dim",
     "tz_softmax_last_axis", "tz_softmax_keylen", "tz_linear_f32", "tz_linear_w8a32",
     "tz_linear_w8a8", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
-    "tz_matmul_epilogue", "tz_ew_add_mul_exp", "tz_ew_unary_chain", "tz_reduce", "tz_gather_rows",
+    "tz_matmul_epilogue", "tz_ew_add_mul_exp", "tz_ew_program_run", "tz_ew_unary_chain", "tz_reduce",
+    "tz_gather_rows",
 ]
 
 
@@ -48,6 +50,15 @@ class ArcticLayer(C.Structure):
     _fields_ += [(n, P) for n in ("query_bias", "key_bias", "value_bias", "attn_output_bias",
                                   "intermediate_bias", "output_bias", "attn_ln_gamma", "attn_ln_beta",
                                   "output_ln_gamma", "output_ln_beta")]
+
+
+class EwInstr(C.Structure):
+    _fields_ = [("op", C.c_int), ("dst", C.c_int), ("a", C.c_int), ("b", C.c_int)]
+
+
+class EwProgram(C.Structure):
+    _fields_ = [("n_inputs", C.c_int), ("in_", P * 4), ("row_stride", C.c_int64 * 4), ("col_stride", C.c_int64 * 4),
+                ("n_instr", C.c_int), ("instr", EwInstr * 16), ("result", C.c_int), ("consts", C.c_float * 4)]
 
 
 class ArcticWeights(C.Structure):
@@ -101,6 +112,7 @@ def _declare(L):
         "tz_matmul_epilogue": [P, P, P, i, P, P, i, P, i, i, i, P],
         "tz_ew_add_mul_exp": [P, P, P, P, P, i64, i, P],
         "tz_ew_unary_chain": [P, P, P, i64, P, i, P],
+        "tz_ew_program_run": [P, C.POINTER(EwProgram), P, i64, i, P],
         "tz_reduce": [P, i, P, i, P, i64, P, P],
         "tz_gather_rows": [P, P, i64, P, i64, i, P, P],
     }

@@ -40,7 +40,7 @@ struct EpiParams {
     int gelu;
     unsigned* row_absmax;
     int n_ops;
-    uint32_t ops;  // op o in bits [4o, 4o+4) (packed: no dynamic indexing of kernel parameters)
+    uint64_t ops;  // op o in bits [5o, 5o+5) (packed: no dynamic indexing of kernel parameters)
     int vec_ok;  // 16-byte aligned rows for vector stores / residual loads
 };
 
@@ -67,6 +67,8 @@ __device__ __forceinline__ float apply_op(int op, float x) {
         case TZ_OP_RSQRT: return 1.0f / sqrtf(x);
         case TZ_OP_SIN: return sinf(x);
         case TZ_OP_COS: return cosf(x);
+        case TZ_OP_ERF: return erff(x);
+        case TZ_OP_GELU_ERF: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
         default: return x;
     }
 }
@@ -139,7 +141,7 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[CW
             float x = v[j];
             if (col < N) {
                 for (int o = 0; o < ep.n_ops; ++o) {
-                    const int op = static_cast<int>((ep.ops >> (4 * o)) & 15u);
+                    const int op = static_cast<int>((ep.ops >> (5 * o)) & 31u);
                     if (op == TZ_OP_ADD) {
                         if (ep.bias) x = x + __ldg(ep.bias + col);
                     } else {
@@ -187,9 +189,15 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[CW
                 v[j + 3] = __fadd_rn(v[j + 3], b.w);
             }
         }
-        if (ep.gelu) {
+        if (ep.gelu == 1) {
 #pragma unroll
             for (int j = 0; j < CW; ++j) v[j] = gelu_fast(v[j]);
+        } else if (ep.gelu == 2) {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) v[j] = apply_op(TZ_OP_GELU, v[j]);
+        } else if (ep.gelu == 3) {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
         }
         if (ep.residual && row_ok) {
 #pragma unroll
@@ -211,7 +219,9 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[CW
                 else if (ep.col_scale)
                     x = __fmul_rn(x, ep.col_scale[col]);
                 if (ep.bias) x = __fadd_rn(x, ep.bias[col]);
-                if (ep.gelu) x = gelu_fast(x);
+                if (ep.gelu == 1) x = gelu_fast(x);
+                else if (ep.gelu == 2) x = apply_op(TZ_OP_GELU, x);
+                else if (ep.gelu == 3) x = x > 0.0f ? x : 0.0f;
                 if (ep.residual && row_ok) x = __fadd_rn(x, ep.residual[static_cast<long long>(row) * ep.ldr + col]);
             }
             v[j] = x;
@@ -513,7 +523,7 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     ep.row_absmax = g.row_absmax;
     ep.n_ops = g.n_ops;
     ep.ops = 0;
-    for (int i = 0; i < 8; ++i) ep.ops |= (static_cast<uint32_t>(g.ops[i]) & 15u) << (4 * i);
+    for (int i = 0; i < 8; ++i) ep.ops |= (static_cast<uint64_t>(g.ops[i]) & 31u) << (5 * i);
     const int out_elem = g.out_type == OUT_F16 ? 2 : 4;
     const bool out_al = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldo * out_elem) % 16 == 0);
     const bool res_al = !g.residual || ((reinterpret_cast<uintptr_t>(g.residual) % 16 == 0) && ((g.ldr * 4) % 16 == 0));

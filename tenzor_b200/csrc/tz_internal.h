@@ -103,7 +103,8 @@ struct GemmArgs {
     void* out = nullptr;               // [M, ldo]
     int64_t ldo = 0;
     int out_type = OUT_F32;
-    int gelu = 0;                      // 1: model GELU (tanhf) after bias, before residual
+    int gelu = 0;                      // after bias: 1 model GELU (hardware tanh), 2 codegen GELU
+                                       // (tanh = 2 sigmoid(2x) - 1), 3 ReLU
     unsigned* row_absmax = nullptr;    // [M] atomicMax of |stored value| (float bits)
     int n_ops = -1;                    // >= 0: generic op chain instead of the fixed epilogue
     int ops[8] = {0};

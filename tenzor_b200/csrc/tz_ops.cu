@@ -97,7 +97,7 @@ int tz_matmul_epilogue(tz_ctx_t ctx, const float* a, const float* b, int trans_b
     TZ_CHECK(ctx && a && b && c && m >= 0 && k > 0 && n > 0 && n_ops >= 0 && n_ops <= 8 && (n_ops == 0 || ops),
              TZ_EINVAL, "tz_matmul_epilogue: bad arguments");
     for (int i = 0; i < n_ops; ++i)
-        TZ_CHECK(ops[i] >= TZ_OP_ADD && ops[i] <= TZ_OP_COS, TZ_EINVAL, "tz_matmul_epilogue: bad op %d", ops[i]);
+        TZ_CHECK(ops[i] >= TZ_OP_ADD && ops[i] <= TZ_OP_GELU_ERF, TZ_EINVAL, "tz_matmul_epilogue: bad op %d", ops[i]);
     cudaStream_t s = pick_stream(ctx, stream);
     const float* bt = b;
     if (!trans_b) {
@@ -110,7 +110,16 @@ int tz_matmul_epilogue(tz_ctx_t ctx, const float* a, const float* b, int trans_b
     GemmArgs g;
     g.kind = KIND_TF32;
     g.a = a; g.lda = k; g.b = bt; g.ldb = k; g.M = m; g.N = n; g.K = k;
-    g.bias = bias; g.out = c; g.ldo = n; g.out_type = OUT_F32;
+    g.out = c; g.ldo = n; g.out_type = OUT_F32;
+    // Chains the fixed epilogue does natively (bias, then one activation) skip the op interpreter.
+    const bool has_add = n_ops >= 1 && ops[0] == TZ_OP_ADD;
+    const int act = n_ops == (has_add ? 2 : 1) ? ops[n_ops - 1] : 0;
+    if (n_ops == 0 || (n_ops == 1 && has_add) || (n_ops <= 2 && (act == TZ_OP_GELU || act == TZ_OP_RELU))) {
+        g.bias = has_add ? bias : nullptr;
+        g.gelu = act == TZ_OP_GELU ? 2 : act == TZ_OP_RELU ? 3 : 0;
+        return launch_gemm(ctx, g, s);
+    }
+    g.bias = bias;
     g.n_ops = n_ops;
     for (int i = 0; i < n_ops; ++i) g.ops[i] = ops[i];
     return launch_gemm(ctx, g, s);

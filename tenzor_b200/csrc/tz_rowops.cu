@@ -222,6 +222,47 @@ __global__ void ew_unary_chain_kernel(const float* x, float* out, long long n, O
     }
 }
 
+// One pass over [rows, cols] evaluating a small register program per element.
+struct EwProgram {
+    int n_in;
+    const float* in[4];
+    long long rs[4], cs[4];
+    int n_instr;
+    int op[16], dst[16], a[16], b[16];
+    int result;
+    float consts[4];
+};
+
+__global__ void ew_program_kernel(EwProgram p, float* __restrict__ out, long long rows, int cols) {
+    const long long n = rows * cols;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / cols, c = i - r * cols;
+        float reg[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) reg[k] = k < p.n_in ? __ldg(p.in[k] + r * p.rs[k] + c * p.cs[k]) : 0.0f;
+#pragma unroll
+        for (int k = 4; k < 12; ++k) reg[k] = 0.0f;
+#pragma unroll
+        for (int k = 12; k < 16; ++k) reg[k] = p.consts[k - 12];
+        for (int t = 0; t < p.n_instr; ++t) {
+            float va = 0.f, vb = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {  // register reads by unrolled select: no local memory
+                va = (k == p.a[t]) ? reg[k] : va;
+                vb = (k == p.b[t]) ? reg[k] : vb;
+            }
+            const float res = binary_op(p.op[t], va, vb);
+#pragma unroll
+            for (int k = 4; k < 12; ++k) reg[k] = (k == p.dst[t]) ? res : reg[k];
+        }
+        float o = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) o = (k == p.result) ? reg[k] : o;
+        out[i] = o;
+    }
+}
+
 // Fused pre-ops + reduction.  Stage 1: per-block partials (f64 for sum/mean); stage 2: one block.
 __global__ void reduce_stage1_kernel(const float* x, long long n, int red, OpList pre, double* part) {
     double acc = (red == TZ_RED_PROD) ? 1.0 : (red == TZ_RED_MAX) ? -INFINITY : (red == TZ_RED_MIN) ? INFINITY : 0.0;
@@ -394,6 +435,42 @@ int tz_ew_add_mul_exp(tz_ctx_t ctx, const float* a, const float* b_row, const fl
     return TZ_OK;
 }
 
+int tz_ew_program_run(tz_ctx_t ctx, const tz_ew_program* prog, float* out, int64_t rows, int cols,
+                      tz_stream_t stream) {
+    TZ_CHECK(ctx && prog && out && rows >= 0 && cols > 0, TZ_EINVAL, "tz_ew_program_run: bad arguments");
+    TZ_CHECK(prog->n_inputs >= 1 && prog->n_inputs <= TZ_EW_MAX_INPUTS && prog->n_instr >= 0 &&
+                 prog->n_instr <= TZ_EW_MAX_INSTR && prog->result >= 0 && prog->result < 16,
+             TZ_EINVAL, "tz_ew_program_run: bad program shape");
+    EwProgram p{};
+    p.n_in = prog->n_inputs;
+    for (int k = 0; k < p.n_in; ++k) {
+        TZ_CHECK(prog->in[k], TZ_EINVAL, "tz_ew_program_run: input %d is null", k);
+        p.in[k] = prog->in[k];
+        p.rs[k] = prog->row_stride[k];
+        p.cs[k] = prog->col_stride[k];
+    }
+    p.n_instr = prog->n_instr;
+    for (int t = 0; t < p.n_instr; ++t) {
+        const tz_ew_instr& in = prog->instr[t];
+        const bool unary = in.op >= TZ_OP_RELU && in.op <= TZ_OP_GELU_ERF;
+        const bool binary = in.op >= TZ_EW_ADD && in.op <= TZ_EW_MIN;
+        TZ_CHECK((unary || binary) && in.dst >= 4 && in.dst < 12 && in.a >= 0 && in.a < 16 && (unary || (in.b >= 0 && in.b < 16)),
+                 TZ_EINVAL, "tz_ew_program_run: bad instruction %d", t);
+        p.op[t] = in.op;
+        p.dst[t] = in.dst;
+        p.a[t] = in.a;
+        p.b[t] = unary ? 0 : in.b;
+    }
+    p.result = prog->result;
+    for (int k = 0; k < 4; ++k) p.consts[k] = prog->consts[k];
+    const long long n = rows * static_cast<long long>(cols);
+    if (n == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    ew_program_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(p, out, rows, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
 int tz_ew_unary_chain(tz_ctx_t ctx, const float* x, float* out, int64_t n, const int* ops, int n_ops,
                       tz_stream_t stream) {
     TZ_CHECK(ctx && x && out && n >= 0 && n_ops >= 0 && n_ops <= 8 && (n_ops == 0 || ops), TZ_EINVAL,
@@ -402,7 +479,7 @@ int tz_ew_unary_chain(tz_ctx_t ctx, const float* x, float* out, int64_t n, const
     OpList l{};
     l.n = n_ops;
     for (int i = 0; i < n_ops; ++i) {
-        TZ_CHECK(ops[i] >= TZ_OP_RELU && ops[i] <= TZ_OP_COS, TZ_EINVAL, "tz_ew_unary_chain: op %d is not unary", ops[i]);
+        TZ_CHECK(ops[i] >= TZ_OP_RELU && ops[i] <= TZ_OP_GELU_ERF, TZ_EINVAL, "tz_ew_unary_chain: op %d is not unary", ops[i]);
         l.op[i] = ops[i];
     }
     cudaStream_t s = pick_stream(ctx, stream);
@@ -419,7 +496,7 @@ int tz_reduce(tz_ctx_t ctx, int reduce_op, const int* pre_ops, int n_pre, const 
     OpList l{};
     l.n = n_pre;
     for (int i = 0; i < n_pre; ++i) {
-        TZ_CHECK(pre_ops[i] >= TZ_OP_RELU && pre_ops[i] <= TZ_OP_COS, TZ_EINVAL, "tz_reduce: op %d is not unary", pre_ops[i]);
+        TZ_CHECK(pre_ops[i] >= TZ_OP_RELU && pre_ops[i] <= TZ_OP_GELU_ERF, TZ_EINVAL, "tz_reduce: op %d is not unary", pre_ops[i]);
         l.op[i] = pre_ops[i];
     }
     cudaStream_t s = pick_stream(ctx, stream);

@@ -49,7 +49,21 @@ __device__ __forceinline__ float unary_op(int op, float x) {
         case TZ_OP_RSQRT: return 1.0f / sqrtf(x);
         case TZ_OP_SIN: return sinf(x);
         case TZ_OP_COS: return cosf(x);
+        case TZ_OP_ERF: return erff(x);
+        case TZ_OP_GELU_ERF: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
         default: return x;
+    }
+}
+
+__device__ __forceinline__ float binary_op(int op, float a, float b) {
+    switch (op) {
+        case TZ_EW_ADD: return a + b;
+        case TZ_EW_SUB: return a - b;
+        case TZ_EW_MUL: return a * b;
+        case TZ_EW_DIV: return a / b;
+        case TZ_EW_MAX: return fmaxf(a, b);
+        case TZ_EW_MIN: return fminf(a, b);
+        default: return unary_op(op, a);
     }
 }
 
