@@ -199,6 +199,17 @@ int tz_linear_w8a32(tz_ctx_t ctx, const float* x, const int8_t* wq, const uint16
  * int8 path is W8A32); scratch from the context arena. */
 int tz_linear_w8a8(tz_ctx_t ctx, const float* x, const int8_t* wq, const uint16_t* scale_f16,
                    const float* bias, float* y, int m, int k, int n, tz_stream_t stream);
+/* tz_linear_w8a8 for callers that cannot allocate device memory while they run (inside a CUDA
+ * graph capture, under an allocator that has reserved all device memory, or on a thread that cannot
+ * take the device-wide synchronisation of cudaMalloc / cudaFree).  This entry point has no
+ * counterpart in the reference.  It allocates nothing: its temporaries live in an 8 MiB device array
+ * that the library owns (every GPU that loads the library holds it until exit), so it needs
+ * m*k + 4*m + 4*n bytes (each part rounded up to 256) <= 8 MiB and returns TZ_EINVAL otherwise.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  All calls share the array: calls that overlap on the GPU race.
+ * Same arguments, result and stream semantics as tz_linear_w8a8. */
+int tz_linear_w8a8_noalloc(tz_ctx_t ctx, const float* x, const int8_t* wq, const uint16_t* scale_f16,
+                           const float* bias, float* y, int m, int k, int n, tz_stream_t stream);
 /* Raw int8 GEMM: c[m,n] = a[m,k] w[n,k]^T in int32 (bit-exact accumulators).  k % 16 == 0. */
 int tz_gemm_i8_i32(tz_ctx_t ctx, const int8_t* a, const int8_t* w, int32_t* c, int m, int k,
                    int n, tz_stream_t stream);

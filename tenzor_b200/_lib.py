@@ -26,7 +26,7 @@ EXPORTS = [
     "tz_arctic_forward", "tz_arctic_forward_padded", "tz_arctic_forward_device",
     "tz_arctic_debug_hidden", "tz_arctic_debug_operand", "tz_arctic_profile", "tz_arctic_profile_read", "tz_layernorm_last_dim",
     "tz_softmax_last_axis", "tz_softmax_keylen", "tz_linear_f32", "tz_linear_w8a32",
-    "tz_linear_w8a8", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
+    "tz_linear_w8a8", "tz_linear_w8a8_noalloc", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
     "tz_matmul_epilogue", "tz_ew_add_mul_exp", "tz_ew_program_run", "tz_ew_unary_chain", "tz_reduce",
     "tz_gather_rows",
 ]
@@ -106,6 +106,7 @@ def _declare(L):
         "tz_linear_f32": [P, P, P, P, P, P, i, i, i, P],
         "tz_linear_w8a32": [P, P, P, P, P, P, i, i, i, P],
         "tz_linear_w8a8": [P, P, P, P, P, P, i, i, i, P],
+        "tz_linear_w8a8_noalloc": [P, P, P, P, P, P, i, i, i, P],
         "tz_gemm_i8_i32": [P, P, P, P, i, i, i, P],
         "tz_quantize_weight_rows": [P, P, P, P, i64, i, P],
         "tz_quantize_act_rows": [P, P, P, P, i64, i, P],
