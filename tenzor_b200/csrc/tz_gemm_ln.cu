@@ -9,12 +9,14 @@
 // numerics of layernorm.zig:26-116 (mean, then the mean of squared deviations, 1/sqrt(var+eps)).
 //
 // One CTA owns whole 128-row blocks (persistent over row blocks): the full 384-column accumulator
-// lives in TMEM (two N=192 MMAs per K step).  192 + 16*32 threads: warp 0 TMA producer (A block and
-// the two 192-row halves of W per 128-byte K block, 3-stage ring), warp 1 TMEM owner + MMA issuer,
+// lives in TMEM (two N=192 MMAs per K step).  64 + 16*32 threads: warp 0 TMA producer (A block and
+// the two 192-row halves of W per 128-byte K block, 2-stage ring), warp 1 TMEM owner + MMA issuer,
 // warps 2..17 epilogue: warp w reads TMEM lane quarter (w % 4) and a 96-column slice.  Per row:
 // pass A dequantises, adds bias and residual, writes x back into TMEM and sums; pass B sums squared
 // deviations; pass C normalises and stores x_out (+ f16 aux, or y back to TMEM and |max|); pass D
-// (AUX = 1) quantises.  The four slices of a row combine their partial sums through shared memory
+// (AUX = 1) quantises.  Residual tiles arrive and x_out tiles leave as 32-row x 16-column TMA boxes
+// (double-buffered per warp), so no thread touches a residual or output row in global memory
+// directly.  The four slices of a row combine their partial sums through shared memory
 // at mbarriers (bounded waits, one phase per tile).  No separate LayerNorm launch and no round trip
 // of the pre-LN activations.
 #include <cuda.h>
@@ -28,7 +30,8 @@
 namespace tz {
 namespace {
 
-constexpr int kN = 384, kHalf = 192, kStages = 3, kEpiWarps = 16, kThreads = 64 + 32 * kEpiWarps;
+constexpr int kN = 384, kHalf = 192, kStages = 2, kEpiWarps = 16, kThreads = 64 + 32 * kEpiWarps;
+constexpr int kBox = 32 * 16 * 4;  // one 32-row x 16-column f32 tile: a TMA box of the residual / output
 constexpr int kSlice = kN / 4;  // 96 columns per epilogue warp
 
 struct LnParams {
@@ -51,8 +54,9 @@ struct LnCfg {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = kN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGING = kEpiWarps * 2 * kBox;  // two residual/output boxes per epilogue warp
     static constexpr int RED_BYTES = 3 * 4 * 128 * 4;
-    static constexpr int SMEM = kStages * STAGE_BYTES + RED_BYTES + 256 + 1024;  // + barriers, alignment
+    static constexpr int SMEM = kStages * STAGE_BYTES + STAGING + RED_BYTES + 512 + 1024;  // + barriers, alignment
     static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -74,22 +78,25 @@ __device__ __forceinline__ float acc_to_f(uint32_t r) {
 
 template <int KIND, int AUX>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
+    gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmX, int M, int K,
                    LnParams p, int* status) {
     using C = LnCfg<KIND>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = tzp::smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-    float* red_sum = reinterpret_cast<float*>(smem + kStages * C::STAGE_BYTES);  // [4 slices][128 rows]
+    uint8_t* staging = smem + kStages * C::STAGE_BYTES;                          // [16 warps][2 boxes]
+    float* red_sum = reinterpret_cast<float*>(staging + C::STAGING);             // [4 slices][128 rows]
     float* red_ssq = red_sum + 4 * 128;
     float* red_max = red_ssq + 4 * 128;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::STAGE_BYTES + C::RED_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING + C::RED_BYTES);
     uint64_t* empty = full + kStages;
     uint64_t* tfull = empty + kStages;
     uint64_t* tempty = tfull + 1;
     uint64_t* drain = tempty + 1;
     uint64_t* red_bar = drain + 1;  // [3]: the epilogue warps' row reductions (sum, ssq, max)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 3);
+    uint64_t* res_bar = red_bar + 3;  // [16 warps][2 boxes]: residual tile arrivals
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 2 * kEpiWarps);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -103,10 +110,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tzp::mbar_init(tempty, kEpiWarps);
         tzp::mbar_init(drain, 1);
         for (int i = 0; i < 3; ++i) tzp::mbar_init(&red_bar[i], kEpiWarps);
+        for (int i = 0; i < 2 * kEpiWarps; ++i) tzp::mbar_init(&res_bar[i], 1);
         *abort_flag = 0;
         tzp::fence_mbar_init();
         tzp::tma_prefetch_desc(&tmA);
         tzp::tma_prefetch_desc(&tmB);
+        tzp::tma_prefetch_desc(&tmRes);
+        tzp::tma_prefetch_desc(&tmX);
     }
     if (warp == 1) {
         tzp::tmem_alloc(tmem_slot, 512);
@@ -196,29 +206,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rloc = q * 32 + lane;
         const int c0 = slice * kSlice;
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0);
+        uint8_t* box[2] = {staging + e * 2 * kBox, staging + e * 2 * kBox + kBox};
+        uint64_t* rbar = res_bar + 2 * e;
+        uint32_t rph = 0;  // phase bit of rbar[0] (bit 0) and rbar[1] (bit 1)
         uint32_t tphase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int row0 = tile * 128 + q * 32;
+            // residual boxes of chunks 0 and 1 (the boxes' previous TMA stores must have read them)
+            if (lane == 0) {
+                tzp::bulk_wait_read<0>();
+                for (int b = 0; b < 2; ++b) {
+                    tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
+                    tzp::tma_load_2d(box[b], &tmRes, c0 + 16 * b, row0, &rbar[b]);
+                }
+            }
+            __syncwarp();
             if (!tzp::mbar_wait(tfull, tphase, status, abort_flag)) break;
             tzp::tc_fence_after();
             const int row = tile * 128 + rloc;
             const bool ok = row < M;
             const float rs = (p.row_scale && ok) ? p.row_scale[row] : 1.0f;
-            const float* res = p.residual + static_cast<long long>(ok ? row : 0) * kN + c0;
 
             // ---- pass A: x = dequant(acc) + bias + residual -> TMEM; row sum ----
             float sum = 0.f;
-            float4 rb[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) rb[j] = ok ? *reinterpret_cast<const float4*>(res + 4 * j) : make_float4(0, 0, 0, 0);
+            bool bad = false;
 #pragma unroll
             for (int c = 0; c < kSlice / 16; ++c) {
+                const int b = c & 1;
                 uint32_t r[16];
                 tzp::tmem_ld16(tbase + 16 * c, r);
-                float4 cur[4] = {rb[0], rb[1], rb[2], rb[3]};
-                if (c + 1 < kSlice / 16) {
+                if (!tzp::mbar_wait(&rbar[b], (rph >> b) & 1u, status, nullptr)) {
+                    tzp::tmem_ld_wait();
+                    bad = true;
+                    break;
+                }
+                rph ^= 1u << b;
+                float4 cur[4];  // this row's 16 residual values (64-byte swizzle of the TMA box)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        rb[j] = ok ? *reinterpret_cast<const float4*>(res + 16 * (c + 1) + 4 * j) : make_float4(0, 0, 0, 0);
+                for (int j = 0; j < 4; ++j)
+                    cur[j] = *reinterpret_cast<const float4*>(box[b] + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
+                __syncwarp();
+                if (lane == 0 && c + 2 < kSlice / 16) {  // refill this box with chunk c + 2
+                    tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
+                    tzp::tma_load_2d(box[b], &tmRes, c0 + 16 * (c + 2), row0, &rbar[b]);
                 }
                 tzp::tmem_ld_wait();
                 const int col = c0 + 16 * c;
@@ -239,11 +269,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         v[2] = __fmul_rn(v[2], cs.z);
                         v[3] = __fmul_rn(v[3], cs.w);
                     }
-                    const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col + 4 * j));
-                    v[0] = __fadd_rn(__fadd_rn(v[0], b.x), cur[j].x);
-                    v[1] = __fadd_rn(__fadd_rn(v[1], b.y), cur[j].y);
-                    v[2] = __fadd_rn(__fadd_rn(v[2], b.z), cur[j].z);
-                    v[3] = __fadd_rn(__fadd_rn(v[3], b.w), cur[j].w);
+                    const float4 bv = __ldg(reinterpret_cast<const float4*>(p.bias + col + 4 * j));
+                    v[0] = __fadd_rn(__fadd_rn(v[0], bv.x), cur[j].x);
+                    v[1] = __fadd_rn(__fadd_rn(v[1], bv.y), cur[j].y);
+                    v[2] = __fadd_rn(__fadd_rn(v[2], bv.z), cur[j].z);
+                    v[3] = __fadd_rn(__fadd_rn(v[3], bv.w), cur[j].w);
                     sum += (v[0] + v[1]) + (v[2] + v[3]);
                     r[4 * j] = __float_as_uint(v[0]);
                     r[4 * j + 1] = __float_as_uint(v[1]);
@@ -252,6 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tzp::tmem_st16(tbase + 16 * c, r);
             }
+            if (bad) break;
             tzp::tmem_st_wait();
             red_sum[slice * 128 + rloc] = sum;
             if (!epi_sync(&red_bar[0], tphase, lane, status)) break;
@@ -279,7 +310,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             // ---- pass C: normalise, store x_out (+ f16 aux, or y -> TMEM and |max|) ----
             float amax = 0.f;
-            float* xo = p.x_out + static_cast<long long>(row) * kN + c0;
 #pragma unroll
             for (int c = 0; c < kSlice / 16; ++c) {
                 uint32_t r[16];
@@ -296,10 +326,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     y[4 * j + 2] = (__uint_as_float(r[4 * j + 2]) - mean) * inv_std * g.z + bb.z;
                     y[4 * j + 3] = (__uint_as_float(r[4 * j + 3]) - mean) * inv_std * g.w + bb.w;
                 }
-                if (ok) {
+                {  // x_out chunk -> staging box (64-byte swizzle) -> one TMA store (rows >= M are clipped)
+                    const int b = c & 1;
+                    if (lane == 0) tzp::bulk_wait_read<1>();
+                    __syncwarp();
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        *reinterpret_cast<float4*>(xo + 16 * c + 4 * j) = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+                        *reinterpret_cast<float4*>(box[b] + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                            make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+                    tzp::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tzp::tma_store_2d(&tmX, box[b], col, row0);
+                        tzp::bulk_commit();
+                    }
                 }
                 if constexpr (AUX == 0) {
                     if (ok) {
@@ -349,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) tzp::mbar_arrive(tempty);
             tphase ^= 1u;
         }
+        if (lane == 0) tzp::bulk_wait_all();
     }
 
     tzp::pdl_trigger();
@@ -386,11 +427,18 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     rc = encode_tmap_2d(&tb, dtype_of(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.K), kN,
                         static_cast<uint64_t>(g.ldb) * C::ELEM, C::BK, kHalf);
     if (rc) return rc;
+    CUtensorMap tr, tx;
+    rc = encode_tmap_2d_swz(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.residual, kN, static_cast<uint64_t>(g.M), kN * 4, 16, 32,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+    rc = encode_tmap_2d_swz(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.x_out, kN, static_cast<uint64_t>(g.M), kN * 4, 16, 32,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
     LnParams p{g.bias, g.col_scale, g.row_scale, g.residual, g.gamma, g.beta, g.eps, g.x_out, g.aux, g.aux_scale};
     const int tiles = (g.M + 127) / 128;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
-    return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, g.M, g.K, p, ctx->d_status);
+    return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, tr, tx, g.M, g.K, p, ctx->d_status);
 }
 
 }  // namespace
