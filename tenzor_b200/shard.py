@@ -62,3 +62,50 @@ def gather_to_rank0(local: "torch.Tensor", index: np.ndarray, total: int, group=
         keep = ib >= 0
         out[ib[keep]] = b[keep]
     return out
+
+
+class RankGather:
+    """Per-step gather of every rank's [n_r, D] rows to rank 0 in global batch order, with all sizes
+    exchanged once at construction: each step is one torch.distributed.gather of a [cap, D] buffer
+    (cap = the largest shard) and, on rank 0, one row gather that puts rows into batch order.
+
+    `reorder(table, ids, out)` performs that row gather; the bench passes the library's
+    tz_gather_rows, the CPU test a torch index."""
+
+    def __init__(self, index: np.ndarray, total: int, dim: int, device, reorder, group=None):
+        import torch
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        n = torch.tensor([len(index)], device=device, dtype=torch.int64)
+        ns = [torch.zeros_like(n) for _ in range(self.world)]
+        dist.all_gather(ns, n, group=group)
+        self.counts = [int(x.item()) for x in ns]
+        self.cap = max(self.counts)
+        idx = torch.full((self.cap,), -1, device=device, dtype=torch.int64)
+        idx[: len(index)] = torch.as_tensor(index, device=device)
+        allidx = [torch.empty_like(idx) for _ in range(self.world)]
+        dist.all_gather(allidx, idx, group=group)
+        self.total = total
+        self.reorder = reorder
+        self.recv = None
+        if self.rank == 0:
+            flat = torch.cat(allidx).cpu().numpy()
+            perm = np.empty(total, np.int32)
+            for slot, g in enumerate(flat):
+                if g >= 0:
+                    perm[g] = slot
+            self.perm = torch.from_numpy(perm).to(device)
+            self.recv = torch.empty((self.world * self.cap, dim), device=device, dtype=torch.float32)
+            self.recv_views = list(self.recv.view(self.world, self.cap, dim).unbind(0))
+            self.out = torch.empty((total, dim), device=device, dtype=torch.float32)
+
+    def step(self, local_padded):
+        """local_padded: [cap, D] with this rank's rows first.  Returns [total, D] on rank 0."""
+        import torch.distributed as dist
+        dist.gather(local_padded, self.recv_views if self.rank == 0 else None, dst=0, group=self.group)
+        if self.rank == 0:
+            self.reorder(self.recv, self.perm, self.out)
+            return self.out
+        return None

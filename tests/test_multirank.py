@@ -26,7 +26,7 @@ def _worker(rank, world, port, q, fail_rank):
     import torch
     import torch.distributed as dist
     from tenzor_b200 import synthetic as S
-    from tenzor_b200.shard import gather_to_rank0, shard_by_tokens
+    from tenzor_b200.shard import RankGather, gather_to_rank0, shard_by_tokens
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
     try:
@@ -36,7 +36,15 @@ def _worker(rank, world, port, q, fail_rank):
         if rank == fail_rank:
             raise RuntimeError("injected rank failure")
         out = gather_to_rank0(local, mine, len(lens))
+        # the bench's per-step gather: sizes exchanged once, padded buffer, reorder on rank 0
+        rg = RankGather(mine, len(lens), 4, torch.device("cpu"),
+                        lambda table, ids, o: o.copy_(table[ids.long()]))
+        pad = torch.zeros((rg.cap, 4))
+        pad[: len(mine)] = local
+        out2 = rg.step(pad)
+        out3 = rg.step(pad)  # a second step reuses the buffers
         if rank == 0:
+            assert torch.equal(out2, out) and torch.equal(out3, out)
             q.put(("ok", out[:, 0].numpy().tolist()))
     except Exception as e:  # noqa: BLE001
         q.put(("err", f"rank {rank}: {type(e).__name__}: {e}"))
