@@ -93,49 +93,118 @@ def traffic_table():
 
 
 class Clocks:
-    """Samples nvidia-smi every 200 ms while the timed region runs."""
+    """SM clock, power and clock-event reasons sampled DURING the timed region.
+
+    NVML (the library nvidia-smi reads) is polled every ~2 ms from a thread, so even a timed region of
+    a few tens of milliseconds gets samples; `mark()` is called from the timing loop right after the
+    steps are enqueued (the GPU is busy then) and only samples taken between `begin()` and `end()`
+    count.  Falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu: int):
         self.gpu = gpu
-        self.rows = []
+        self.rows = []  # (t, sm_mhz, max_mhz, power_w, [reason names])
+        self.window = []
         self.proc = None
+        self.nv = None
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml as N
+        N.nvmlInit()
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(self.gpu)
+            return N, N.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0")
+        except Exception:
+            return N, N.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _sample_nvml(self):
+        N, h = self.nv
+        r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+        bits = [N.nvmlClocksEventReasonHwSlowdown, N.nvmlClocksEventReasonHwThermalSlowdown,
+                N.nvmlClocksEventReasonSwThermalSlowdown, N.nvmlClocksEventReasonSwPowerCap]
+        self.rows.append((time.perf_counter(), float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)),
+                          float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)),
+                          N.nvmlDeviceGetPowerUsage(h) / 1000.0, [n for n, b in zip(self.NAMES, bits) if r & b]))
+
+    def _poll(self):
+        while not self.stop.is_set():
+            try:
+                self._sample_nvml()
+            except Exception:
+                return
+            time.sleep(0.002)
 
     def __enter__(self):
+        try:
+            self.nv = self._nvml_handle()
+            self._sample_nvml()
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nv = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t = threading.Thread(target=self._read_smi, daemon=True)
             self.t.start()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
-    def _read(self):
+    def _read_smi(self):
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            r = [x.strip() for x in line.split(",")]
+            if len(r) > 8 and r[1].replace(".", "").isdigit():
+                self.rows.append((time.perf_counter(), float(r[1]), float(r[2]) if r[2].replace(".", "").isdigit() else None,
+                                  None, [self.NAMES[i] for i in range(4) if r[5 + i] == "Active"]))
+
+    def begin(self):
+        self.window.append([time.perf_counter(), None])
+
+    def mark(self):
+        """Called while the GPU is busy with the timed steps: one sample inside the window."""
+        if self.nv:
+            try:
+                self._sample_nvml()
+            except Exception:
+                pass
+
+    def end(self):
+        self.window[-1][1] = time.perf_counter()
 
     def __exit__(self, *a):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        elif self.nv:
+            self.t.join(timeout=1)
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+        rows = [r for r in self.rows if any(a <= r[0] <= (b or a) for a, b in self.window)] if self.window else []
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock sample inside the timed region"],
+                    "samples": 0}
+        sm = [r[1] for r in rows]
+        mx = [r[2] for r in rows if r[2]]
+        pw = [r[3] for r in rows if r[3] is not None]
+        reasons = sorted({n for r in rows for n in r[4]})
+        out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+               "samples": len(rows), "source": "nvml" if self.nv else "nvidia-smi"}
+        if pw:
+            out["power_w_median"] = statistics.median(pw)
+        return out
 
 
 def cpu_forward_timing(w_ckpt, ids, lens, mode_name, budget_s=12.0, max_seqs=None):
@@ -277,12 +346,18 @@ def run_ours(a):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        if clk:
+            clk.begin()
         for i in range(a.steps):
             flush.zero_()
             evs[i][0].record(stream)
             step()
             evs[i][1].record(stream)
+        if clk:
+            clk.mark()
         torch.cuda.synchronize()
+        if clk:
+            clk.end()
         if world > 1:
             dist.barrier()
         t = sum(s_.elapsed_time(e_) for s_, e_ in evs)
@@ -293,7 +368,7 @@ def run_ours(a):
 
     # 1) the headline: K steps, nothing but the forward (+ gather) on the stream
     with Clocks(local) as clk:
-        ms = timed_loop()
+        ms = timed_loop(clk)
     # 2) the same K steps with CUDA events recorded between the forward's launches on the launching
     #    stream: per-kernel-class durations for the roofline
     L.check(L.lib().tz_arctic_profile(model.handle, a.steps))

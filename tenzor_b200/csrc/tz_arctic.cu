@@ -1,8 +1,9 @@
 // tz_arctic.cu -- Arctic-embed-xs forward on sm_100a: model kernels (embedding + LayerNorm, per-token
 // requantisation of f16 activations for the W8A8 path, CLS pooling + L2 norm) and the host
 // orchestration behind tz_arctic_*.  Per layer: QKV GEMM (tz_gemm.cu) -> attention
-// (tz_attention.cu) -> [requant] -> output projection + residual + LayerNorm (tz_gemm_ln.cu) ->
-// FFN1 + GELU (tz_gemm.cu) -> [requant] -> FFN2 + residual + LayerNorm (tz_gemm_ln.cu).
+// (tz_attention.cu) -> output projection + residual + LayerNorm (tz_gemm_ln.cu) -> FFN1 + GELU
+// (tz_gemm.cu) -> FFN2 + residual + LayerNorm (tz_gemm_ln.cu).  In W8A8 the f16 attention and GELU
+// outputs carry their row |max| and are quantised per token inside the consuming gemm_ln kernel.
 //
 // Reference call stack replaced (arctic.zig): forward 874-898 -> embeddingsImpl 543-585 ->
 // encoder 830-848 -> transformerBlock 814-826 -> selfAttention 639-747 / feedForward 760-810 ->
@@ -12,8 +13,10 @@
 //   X    f32 [T,384]   residual stream (LayerNorm outputs)
 //   XA   f16 [T,384]   GEMM operand copy of X (F32 / W8A32)   | int8 [T,384] + xs f32 [T] (W8A8)
 //   QKV  f16 [T,1152]  Q | K | V, head h at columns h*32 of each third
-//   OA   f16 [T,384]   attention output (F32 / W8A32)        | int8 + os [T] (W8A8)
-//   H    f16 [T,1536]  GELU(FFN1)                              (+ int8 HQ + hs [T] for W8A8)
+//   OA   f16 [T,384]   attention output (F32 / W8A32); W8A8 writes it into H instead, with its
+//                      row |max| in omax [T]
+//   H    f16 [T,1536]  GELU(FFN1) (+ row |max| in hmax [T] for W8A8)
+// W8A8 keeps no int8 copy of the attention or GELU outputs: the consuming gemm_ln quantises them.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -167,7 +170,7 @@ __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __r
 // accumulated by its producer (GEMM epilogue or attention): s = max/127 (1 if 0),
 // q = clamp(round(x * (1/s))); the row max is reset to 0 for the next producer.  Warp per row.
 __global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsigned* __restrict__ xmax,
-                                    int8_t* __restrict__ q, float* __restrict__ qs, long long rows) {
+                                    int8_t* __restrict__ q, float* __restrict__ qs, long long rows, int reset) {
     tzp::pdl_wait();
     tzp::pdl_trigger();
     const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -192,7 +195,7 @@ __global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsi
     __syncwarp();
     if (lane == 0) {
         qs[row] = sc;
-        xmax[row] = 0u;
+        if (reset) xmax[row] = 0u;
     }
 }
 
@@ -448,14 +451,16 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
     A(sizeof(float) * nb * kH, reinterpret_cast<void**>(&m->out));
     if (m->mode == TZ_QUANT_W8A8) {
         A(T * kH, &m->XA);
-        A(T * kH, &m->OA);
         A(sizeof(float) * T, reinterpret_cast<void**>(&m->xs));
-        A(sizeof(float) * T, reinterpret_cast<void**>(&m->os));
-        A(sizeof(float) * T, reinterpret_cast<void**>(&m->hs));
         A(sizeof(unsigned) * T, reinterpret_cast<void**>(&m->hmax));
         A(sizeof(unsigned) * T, reinterpret_cast<void**>(&m->omax));
         A(sizeof(__half) * T * kF, &m->Hh);
-        A(T * kF, &m->HQ);
+        if (m->keep_stages) {  // int8 copies of the in-kernel-quantised operands, for the parity hook
+            A(T * kH, &m->OA);
+            A(sizeof(float) * T, reinterpret_cast<void**>(&m->os));
+            A(sizeof(float) * T, reinterpret_cast<void**>(&m->hs));
+            A(T * kF, &m->HQ);
+        }
     } else {
         A(sizeof(__half) * T * kH, &m->XA);
         A(sizeof(__half) * T * kH, &m->OA);
@@ -543,24 +548,24 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if ((rc = launch_gemm(ctx, g, s))) return rc;
         if ((rc = prof_mark(m, P_ATTN, s))) return rc;
         // attention
-        // W8A8: the f16 attention output goes through the (still free) H buffer and is requantised
+        // W8A8: the f16 attention output (with each row's |max|) goes through the (still free) H
+        // buffer; the output projection quantises it per token inside its own kernel.
         if ((rc = launch_attention(ctx, m->QKV, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s, pdl)))
             return rc;
-        if (q8) {
-            if ((rc = prof_mark(m, P_QUANT, s))) return rc;
-            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, pdl,
-                                    static_cast<const __half*>(m->Hh), kH, m->omax, static_cast<int8_t*>(m->OA), m->os, T)))
+        if (q8 && l == 0 && m->keep_stages) {  // parity hook only: the same quantisation, kept aside
+            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, false,
+                                    static_cast<const __half*>(m->Hh), kH, m->omax, static_cast<int8_t*>(m->OA), m->os, T, 0)))
                 return rc;
+            if ((rc = keep_operand(m, 1, m->OA, m->os, T, kH, s))) return rc;
         }
         // output projection + bias + residual + LayerNorm in one kernel (arctic.zig:716-746)
         GemmLnArgs o;
         o.pdl = pdl;
         o.kind = g.kind;
-        o.a = m->OA; o.lda = kH; o.b = L.wo; o.ldb = kH; o.M = M; o.K = kH;
-        o.bias = L.bo; o.col_scale = wscale ? L.so : nullptr; o.row_scale = q8 ? m->os : nullptr;
+        o.a = q8 ? m->Hh : m->OA; o.lda = kH; o.b = L.wo; o.ldb = kH; o.M = M; o.K = kH;
+        o.bias = L.bo; o.col_scale = wscale ? L.so : nullptr; o.a_absmax = q8 ? m->omax : nullptr;
         o.residual = m->X; o.gamma = L.ln1g; o.beta = L.ln1b; o.eps = kEps;
         o.x_out = m->X; o.aux = m->XA; o.aux_scale = q8 ? m->xs : nullptr; o.aux_int8 = q8;
-        if (l == 0 && (rc = keep_operand(m, 1, m->OA, m->os, T, kH, s))) return rc;
         if ((rc = prof_mark(m, P_OPROJ, s))) return rc;
         if ((rc = launch_gemm_ln(ctx, o, s))) return rc;
         // FFN1 + bias + GELU
@@ -573,21 +578,21 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if (l == 0 && (rc = keep_operand(m, 2, m->XA, m->xs, T, kH, s))) return rc;
         if ((rc = prof_mark(m, P_FFN1, s))) return rc;
         if ((rc = launch_gemm(ctx, f1, s))) return rc;
-        if (q8) {
-            if ((rc = prof_mark(m, P_QUANT, s))) return rc;
-            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, pdl,
-                                    static_cast<const __half*>(m->Hh), kF, m->hmax, static_cast<int8_t*>(m->HQ), m->hs, T)))
+        if (q8 && l == 0 && m->keep_stages) {  // parity hook only
+            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, false,
+                                    static_cast<const __half*>(m->Hh), kF, m->hmax, static_cast<int8_t*>(m->HQ), m->hs, T, 0)))
                 return rc;
+            if ((rc = keep_operand(m, 3, m->HQ, m->hs, T, kF, s))) return rc;
         }
-        // FFN2 + bias + residual + LayerNorm in one kernel (arctic.zig:779-807)
+        // FFN2 + bias + residual + LayerNorm in one kernel (arctic.zig:779-807); W8A8 quantises the
+        // f16 GELU output per token inside the kernel.
         GemmLnArgs f2;
         f2.pdl = pdl;
         f2.kind = g.kind;
-        f2.a = q8 ? m->HQ : m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.K = kF;
-        f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.row_scale = q8 ? m->hs : nullptr;
+        f2.a = m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.K = kF;
+        f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.a_absmax = q8 ? m->hmax : nullptr;
         f2.residual = m->X; f2.gamma = L.ln2g; f2.beta = L.ln2b; f2.eps = kEps;
         f2.x_out = m->X; f2.aux = m->XA; f2.aux_scale = q8 ? m->xs : nullptr; f2.aux_int8 = q8;
-        if (l == 0 && q8 && (rc = keep_operand(m, 3, m->HQ, m->hs, T, kF, s))) return rc;
         if ((rc = prof_mark(m, P_FFN2, s))) return rc;
         if ((rc = launch_gemm_ln(ctx, f2, s))) return rc;
         if (m->keep_stages)

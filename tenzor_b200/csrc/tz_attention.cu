@@ -10,7 +10,8 @@
 // the sequence and the CTA's Q rows are staged in shared memory with cp.async (16-byte chunks
 // XOR-swizzled so ldmatrix is conflict-free; rows past the sequence are zero-filled).  S = Q K^T and
 // O = P V run on mma.sync m16n8k16 (f16 in, f32 accumulate) with an online softmax over 64-key
-// blocks (exp2 with the 1/sqrt(32)*log2(e) scale folded in); scores never leave registers.  The
+// blocks (exp2 with the 1/sqrt(32)*log2(e) scale folded in); scores never leave registers.  Full
+// 64-key blocks run unmasked; the ragged last block runs at 16-key granularity with the key mask.  The
 // f16 output goes straight to global memory; for the W8A8 path each row's |max| over the 12 heads
 // is accumulated with atomicMax for the per-token requantisation that follows.
 #include <cuda_fp16.h>
@@ -30,7 +31,85 @@ __device__ __forceinline__ uint32_t kv_off(int row, int chunk) {
     return static_cast<uint32_t>(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
 }
 
-__global__ void __launch_bounds__(128)
+// One block of keys [kb, kb + 16*NCH) for the warp's 16 query rows: S = Q K^T on the tensor cores,
+// the online-softmax update, then O += P V.  MASK = the block runs past the sequence's last key.
+// Scores stay in raw units (m0/m1 are raw maxima); the 1/sqrt(32)*log2(e) scale and the max are
+// applied by one FMA inside the exponent, which is exact in order: the scale is positive.
+template <int NCH, bool MASK>
+__device__ __forceinline__ void attend_block(int kb, int L, uint32_t kaddr, uint32_t vaddr, const uint32_t (&qa)[2][4],
+                                             float (&o)[4][4], float& m0, float& m1, float& l0, float& l1, int lane) {
+    constexpr float sl2 = 0.17677669529663687f * 1.4426950408889634f;  // 1/sqrt(32) * log2(e)
+    const int cq = 2 * (lane & 3);
+    const int mi = lane >> 3;
+    float s[2 * NCH][4];
+#pragma unroll
+    for (int j = 0; j < 2 * NCH; ++j) {
+        s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        uint32_t bk[4];
+        tzp::ldmatrix_x4(bk, kaddr + kv_off(kb + 8 * j + (lane & 7), mi));
+        tzp::mma_f16_16816(s[j], qa[0], bk[0], bk[1]);
+        tzp::mma_f16_16816(s[j], qa[1], bk[2], bk[3]);
+    }
+    if (MASK) {
+#pragma unroll
+        for (int j = 0; j < 2 * NCH; ++j) {
+            const int key = kb + 8 * j + cq;
+            if (key >= L) s[j][0] = s[j][2] = -INFINITY;
+            if (key + 1 >= L) s[j][1] = s[j][3] = -INFINITY;
+        }
+    }
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int j = 0; j < 2 * NCH; ++j) {
+        mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float al0 = tzp::ex2_approx((m0 - mx0) * sl2), al1 = tzp::ex2_approx((m1 - mx1) * sl2);
+    const float nb0 = -mx0 * sl2, nb1 = -mx1 * sl2;
+    m0 = mx0;
+    m1 = mx1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2 * NCH; ++j) {
+        s[j][0] = tzp::ex2_approx(fmaf(s[j][0], sl2, nb0));
+        s[j][1] = tzp::ex2_approx(fmaf(s[j][1], sl2, nb0));
+        s[j][2] = tzp::ex2_approx(fmaf(s[j][2], sl2, nb1));
+        s[j][3] = tzp::ex2_approx(fmaf(s[j][3], sl2, nb1));
+        ps0 += s[j][0] + s[j][1];
+        ps1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        o[i][0] *= al0;
+        o[i][1] *= al0;
+        o[i][2] *= al1;
+        o[i][3] *= al1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < NCH; ++kk) {
+        uint32_t a[4];
+        a[0] = tzp::pack_half2(s[2 * kk][0], s[2 * kk][1]);
+        a[1] = tzp::pack_half2(s[2 * kk][2], s[2 * kk][3]);
+        a[2] = tzp::pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        a[3] = tzp::pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+        for (int jd = 0; jd < 2; ++jd) {
+            uint32_t bv[4];
+            tzp::ldmatrix_x4_trans(bv, vaddr + kv_off(kb + 16 * kk + (mi & 1) * 8 + (lane & 7), 2 * jd + (mi >> 1)));
+            tzp::mma_f16_16816(o[2 * jd], a, bv[0], bv[1]);
+            tzp::mma_f16_16816(o[2 * jd + 1], a, bv[2], bv[3]);
+        }
+    }
+}
+
+// 86 registers unbounded (5 CTAs = 20 warps per SM); capped for 7 CTAs per SM.
+__global__ void __launch_bounds__(128, 7)
     attention_kernel(const __half* __restrict__ qkv, const int* __restrict__ cu_seqlens, int lpad,
                      __half* __restrict__ out, unsigned* __restrict__ row_absmax) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -47,7 +126,7 @@ __global__ void __launch_bounds__(128)
     uint8_t* ks = sm;
     uint8_t* vs = sm + kv_bytes;
     uint8_t* qs = sm + 2 * kv_bytes;
-    const int nkeys = (L + 63) & ~63;  // keys staged (zero-filled past L)
+    const int nkeys = (L + 15) & ~15;  // keys staged (zero-filled past L up to the 16-key chunk)
     for (int i = tid; i < nkeys * 4; i += 128) {
         const int key = i >> 2, c = i & 3;
         const bool ok = key < L;
@@ -68,7 +147,6 @@ __global__ void __launch_bounds__(128)
     if (q0 + warp * 16 >= L) return;  // no further block-wide synchronisation below
 
     const uint32_t kaddr = tzp::smem_u32(ks), vaddr = tzp::smem_u32(vs), qaddr = tzp::smem_u32(qs);
-    const float sl2 = 0.17677669529663687f * 1.4426950408889634f;  // 1/sqrt(32) * log2(e)
     const int cq = 2 * (lane & 3);
     const int mi = lane >> 3;
 
@@ -82,69 +160,14 @@ __global__ void __launch_bounds__(128)
     for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-    for (int kb = 0; kb < L; kb += 64) {
-        float s[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-            uint32_t bk[4];
-            tzp::ldmatrix_x4(bk, kaddr + kv_off(kb + 8 * j + (lane & 7), mi));
-            tzp::mma_f16_16816(s[j], qa[0], bk[0], bk[1]);
-            tzp::mma_f16_16816(s[j], qa[1], bk[2], bk[3]);
-        }
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int key = kb + 8 * j + cq;
-            s[j][0] = key < L ? s[j][0] * sl2 : -INFINITY;
-            s[j][1] = key + 1 < L ? s[j][1] * sl2 : -INFINITY;
-            s[j][2] = key < L ? s[j][2] * sl2 : -INFINITY;
-            s[j][3] = key + 1 < L ? s[j][3] * sl2 : -INFINITY;
-            mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
-            mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
-        }
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-        m0 = mn0;
-        m1 = mn1;
-        float ps0 = 0.f, ps1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            s[j][0] = exp2f(s[j][0] - mn0);
-            s[j][1] = exp2f(s[j][1] - mn0);
-            s[j][2] = exp2f(s[j][2] - mn1);
-            s[j][3] = exp2f(s[j][3] - mn1);
-            ps0 += s[j][0] + s[j][1];
-            ps1 += s[j][2] + s[j][3];
-        }
-        l0 = l0 * al0 + ps0;
-        l1 = l1 * al1 + ps1;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            o[i][0] *= al0;
-            o[i][1] *= al0;
-            o[i][2] *= al1;
-            o[i][3] *= al1;
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t a[4];
-            a[0] = tzp::pack_half2(s[2 * kk][0], s[2 * kk][1]);
-            a[1] = tzp::pack_half2(s[2 * kk][2], s[2 * kk][3]);
-            a[2] = tzp::pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-            a[3] = tzp::pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-            for (int jd = 0; jd < 2; ++jd) {
-                uint32_t bv[4];
-                tzp::ldmatrix_x4_trans(bv, vaddr + kv_off(kb + 16 * kk + (mi & 1) * 8 + (lane & 7), 2 * jd + (mi >> 1)));
-                tzp::mma_f16_16816(o[2 * jd], a, bv[0], bv[1]);
-                tzp::mma_f16_16816(o[2 * jd + 1], a, bv[2], bv[3]);
-            }
-        }
+    int kb = 0;
+    for (; kb + 64 <= L; kb += 64) attend_block<4, false>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane);
+    switch ((L - kb + 15) >> 4) {  // the ragged tail, in 16-key chunks
+        case 1: attend_block<1, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        case 2: attend_block<2, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        case 3: attend_block<3, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        case 4: attend_block<4, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        default: break;
     }
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);

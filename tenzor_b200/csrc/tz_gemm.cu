@@ -287,7 +287,18 @@ __device__ __forceinline__ void stage_chunk(const EpiParams& ep, uint32_t buf, i
     }
 }
 
-template <int KIND, int BN, int STAGES, int EPI_WARPS>
+// Flags of the specialised epilogue (FAST != 0): f16 output through TMA, full column tiles, bias,
+// no residual / op chain.  Everything else takes the general epilogue (FAST == 0).
+constexpr int F_ON = 1, F_GELU = 2, F_AMAX = 4, F_RSCALE = 8, F_CSCALE = 16;
+
+__device__ __forceinline__ float gelu_fast2(float x) {
+    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) with the cubic as x (k0 + k1 x^2)
+    const float inner = x * fmaf(0.7978845608f * 0.044715f, x * x, 0.7978845608f);
+    const float hx = 0.5f * x;
+    return fmaf(hx, tzp::tanh_approx(inner), hx);
+}
+
+template <int KIND, int BN, int STAGES, int EPI_WARPS, int FAST>
 __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, int M, int N, int K, EpiParams ep, int use_tma_store,
@@ -410,6 +421,119 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             tzp::umma_commit(drain);
             tzp::mbar_wait(drain, 0, status, nullptr);
         }
+    } else if constexpr (FAST != 0) {
+        // ---- specialised epilogue: straight-line code per tile ----
+        // Per tile, before the accumulator is ready: this row's scale and the slice's bias / column
+        // scales (into this warp's staging area, read back as broadcasts).  Then the NCH chunks of
+        // 16 columns: TMEM load of chunk c+1 in flight while chunk c is converted and staged; the
+        // accumulator is released as soon as its last chunk is in registers; one proxy fence and NCH
+        // TMA stores per tile.  |max| is taken on the f32 values (f16 rounding is monotonic, so the
+        // f16 of the max equals the max of the f16 values).
+        constexpr int CPW = C::COLS_PER_WARP;
+        constexpr int NCH = CPW / CW;
+        constexpr int BOX = 32 * CW * 2;  // one 32 x 16 f16 box
+        static_assert(NCH * BOX + 2 * CPW * 4 <= 2 * C::EPI_BUF, "fast epilogue staging");
+        const int e = warp - 2;
+        const int q = warp & 3;
+        const int slice = e >> 2;
+        uint8_t* wst = staging + e * 2 * C::EPI_BUF;
+        float* cvb = reinterpret_cast<float*>(wst + NCH * BOX);
+        float* cvs = cvb + CPW;
+        const uint32_t wst_a = tzp::smem_u32(wst);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int m0 = (tile / n_tiles) * 128;
+            const int n0 = (tile % n_tiles) * BN;
+            const int row0 = m0 + q * 32;
+            const int row = row0 + lane;
+            const bool row_ok = row < M;
+            const int cbase = n0 + slice * CPW;
+            float rs = 1.0f;
+            if constexpr ((FAST & F_RSCALE) != 0) rs = row_ok ? __ldg(ep.row_scale + row) : 1.0f;
+            if (lane == 0) tzp::bulk_wait_read<0>();  // the previous tile's stores have read the boxes
+            for (int i = lane; i < CPW; i += 32) {
+                cvb[i] = __ldg(ep.bias + cbase + i);
+                if constexpr ((FAST & (F_RSCALE | F_CSCALE)) != 0) cvs[i] = __ldg(ep.col_scale + cbase + i);
+            }
+            __syncwarp();
+            if (!tzp::mbar_wait(&tfull[acc], acc_phase, status, abort_flag)) break;
+            tzp::tc_fence_after();
+            const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + slice * CPW);
+            uint32_t ra[CW], rb[CW];
+            tzp::tmem_ld16(tcol, ra);
+            tzp::tmem_ld_wait();
+            float amax = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                uint32_t(&cur)[CW] = (c & 1) ? rb : ra;
+                uint32_t(&nxt)[CW] = (c & 1) ? ra : rb;
+                if (c + 1 < NCH) {
+                    tzp::tmem_ld16(tcol + 16 * (c + 1), nxt);
+                } else {  // every TMEM load of this tile has completed: release the accumulator
+                    tzp::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tzp::mbar_arrive(&tempty[acc]);
+                }
+                float v[CW];
+#pragma unroll
+                for (int j = 0; j < CW; ++j) {
+                    if constexpr (KIND == KIND_I8)
+                        v[j] = __int2float_rn(static_cast<int>(cur[j]));
+                    else
+                        v[j] = __uint_as_float(cur[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < CW; j += 4) {
+                    const float4 b = *reinterpret_cast<const float4*>(cvb + 16 * c + j);
+                    if constexpr ((FAST & F_RSCALE) != 0) {
+                        const float4 cs = *reinterpret_cast<const float4*>(cvs + 16 * c + j);
+                        v[j] = __fmul_rn(v[j], __fmul_rn(rs, cs.x));
+                        v[j + 1] = __fmul_rn(v[j + 1], __fmul_rn(rs, cs.y));
+                        v[j + 2] = __fmul_rn(v[j + 2], __fmul_rn(rs, cs.z));
+                        v[j + 3] = __fmul_rn(v[j + 3], __fmul_rn(rs, cs.w));
+                    } else if constexpr ((FAST & F_CSCALE) != 0) {
+                        const float4 cs = *reinterpret_cast<const float4*>(cvs + 16 * c + j);
+                        v[j] = __fmul_rn(v[j], cs.x);
+                        v[j + 1] = __fmul_rn(v[j + 1], cs.y);
+                        v[j + 2] = __fmul_rn(v[j + 2], cs.z);
+                        v[j + 3] = __fmul_rn(v[j + 3], cs.w);
+                    }
+                    v[j] = __fadd_rn(v[j], b.x);
+                    v[j + 1] = __fadd_rn(v[j + 1], b.y);
+                    v[j + 2] = __fadd_rn(v[j + 2], b.z);
+                    v[j + 3] = __fadd_rn(v[j + 3], b.w);
+                }
+#pragma unroll
+                for (int j = 0; j < CW; ++j) {
+                    if constexpr ((FAST & F_GELU) != 0) v[j] = gelu_fast2(v[j]);
+                    if constexpr ((FAST & F_AMAX) != 0) amax = fmaxf(amax, fabsf(v[j]));
+                }
+                const uint32_t buf = wst_a + static_cast<uint32_t>(c * BOX);
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const uint32_t a = buf + lane * 32 + ((u ^ ((lane >> 2) & 1)) << 4);
+                    tzp::st_shared_v4(a, tzp::pack_half2(v[8 * u], v[8 * u + 1]), tzp::pack_half2(v[8 * u + 2], v[8 * u + 3]),
+                                      tzp::pack_half2(v[8 * u + 4], v[8 * u + 5]), tzp::pack_half2(v[8 * u + 6], v[8 * u + 7]));
+                }
+                if (c + 1 < NCH) tzp::tmem_ld_wait();
+            }
+            tzp::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+#pragma unroll
+                for (int c = 0; c < NCH; ++c) tzp::tma_store_2d(&tmOut, wst + c * BOX, cbase + 16 * c, row0);
+                tzp::bulk_commit();
+            }
+            if constexpr ((FAST & F_AMAX) != 0) {
+                if (row_ok) atomicMax(ep.row_absmax + row, __float_as_uint(__half2float(__float2half_rn(amax))));
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (lane == 0) tzp::bulk_wait_all();
     } else {
         // ---- epilogue warps: warp e reads TMEM lane quarter (warp % 4), column slice e / 4 ----
         const int e = warp - 2;
@@ -491,10 +615,10 @@ CUtensorMapDataType tmap_dtype(int kind) {
     }
 }
 
-template <int KIND, int BN, int STAGES, int EPI_WARPS>
+template <int KIND, int BN, int STAGES, int EPI_WARPS, int FAST = 0>
 int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     using C = Cfg<KIND, BN, STAGES, EPI_WARPS>;
-    auto kern = gemm_tc_kernel<KIND, BN, STAGES, EPI_WARPS>;
+    auto kern = gemm_tc_kernel<KIND, BN, STAGES, EPI_WARPS, FAST>;
     static unsigned attr_set = 0;  // one bit per device
     int dev = 0;
     TZ_CUDA(cudaGetDevice(&dev));
@@ -543,6 +667,7 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     } else {
         to = tb;  // unused
     }
+    if (FAST != 0 && !use_tma) return fail(TZ_EINVAL, "gemm: specialised epilogue without TMA store");
     const int n_tiles = (g.N + BN - 1) / BN;
     const int tiles = ((g.M + 127) / 128) * n_tiles;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
@@ -563,6 +688,40 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     TZ_CHECK(reinterpret_cast<uintptr_t>(g.a) % 16 == 0 && reinterpret_cast<uintptr_t>(g.b) % 16 == 0,
              TZ_EINVAL, "gemm: operands must be 16-byte aligned");
     TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm: row_scale needs col_scale");
+    // The specialised epilogue: f16 output with 16-byte aligned rows, N a multiple of 192, bias,
+    // optional row/column dequantisation scales, optional GELU (tanh form) and row |max|.
+    const bool fast = (g.kind == KIND_I8 || g.kind == KIND_F16) && g.out_type == OUT_F16 && g.N % 192 == 0 && g.bias &&
+                      !g.residual && g.n_ops < 0 && (g.gelu == 0 || g.gelu == 1) &&
+                      reinterpret_cast<uintptr_t>(g.out) % 16 == 0 && (g.ldo * 2) % 16 == 0;
+    if (fast) {
+        const int f = F_ON | (g.gelu == 1 ? F_GELU : 0) | (g.row_absmax ? F_AMAX : 0) |
+                      (g.row_scale ? F_RSCALE : (g.col_scale ? F_CSCALE : 0));
+#define TZ_FAST_CASE(K_, F_) \
+    case F_: return launch_impl<K_, 192, 4, 16, F_>(ctx, g, s);
+#define TZ_FAST_KIND(K_)                                                                                       \
+    switch (f) {                                                                                               \
+        TZ_FAST_CASE(K_, F_ON)                                                                                 \
+        TZ_FAST_CASE(K_, F_ON | F_GELU)                                                                        \
+        TZ_FAST_CASE(K_, F_ON | F_AMAX)                                                                        \
+        TZ_FAST_CASE(K_, F_ON | F_GELU | F_AMAX)                                                               \
+        TZ_FAST_CASE(K_, F_ON | F_CSCALE)                                                                      \
+        TZ_FAST_CASE(K_, F_ON | F_CSCALE | F_GELU)                                                             \
+        TZ_FAST_CASE(K_, F_ON | F_CSCALE | F_AMAX)                                                             \
+        TZ_FAST_CASE(K_, F_ON | F_CSCALE | F_GELU | F_AMAX)                                                    \
+        TZ_FAST_CASE(K_, F_ON | F_RSCALE)                                                                      \
+        TZ_FAST_CASE(K_, F_ON | F_RSCALE | F_GELU)                                                             \
+        TZ_FAST_CASE(K_, F_ON | F_RSCALE | F_AMAX)                                                             \
+        TZ_FAST_CASE(K_, F_ON | F_RSCALE | F_GELU | F_AMAX)                                                    \
+        default: break;                                                                                        \
+    }
+        if (g.kind == KIND_I8) {
+            TZ_FAST_KIND(KIND_I8)
+        } else {
+            TZ_FAST_KIND(KIND_F16)
+        }
+#undef TZ_FAST_KIND
+#undef TZ_FAST_CASE
+    }
     switch (g.kind) {
         // BN = 192 when it divides N (every Arctic projection: 384, 1152, 1536): 25% more output per
         // byte of A staged than BN = 128, and no partial tiles.

@@ -45,6 +45,9 @@ struct LnParams {
     float* x_out;
     void* aux;
     float* aux_scale;
+    const __half* a16;    // AQ: f16 A [M, K]
+    long long lda16;
+    unsigned* a_absmax;   // AQ: per-row |max| bits of A
 };
 
 template <int KIND>
@@ -76,7 +79,12 @@ __device__ __forceinline__ float acc_to_f(uint32_t r) {
         return __uint_as_float(r);
 }
 
-template <int KIND, int AUX>
+// AQ = 1: the A operand arrives as f16 rows with their |max| and the epilogue warps quantise it into
+// the int8 stages (per-token W8A8 scale s = |max| / 127, or 1 for an all-zero row; q = clamp(round(x /
+// s))) while the producer streams only W: no separate requantisation pass over A.  The epilogue
+// warps are otherwise idle during the mainloop (one TMEM accumulator: the MMAs of the next tile wait
+// for this tile's epilogue anyway).
+template <int KIND, int AUX, int AQ>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmX, int M, int K,
@@ -96,7 +104,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* drain = tempty + 1;
     uint64_t* red_bar = drain + 1;  // [3]: the epilogue warps' row reductions (sum, ssq, max)
     uint64_t* res_bar = red_bar + 3;  // [16 warps][2 boxes]: residual tile arrivals
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 2 * kEpiWarps);
+    uint64_t* afull = res_bar + 2 * kEpiWarps;  // [kStages] (AQ): A stage quantised by all epilogue threads
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afull + kStages);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -111,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tzp::mbar_init(drain, 1);
         for (int i = 0; i < 3; ++i) tzp::mbar_init(&red_bar[i], kEpiWarps);
         for (int i = 0; i < 2 * kEpiWarps; ++i) tzp::mbar_init(&res_bar[i], 1);
+        for (int s = 0; s < kStages; ++s) tzp::mbar_init(&afull[s], 32 * kEpiWarps);
         *abort_flag = 0;
         tzp::fence_mbar_init();
         tzp::tma_prefetch_desc(&tmA);
@@ -143,8 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
-                    tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-                    tzp::tma_load_2d(sa, &tmA, kb * C::BK, tile * 128, &full[stage]);
+                    tzp::mbar_arrive_expect_tx(&full[stage], AQ ? C::B_BYTES : C::STAGE_BYTES);
+                    if constexpr (!AQ) tzp::tma_load_2d(sa, &tmA, kb * C::BK, tile * 128, &full[stage]);
                     tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, 0, &full[stage]);
                     tzp::tma_load_2d(sa + C::A_BYTES + kHalf * 128, &tmB, kb * C::BK, kHalf, &full[stage]);
                     armed |= 1u << stage;
@@ -171,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tzp::tc_fence_after();
                 bool ok = true;
                 for (int kb = 0; kb < kblocks; ++kb) {
-                    if (!tzp::mbar_wait(&full[stage], phase, status, abort_flag)) {
+                    if (!tzp::mbar_wait(&full[stage], phase, status, abort_flag) ||
+                        (AQ && !tzp::mbar_wait(&afull[stage], phase, status, abort_flag))) {
                         ok = false;
                         break;
                     }
@@ -210,6 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t* rbar = res_bar + 2 * e;
         uint32_t rph = 0;  // phase bit of rbar[0] (bit 0) and rbar[1] (bit 1)
         uint32_t tphase = 0;
+        int cstage = 0;  // AQ: the A stages this thread quantises, in the MMA's order
+        uint32_t cphase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int row0 = tile * 128 + q * 32;
             // residual boxes of chunks 0 and 1 (the boxes' previous TMA stores must have read them)
@@ -221,11 +234,79 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             __syncwarp();
+            if constexpr (AQ) {
+                // ---- quantise this tile's A rows into the int8 stages ----
+                // Thread t: row t / 4 of the tile, 32 columns (64 bytes of f16) at (t % 4) * 32 of
+                // each 128-column K block; writes two 16-byte chunks of the SWIZZLE_128B row
+                // (chunk c of row r at c ^ (r % 8)).  The next K block's loads are in flight while
+                // this one is converted.
+                const int t = threadIdx.x - 64;
+                const int crow = t >> 2, qq = t & 3;
+                const int grow = tile * 128 + crow;
+                const bool cok = grow < M;
+                float inv = 1.0f;
+                if (cok) {
+                    const float mx = __uint_as_float(p.a_absmax[grow]);
+                    const float sc = (mx == 0.0f) ? 1.0f : __fdiv_rn(mx, 127.0f);
+                    inv = __fdiv_rn(1.0f, sc);
+                }
+                const uint4* src = reinterpret_cast<const uint4*>(p.a16 + static_cast<long long>(cok ? grow : 0) * p.lda16 + qq * 32);
+                uint4 x[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) x[i] = cok ? __ldcs(src + i) : make_uint4(0, 0, 0, 0);
+                bool cbad = false;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    uint4 nx[4];
+                    if (kb + 1 < kblocks) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) nx[i] = cok ? __ldcs(src + (kb + 1) * 16 + i) : make_uint4(0, 0, 0, 0);
+                    }
+                    int got = 1;
+                    if (lane == 0) got = tzp::mbar_wait(&empty[cstage], cphase ^ 1u, status, abort_flag) ? 1 : 0;
+                    got = __shfl_sync(0xffffffffu, got, 0);
+                    if (!got) {
+                        cbad = true;
+                        break;
+                    }
+                    uint32_t w[8];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __half2* hp = reinterpret_cast<const __half2*>(&x[i]);
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            const float2 f0 = __half22float2(hp[2 * j]);
+                            const float2 f1 = __half22float2(hp[2 * j + 1]);
+                            w[2 * i + j] = static_cast<uint32_t>(static_cast<uint8_t>(quant1(f0.x, inv))) |
+                                           (static_cast<uint32_t>(static_cast<uint8_t>(quant1(f0.y, inv))) << 8) |
+                                           (static_cast<uint32_t>(static_cast<uint8_t>(quant1(f1.x, inv))) << 16) |
+                                           (static_cast<uint32_t>(static_cast<uint8_t>(quant1(f1.y, inv))) << 24);
+                        }
+                    }
+                    const uint32_t rowa = tzp::smem_u32(smem + cstage * C::STAGE_BYTES) + static_cast<uint32_t>(crow * 128);
+                    tzp::st_shared_v4(rowa + (static_cast<uint32_t>((2 * qq) ^ (crow & 7)) << 4), w[0], w[1], w[2], w[3]);
+                    tzp::st_shared_v4(rowa + (static_cast<uint32_t>((2 * qq + 1) ^ (crow & 7)) << 4), w[4], w[5], w[6], w[7]);
+                    tzp::fence_proxy_async();
+                    tzp::mbar_arrive(&afull[cstage]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) x[i] = nx[i];
+                    if (++cstage == kStages) {
+                        cstage = 0;
+                        cphase ^= 1u;
+                    }
+                }
+                if (cbad) break;
+            }
             if (!tzp::mbar_wait(tfull, tphase, status, abort_flag)) break;
             tzp::tc_fence_after();
             const int row = tile * 128 + rloc;
             const bool ok = row < M;
-            const float rs = (p.row_scale && ok) ? p.row_scale[row] : 1.0f;
+            float rs = (p.row_scale && ok) ? p.row_scale[row] : 1.0f;
+            if constexpr (AQ) {
+                if (ok) {
+                    const float mx = __uint_as_float(p.a_absmax[row]);
+                    rs = (mx == 0.0f) ? 1.0f : __fdiv_rn(mx, 127.0f);
+                }
+            }
 
             // ---- pass A: x = dequant(acc) + bias + residual -> TMEM; row sum ----
             float sum = 0.f;
@@ -256,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 4; ++j) {
                     float v[4] = {acc_to_f<KIND>(r[4 * j]), acc_to_f<KIND>(r[4 * j + 1]), acc_to_f<KIND>(r[4 * j + 2]),
                                   acc_to_f<KIND>(r[4 * j + 3])};
-                    if (p.row_scale) {
+                    if (AQ || p.row_scale) {
                         const float4 cs = __ldg(reinterpret_cast<const float4*>(p.col_scale + col + 4 * j));
                         v[0] = __fmul_rn(v[0], __fmul_rn(rs, cs.x));
                         v[1] = __fmul_rn(v[1], __fmul_rn(rs, cs.y));
@@ -384,6 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (ok && slice == 0) p.aux_scale[row] = sc;
             }
+            if constexpr (AQ) {
+                if (ok && slice == 0) p.a_absmax[row] = 0u;  // every reader of this row's |max| is done
+            }
             tzp::tc_fence_before();
             __syncwarp();
             if (lane == 0) tzp::mbar_arrive(tempty);
@@ -409,10 +493,10 @@ CUtensorMapDataType dtype_of(int kind) {
                                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-template <int KIND, int AUX>
+template <int KIND, int AUX, int AQ = 0>
 int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     using C = LnCfg<KIND>;
-    auto kern = gemm_ln_kernel<KIND, AUX>;
+    auto kern = gemm_ln_kernel<KIND, AUX, AQ>;
     static unsigned attr_set = 0;
     int dev = 0;
     TZ_CUDA(cudaGetDevice(&dev));
@@ -421,9 +505,12 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
         attr_set |= 1u << (dev & 31);
     }
     CUtensorMap ta, tb;
-    int rc = encode_tmap_2d(&ta, dtype_of(KIND), C::ELEM, g.a, static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M),
+    int rc = TZ_OK;
+    if (!AQ) {
+        rc = encode_tmap_2d(&ta, dtype_of(KIND), C::ELEM, g.a, static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M),
                             static_cast<uint64_t>(g.lda) * C::ELEM, C::BK, 128);
-    if (rc) return rc;
+        if (rc) return rc;
+    }
     rc = encode_tmap_2d(&tb, dtype_of(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.K), kN,
                         static_cast<uint64_t>(g.ldb) * C::ELEM, C::BK, kHalf);
     if (rc) return rc;
@@ -434,7 +521,9 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     rc = encode_tmap_2d_swz(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.x_out, kN, static_cast<uint64_t>(g.M), kN * 4, 16, 32,
                             CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
-    LnParams p{g.bias, g.col_scale, g.row_scale, g.residual, g.gamma, g.beta, g.eps, g.x_out, g.aux, g.aux_scale};
+    if (AQ) ta = tb;  // unused: A arrives through the epilogue warps
+    LnParams p{g.bias, g.col_scale, g.row_scale, g.residual, g.gamma, g.beta, g.eps, g.x_out, g.aux, g.aux_scale,
+               AQ ? static_cast<const __half*>(g.a) : nullptr, g.lda, g.a_absmax};
     const int tiles = (g.M + 127) / 128;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
@@ -449,6 +538,13 @@ int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     TZ_CHECK(g.a && g.b && g.bias && g.residual && g.gamma && g.beta && g.x_out && g.aux, TZ_EINVAL, "gemm_ln: null operand");
     TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm_ln: row_scale needs col_scale");
     TZ_CHECK(g.aux_int8 == (g.aux_scale != nullptr), TZ_EINVAL, "gemm_ln: int8 aux needs its scale vector");
+    if (g.a_absmax) {
+        TZ_CHECK(g.kind == KIND_I8 && g.aux_int8 && !g.row_scale && g.col_scale, TZ_EINVAL,
+                 "gemm_ln: in-kernel A quantisation needs the int8 kind, int8 aux, column scales and no row scales");
+        TZ_CHECK(g.K % 128 == 0 && g.lda % 8 == 0 && reinterpret_cast<uintptr_t>(g.a) % 16 == 0, TZ_EINVAL,
+                 "gemm_ln: in-kernel A quantisation needs K %% 128 == 0 and 16-byte aligned f16 rows (K=%d)", g.K);
+        return launch_ln_impl<KIND_I8, 1, 1>(ctx, g, s);
+    }
     if (g.kind == KIND_I8) return g.aux_int8 ? launch_ln_impl<KIND_I8, 1>(ctx, g, s) : launch_ln_impl<KIND_I8, 0>(ctx, g, s);
     if (g.kind == KIND_F16) return g.aux_int8 ? launch_ln_impl<KIND_F16, 1>(ctx, g, s) : launch_ln_impl<KIND_F16, 0>(ctx, g, s);
     return fail(TZ_EUNSUPPORTED, "gemm_ln: kind %d", g.kind);

@@ -130,6 +130,11 @@ struct GemmLnArgs {
     void* aux = nullptr;               // [M, 384] f16 or int8
     float* aux_scale = nullptr;        // [M] when aux is int8
     bool aux_int8 = false;
+    // W8A8 with the A operand quantised inside the kernel: `a` is then f16 [M, K] (row stride lda)
+    // and a_absmax [M] holds each row's |max| (float bits, accumulated by the producer with
+    // atomicMax); the kernel derives the per-token scale from it, quantises A into its int8 stages
+    // and resets a_absmax[row] to 0 once the row is done.  kind must be KIND_I8, row_scale null.
+    unsigned* a_absmax = nullptr;
     bool pdl = false;
 };
 int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s);
