@@ -35,8 +35,8 @@
 #include "tz_rowops.cuh"
 
 namespace tz {
-int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int batch, int max_len, void* out,
-                     unsigned* row_absmax, cudaStream_t s, bool pdl);
+int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const int* cu_seqlens, int batch, int max_len,
+                     void* out, unsigned* row_absmax, cudaStream_t s, bool pdl);
 int launch_f32_to_f16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s);
 int launch_i8_to_f16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s);
 int launch_f16bits_to_f32(tz_ctx_t ctx, const uint16_t* x, float* y, long long n, cudaStream_t s);
@@ -92,10 +92,8 @@ __device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __res
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             const int col = c * 128 + lane * 4;
-            uint32_t w = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) w |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(v[4 * c + i], inv))) << (8 * i);
-            *reinterpret_cast<uint32_t*>(a + col) = w;
+            *reinterpret_cast<uint32_t*>(a + col) = pack_q4(quant1_bits(v[4 * c], inv), quant1_bits(v[4 * c + 1], inv),
+                                                            quant1_bits(v[4 * c + 2], inv), quant1_bits(v[4 * c + 3], inv));
         }
         if (lane == 0) aux_s[row] = sc;
     }
@@ -184,12 +182,10 @@ __global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsi
     for (int col = lane * 8; col < cols; col += 256) {
         const uint4 raw = *reinterpret_cast<const uint4*>(xr + col);
         const __half* hv = reinterpret_cast<const __half*>(&raw);
-        uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            w0 |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(__half2float(hv[i]), inv))) << (8 * i);
-            w1 |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(__half2float(hv[i + 4]), inv))) << (8 * i);
-        }
+        const uint32_t w0 = pack_q4(quant1_bits(__half2float(hv[0]), inv), quant1_bits(__half2float(hv[1]), inv),
+                                    quant1_bits(__half2float(hv[2]), inv), quant1_bits(__half2float(hv[3]), inv));
+        const uint32_t w1 = pack_q4(quant1_bits(__half2float(hv[4]), inv), quant1_bits(__half2float(hv[5]), inv),
+                                    quant1_bits(__half2float(hv[6]), inv), quant1_bits(__half2float(hv[7]), inv));
         *reinterpret_cast<uint2*>(qr + col) = make_uint2(w0, w1);
     }
     __syncwarp();
@@ -550,7 +546,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         // attention
         // W8A8: the f16 attention output (with each row's |max|) goes through the (still free) H
         // buffer; the output projection quantises it per token inside its own kernel.
-        if ((rc = launch_attention(ctx, m->QKV, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s, pdl)))
+        if ((rc = launch_attention(ctx, m->QKV, T, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s, pdl)))
             return rc;
         if (q8 && l == 0 && m->keep_stages) {  // parity hook only: the same quantisation, kept aside
             if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, false,

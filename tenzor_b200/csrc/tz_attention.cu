@@ -7,8 +7,9 @@
 // the masked-batch form with key mask = (position < length).
 //
 // CTA = (64-query block, head, sequence); 4 warps x 16 query rows.  K_h and V_h for every key of
-// the sequence and the CTA's Q rows are staged in shared memory with cp.async (16-byte chunks
-// XOR-swizzled so ldmatrix is conflict-free; rows past the sequence are zero-filled).  S = Q K^T and
+// the sequence and the CTA's Q rows arrive in shared memory as 16-row TMA boxes (32 f16 columns,
+// 64-byte swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3), so ldmatrix is conflict-free),
+// issued by one thread and completed on one mbarrier; V rows past the sequence's end are zeroed.  S = Q K^T and
 // O = P V run on mma.sync m16n8k16 (f16 in, f32 accumulate) with an online softmax over 64-key
 // blocks (exp2 with the 1/sqrt(32)*log2(e) scale folded in); scores never leave registers.  Full
 // 64-key blocks run unmasked; the ragged last block runs at 16-key granularity with the key mask.  The
@@ -109,42 +110,54 @@ __device__ __forceinline__ void attend_block(int kb, int L, uint32_t kaddr, uint
 }
 
 // 86 registers unbounded (5 CTAs = 20 warps per SM); capped for 7 CTAs per SM.
-__global__ void __launch_bounds__(128, 7)
-    attention_kernel(const __half* __restrict__ qkv, const int* __restrict__ cu_seqlens, int lpad,
-                     __half* __restrict__ out, unsigned* __restrict__ row_absmax) {
-    extern __shared__ __align__(128) uint8_t sm[];
+// 80 registers: 6 CTAs (24 warps) per SM.
+__global__ void __launch_bounds__(128)
+    attention_kernel(const __grid_constant__ CUtensorMap tmQKV, const int* __restrict__ cu_seqlens, int lpad,
+                     __half* __restrict__ out, unsigned* __restrict__ row_absmax, int* status) {
+    extern __shared__ uint8_t sm_raw[];
+    __shared__ uint64_t bar;
+    uint8_t* sm = sm_raw + ((1024u - (tzp::smem_u32(sm_raw) & 1023u)) & 1023u);  // swizzle-atom aligned
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        tzp::mbar_init(&bar, 1);
+        tzp::fence_mbar_init();
+        tzp::tma_prefetch_desc(&tmQKV);
+    }
+    __syncthreads();
     tzp::pdl_wait();
     const int b = blockIdx.z;
     const int h = blockIdx.y;
     const int seq0 = cu_seqlens[b];
     const int L = cu_seqlens[b + 1] - seq0;
     const int q0 = blockIdx.x * kQTile;
-    if (q0 >= L) return;
+    if (q0 >= L) return;  // uniform over the CTA
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kv_bytes = lpad * 64;
     uint8_t* ks = sm;
     uint8_t* vs = sm + kv_bytes;
     uint8_t* qs = sm + 2 * kv_bytes;
-    const int nkeys = (L + 15) & ~15;  // keys staged (zero-filled past L up to the 16-key chunk)
-    for (int i = tid; i < nkeys * 4; i += 128) {
-        const int key = i >> 2, c = i & 3;
-        const bool ok = key < L;
-        const __half* src = qkv + static_cast<long long>(seq0 + (ok ? key : 0)) * kQKV + kHidden + h * kHd + c * 8;
-        tzp::cp_async16(ks + kv_off(key, c), src, ok);
-        tzp::cp_async16(vs + kv_off(key, c), src + kHidden, ok);
+    const int nk16 = (L + 15) >> 4;                                  // 16-key boxes of K and of V
+    const int nq16 = ((L - q0 < kQTile ? L - q0 : kQTile) + 15) >> 4;  // 16-row boxes of Q
+    if (tid == 0) {
+        tzp::mbar_arrive_expect_tx(&bar, static_cast<uint32_t>((2 * nk16 + nq16) * 16 * 64));
+        for (int i = 0; i < nk16; ++i) {
+            tzp::tma_load_2d(ks + i * 1024, &tmQKV, kHidden + h * kHd, seq0 + 16 * i, &bar);
+            tzp::tma_load_2d(vs + i * 1024, &tmQKV, 2 * kHidden + h * kHd, seq0 + 16 * i, &bar);
+        }
+        for (int i = 0; i < nq16; ++i) tzp::tma_load_2d(qs + i * 1024, &tmQKV, h * kHd, seq0 + q0 + 16 * i, &bar);
     }
-    for (int i = tid; i < kQTile * 4; i += 128) {
-        const int r = i >> 2, c = i & 3;
-        const bool ok = q0 + r < L;
-        const __half* src = qkv + static_cast<long long>(seq0 + (ok ? q0 + r : 0)) * kQKV + h * kHd + c * 8;
-        tzp::cp_async16(qs + kv_off(r, c), src, ok);
+    const bool landed = tzp::mbar_wait(&bar, 0, status, nullptr);
+    // Keys in [L, 16 * nk16) are masked to -inf, but their V rows (the next sequence's tokens) still
+    // enter P V with weight 0: zero them so a non-finite value there cannot leak in.
+    if (landed && (L & 15)) {
+        for (int i = tid; i < (16 * nk16 - L) * 4; i += 128) {
+            const int key = L + (i >> 2);
+            *reinterpret_cast<uint4*>(vs + kv_off(key, i & 3)) = make_uint4(0, 0, 0, 0);
+        }
     }
-    tzp::cp_async_commit();
-    tzp::cp_async_wait<0>();
     __syncthreads();
     tzp::pdl_trigger();
-    if (q0 + warp * 16 >= L) return;  // no further block-wide synchronisation below
+    if (!landed || q0 + warp * 16 >= L) return;  // no further block-wide synchronisation below
 
     const uint32_t kaddr = tzp::smem_u32(ks), vaddr = tzp::smem_u32(vs), qaddr = tzp::smem_u32(qs);
     const int cq = 2 * (lane & 3);
@@ -206,13 +219,13 @@ __global__ void __launch_bounds__(128, 7)
 
 size_t attention_smem_bytes(int max_len) {
     const int lpad = (max_len + 63) / 64 * 64;
-    return static_cast<size_t>(2) * lpad * 64 + static_cast<size_t>(kQTile) * 64;
+    return static_cast<size_t>(2) * lpad * 64 + static_cast<size_t>(kQTile) * 64 + 1024;  // + alignment
 }
 
-// qkv f16 [T, 1152]; cu_seqlens device [B+1]; out f16 [T, 384]; row_absmax (optional) [T] float
-// bits, accumulated with atomicMax (must start at zero).
-int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int batch, int max_len, void* out,
-                     unsigned* row_absmax, cudaStream_t s, bool pdl) {
+// qkv f16 [T, 1152] (16-byte aligned); cu_seqlens device [B+1]; out f16 [T, 384]; row_absmax
+// (optional) [T] float bits, accumulated with atomicMax (must start at zero).
+int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const int* cu_seqlens, int batch, int max_len,
+                     void* out, unsigned* row_absmax, cudaStream_t s, bool pdl) {
     TZ_CHECK(max_len >= 1 && max_len <= 512, TZ_EINVAL, "attention: max_len %d outside [1, 512]", max_len);
     if (batch == 0) return TZ_OK;
     const int lpad = (max_len + 63) / 64 * 64;
@@ -225,9 +238,13 @@ int launch_attention(tz_ctx_t ctx, const void* qkv, const int* cu_seqlens, int b
                                      static_cast<int>(attention_smem_bytes(512))));
         set |= 1u << (dev & 31);
     }
+    CUtensorMap tm;  // QKV f16 [T, 1152]: 16-row x 32-column boxes, 64-byte swizzle; rows >= T read as 0
+    int rc = encode_tmap_2d_swz(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens),
+                                kQKV * 2, kHd, 16, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
     dim3 grid((max_len + kQTile - 1) / kQTile, kHeads, batch);
-    return launch_kernel(attention_kernel, grid, dim3(128), smem, s, pdl, static_cast<const __half*>(qkv), cu_seqlens, lpad,
-                         static_cast<__half*>(out), row_absmax);
+    return launch_kernel(attention_kernel, grid, dim3(128), smem, s, pdl, tm, cu_seqlens, lpad, static_cast<__half*>(out),
+                         row_absmax, ctx->d_status);
 }
 
 }  // namespace tz

@@ -58,9 +58,11 @@ struct LnCfg {
     static constexpr int B_BYTES = kN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGING = kEpiWarps * 2 * kBox;  // two residual/output boxes per epilogue warp
-    static constexpr int RED_BYTES = 3 * 4 * 128 * 4;
+    static constexpr int RED_BYTES = 3 * 4 * 128 * 4 + 4 * kN * 4;  // row reductions + the 4 column vectors
     static constexpr int SMEM = kStages * STAGE_BYTES + STAGING + RED_BYTES + 512 + 1024;  // + barriers, alignment
     static_assert(SMEM <= 227 * 1024, "shared memory");
+    static_assert((kSlice / 16) % 2 == 0, "x_out chunks are stored in pairs");
+    static_assert(32 * kSlice <= 2 * kBox, "the int8 LayerNorm output of one warp fits its two staging boxes");
 };
 
 // All epilogue warps meet here (one arrival per warp after its shared-memory writes); bounded wait on
@@ -87,7 +89,8 @@ __device__ __forceinline__ float acc_to_f(uint32_t r) {
 template <int KIND, int AUX, int AQ>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmX, int M, int K,
+                   const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmX,
+                   const __grid_constant__ CUtensorMap tmAux, int M, int K,
                    LnParams p, int* status) {
     using C = LnCfg<KIND>;
     extern __shared__ uint8_t smem_raw[];
@@ -97,6 +100,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* red_sum = reinterpret_cast<float*>(staging + C::STAGING);             // [4 slices][128 rows]
     float* red_ssq = red_sum + 4 * 128;
     float* red_max = red_ssq + 4 * 128;
+    float* sv_bias = red_max + 4 * 128;  // [384] each: bias, column scale, gamma, beta (shared memory copies)
+    float* sv_cs = sv_bias + kN;
+    float* sv_g = sv_cs + kN;
+    float* sv_b = sv_g + kN;
     uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING + C::RED_BYTES);
     uint64_t* empty = full + kStages;
     uint64_t* tfull = empty + kStages;
@@ -127,10 +134,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tzp::tma_prefetch_desc(&tmB);
         tzp::tma_prefetch_desc(&tmRes);
         tzp::tma_prefetch_desc(&tmX);
+        if (AUX == 1) tzp::tma_prefetch_desc(&tmAux);
     }
     if (warp == 1) {
         tzp::tmem_alloc(tmem_slot, 512);
         tzp::tmem_relinquish();
+    }
+    if (warp >= 2) {  // the per-column vectors are weights: read them before waiting on the previous kernel
+        for (int i = threadIdx.x - 64; i < kN; i += 32 * kEpiWarps) {
+            sv_bias[i] = p.bias[i];
+            sv_cs[i] = p.col_scale ? p.col_scale[i] : 1.0f;
+            sv_g[i] = p.gamma[i];
+            sv_b[i] = p.beta[i];
+        }
     }
     tzp::tc_fence_before();
     __syncthreads();
@@ -251,15 +267,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     inv = __fdiv_rn(1.0f, sc);
                 }
                 const uint4* src = reinterpret_cast<const uint4*>(p.a16 + static_cast<long long>(cok ? grow : 0) * p.lda16 + qq * 32);
-                uint4 x[4];
+                uint4 x[4], x1[4];  // K blocks kb and kb + 1 in flight
 #pragma unroll
-                for (int i = 0; i < 4; ++i) x[i] = cok ? __ldcs(src + i) : make_uint4(0, 0, 0, 0);
+                for (int i = 0; i < 4; ++i) {
+                    x[i] = cok ? __ldcs(src + i) : make_uint4(0, 0, 0, 0);
+                    x1[i] = (cok && kblocks > 1) ? __ldcs(src + 16 + i) : make_uint4(0, 0, 0, 0);
+                }
                 bool cbad = false;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     uint4 nx[4];
-                    if (kb + 1 < kblocks) {
+                    if (kb + 2 < kblocks) {
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) nx[i] = cok ? __ldcs(src + (kb + 1) * 16 + i) : make_uint4(0, 0, 0, 0);
+                        for (int i = 0; i < 4; ++i) nx[i] = cok ? __ldcs(src + (kb + 2) * 16 + i) : make_uint4(0, 0, 0, 0);
                     }
                     int got = 1;
                     if (lane == 0) got = tzp::mbar_wait(&empty[cstage], cphase ^ 1u, status, abort_flag) ? 1 : 0;
@@ -276,10 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 2; ++j) {
                             const float2 f0 = __half22float2(hp[2 * j]);
                             const float2 f1 = __half22float2(hp[2 * j + 1]);
-                            w[2 * i + j] = static_cast<uint32_t>(static_cast<uint8_t>(quant1(f0.x, inv))) |
-                                           (static_cast<uint32_t>(static_cast<uint8_t>(quant1(f0.y, inv))) << 8) |
-                                           (static_cast<uint32_t>(static_cast<uint8_t>(quant1(f1.x, inv))) << 16) |
-                                           (static_cast<uint32_t>(static_cast<uint8_t>(quant1(f1.y, inv))) << 24);
+                            w[2 * i + j] = pack_q4(quant1_bits(f0.x, inv), quant1_bits(f0.y, inv), quant1_bits(f1.x, inv),
+                                                   quant1_bits(f1.y, inv));
                         }
                     }
                     const uint32_t rowa = tzp::smem_u32(smem + cstage * C::STAGE_BYTES) + static_cast<uint32_t>(crow * 128);
@@ -288,7 +305,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tzp::fence_proxy_async();
                     tzp::mbar_arrive(&afull[cstage]);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) x[i] = nx[i];
+                    for (int i = 0; i < 4; ++i) {
+                        x[i] = x1[i];
+                        x1[i] = nx[i];
+                    }
                     if (++cstage == kStages) {
                         cstage = 0;
                         cphase ^= 1u;
@@ -338,19 +358,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float v[4] = {acc_to_f<KIND>(r[4 * j]), acc_to_f<KIND>(r[4 * j + 1]), acc_to_f<KIND>(r[4 * j + 2]),
                                   acc_to_f<KIND>(r[4 * j + 3])};
                     if (AQ || p.row_scale) {
-                        const float4 cs = __ldg(reinterpret_cast<const float4*>(p.col_scale + col + 4 * j));
+                        const float4 cs = *reinterpret_cast<const float4*>(sv_cs + col + 4 * j);
                         v[0] = __fmul_rn(v[0], __fmul_rn(rs, cs.x));
                         v[1] = __fmul_rn(v[1], __fmul_rn(rs, cs.y));
                         v[2] = __fmul_rn(v[2], __fmul_rn(rs, cs.z));
                         v[3] = __fmul_rn(v[3], __fmul_rn(rs, cs.w));
                     } else if (p.col_scale) {
-                        const float4 cs = __ldg(reinterpret_cast<const float4*>(p.col_scale + col + 4 * j));
+                        const float4 cs = *reinterpret_cast<const float4*>(sv_cs + col + 4 * j);
                         v[0] = __fmul_rn(v[0], cs.x);
                         v[1] = __fmul_rn(v[1], cs.y);
                         v[2] = __fmul_rn(v[2], cs.z);
                         v[3] = __fmul_rn(v[3], cs.w);
                     }
-                    const float4 bv = __ldg(reinterpret_cast<const float4*>(p.bias + col + 4 * j));
+                    const float4 bv = *reinterpret_cast<const float4*>(sv_bias + col + 4 * j);
                     v[0] = __fadd_rn(__fadd_rn(v[0], bv.x), cur[j].x);
                     v[1] = __fadd_rn(__fadd_rn(v[1], bv.y), cur[j].y);
                     v[2] = __fadd_rn(__fadd_rn(v[2], bv.z), cur[j].z);
@@ -400,26 +420,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float y[16];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const float4 g = __ldg(reinterpret_cast<const float4*>(p.gamma + col + 4 * j));
-                    const float4 bb = __ldg(reinterpret_cast<const float4*>(p.beta + col + 4 * j));
+                    const float4 g = *reinterpret_cast<const float4*>(sv_g + col + 4 * j);
+                    const float4 bb = *reinterpret_cast<const float4*>(sv_b + col + 4 * j);
                     y[4 * j] = (__uint_as_float(r[4 * j]) - mean) * inv_std * g.x + bb.x;
                     y[4 * j + 1] = (__uint_as_float(r[4 * j + 1]) - mean) * inv_std * g.y + bb.y;
                     y[4 * j + 2] = (__uint_as_float(r[4 * j + 2]) - mean) * inv_std * g.z + bb.z;
                     y[4 * j + 3] = (__uint_as_float(r[4 * j + 3]) - mean) * inv_std * g.w + bb.w;
                 }
-                {  // x_out chunk -> staging box (64-byte swizzle) -> one TMA store (rows >= M are clipped)
+                {  // x_out chunks in pairs -> the two staging boxes (64-byte swizzle) -> one proxy fence and two
+                   // TMA stores per pair (rows >= M are clipped)
                     const int b = c & 1;
-                    if (lane == 0) tzp::bulk_wait_read<1>();
-                    __syncwarp();
+                    if (b == 0) {
+                        if (lane == 0) tzp::bulk_wait_read<0>();  // the previous pair's stores have read both boxes
+                        __syncwarp();
+                    }
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         *reinterpret_cast<float4*>(box[b] + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
                             make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-                    tzp::fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tzp::tma_store_2d(&tmX, box[b], col, row0);
-                        tzp::bulk_commit();
+                    if (b == 1) {
+                        tzp::fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tzp::tma_store_2d(&tmX, box[0], col - 16, row0);
+                            tzp::tma_store_2d(&tmX, box[1], col, row0);
+                            tzp::bulk_commit();
+                        }
                     }
                 }
                 if constexpr (AUX == 0) {
@@ -447,7 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float m = fmaxf(fmaxf(red_max[rloc], red_max[128 + rloc]), fmaxf(red_max[256 + rloc], red_max[384 + rloc]));
                 const float sc = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
                 const float inv = __fdiv_rn(1.0f, sc);
-                int8_t* a = static_cast<int8_t*>(p.aux) + static_cast<long long>(row) * kN + c0;
+                // this warp's 32 x 96 int8 block, row-major (96-byte rows) in its staging boxes once the
+                // x_out stores have read them, then one TMA store
+                if (lane == 0) tzp::bulk_wait_read<0>();
+                __syncwarp();
+                uint8_t* qrow = box[0] + lane * kSlice;
 #pragma unroll
                 for (int c = 0; c < kSlice / 16; ++c) {
                     uint32_t r[16];
@@ -455,13 +485,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tzp::tmem_ld_wait();
                     uint32_t w[4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        w[j] = 0;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            w[j] |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(__uint_as_float(r[4 * j + i]), inv))) << (8 * i);
-                    }
-                    if (ok) *reinterpret_cast<uint4*>(a + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int j = 0; j < 4; ++j)
+                        w[j] = pack_q4(quant1_bits(__uint_as_float(r[4 * j]), inv), quant1_bits(__uint_as_float(r[4 * j + 1]), inv),
+                                       quant1_bits(__uint_as_float(r[4 * j + 2]), inv), quant1_bits(__uint_as_float(r[4 * j + 3]), inv));
+                    *reinterpret_cast<uint4*>(qrow + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                tzp::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    tzp::tma_store_2d(&tmAux, box[0], c0, row0);
+                    tzp::bulk_commit();
                 }
                 if (ok && slice == 0) p.aux_scale[row] = sc;
             }
@@ -521,13 +554,19 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     rc = encode_tmap_2d_swz(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.x_out, kN, static_cast<uint64_t>(g.M), kN * 4, 16, 32,
                             CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
+    CUtensorMap tq = tx;  // AUX = 1: the int8 LayerNorm output [M, 384], one 96 x 32 box per epilogue warp
+    if (AUX == 1) {
+        rc = encode_tmap_2d_swz(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.aux, kN, static_cast<uint64_t>(g.M), kN, kSlice, 32,
+                                CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    }
     if (AQ) ta = tb;  // unused: A arrives through the epilogue warps
     LnParams p{g.bias, g.col_scale, g.row_scale, g.residual, g.gamma, g.beta, g.eps, g.x_out, g.aux, g.aux_scale,
                AQ ? static_cast<const __half*>(g.a) : nullptr, g.lda, g.a_absmax};
     const int tiles = (g.M + 127) / 128;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
-    return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, tr, tx, g.M, g.K, p, ctx->d_status);
+    return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, tr, tx, tq, g.M, g.K, p, ctx->d_status);
 }
 
 }  // namespace

@@ -20,11 +20,29 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// q = clamp(round(x * inv), -127, 127), round half away from zero (Zig @round / C roundf).
+// q = clamp(round(x * inv), -127, 127), round half away from zero (Zig @round / C roundf), with
+// q's two's-complement byte in the low 8 bits of the result.  Computed with adds on the FMA pipe
+// instead of a round + float-to-int conversion pair (both on the narrow conversion pipe):
+//   t = clamp(x * inv, -127, 127)             (clamping first is equivalent: round is monotonic and
+//                                               +-127 are integers; NaN -> -127 as fmaxf drops it)
+//   a = RD(|t| + 0.5)                          (rounding down keeps floor(a) = floor(|t| + 0.5))
+//   f = RD(a + 2^23) - 2^23                    (floor: the sum's unit in the last place is 1)
+//   bits(copysign(f, t) + 1.5 * 2^23)          (an integer in [2^23, 2^24): its low byte is the
+//                                               two's-complement byte of copysign(f, t))
+__device__ __forceinline__ uint32_t quant1_bits(float x, float inv) {
+    const float t = fminf(fmaxf(__fmul_rn(x, inv), -127.0f), 127.0f);
+    const float a = __fadd_rd(fabsf(t), 0.5f);
+    const float f = __fsub_rn(__fadd_rd(a, 8388608.0f), 8388608.0f);
+    return __float_as_uint(__fadd_rn(copysignf(f, t), 12582912.0f));
+}
+
 __device__ __forceinline__ int8_t quant1(float x, float inv) {
-    float r = roundf(__fmul_rn(x, inv));
-    r = fminf(fmaxf(r, -127.0f), 127.0f);
-    return static_cast<int8_t>(static_cast<int>(r));
+    return static_cast<int8_t>(quant1_bits(x, inv) & 0xFFu);
+}
+
+// Low bytes of four quant1_bits results packed little-endian into one word.
+__device__ __forceinline__ uint32_t pack_q4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }

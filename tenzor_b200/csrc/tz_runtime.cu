@@ -91,8 +91,13 @@ int encode_tmap_2d_swz(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
     TZ_CHECK(enc, TZ_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
     TZ_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, TZ_EINVAL, "TMA base must be 16-byte aligned");
     TZ_CHECK(row_stride_bytes % 16 == 0, TZ_EINVAL, "TMA row stride must be a multiple of 16 bytes");
-    const uint32_t span = swz == CU_TENSOR_MAP_SWIZZLE_128B ? 128 : swz == CU_TENSOR_MAP_SWIZZLE_64B ? 64 : 32;
-    TZ_CHECK(box_inner * static_cast<uint32_t>(elem_bytes) <= span, TZ_EINVAL, "TMA box too wide for its swizzle");
+    const uint32_t inner_bytes = box_inner * static_cast<uint32_t>(elem_bytes);
+    TZ_CHECK(inner_bytes % 16 == 0 && box_inner <= 256 && box_outer <= 256, TZ_EINVAL,
+             "TMA box inner extent must be a multiple of 16 bytes (at most 256 x 256 elements)");
+    if (swz != CU_TENSOR_MAP_SWIZZLE_NONE) {
+        const uint32_t span = swz == CU_TENSOR_MAP_SWIZZLE_128B ? 128 : swz == CU_TENSOR_MAP_SWIZZLE_64B ? 64 : 32;
+        TZ_CHECK(inner_bytes <= span, TZ_EINVAL, "TMA box too wide for its swizzle");
+    }
     cuuint64_t dims[2] = {inner, outer < 1 ? 1 : outer};
     cuuint64_t strides[1] = {row_stride_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};

@@ -133,6 +133,28 @@ def test_quantize_act_rows_bit_exact(ctx, oracle):
     assert (host(q) == qo).all() and (host(s) == so).all()
 
 
+def test_quantize_act_rows_ties_bit_exact(ctx, oracle):
+    """Rounding edge cases of q = clamp(round_half_away(x / s)): rows whose |max| is 127 have s = 1,
+    so x / s = x exactly and every half-integer is a tie."""
+    from tenzor_b200 import ops
+    edge = np.array([0.5, -0.5, 1.5, -1.5, 2.5, -2.5, 125.5, -125.5, 126.5, -126.5, 127.0, -127.0,
+                     0.49999997, -0.49999997, 0.50000006, -0.50000006, 2.4999998, -2.4999998, 0.0, -0.0,
+                     1e-30, -1e-30, 63.5, -63.5, 126.49999, -126.49999, 3.0, -3.0], np.float32)
+    rng = np.random.default_rng(13)
+    rows = []
+    for _ in range(64):
+        r = rng.choice(edge, 384).astype(np.float32)
+        r[rng.integers(0, 384)] = 127.0 if rng.random() < 0.5 else -127.0
+        rows.append(r)
+    halves = (rng.integers(-254, 255, (64, 384)) / 2.0).astype(np.float32)  # every value a tie or an integer
+    halves[:, 0] = 127.0
+    x = np.concatenate([np.stack(rows), halves, rng.normal(0, 3, (32, 384)).astype(np.float32) * 37.0])
+    q, s = ops.quantize_act_rows(ctx, dev(x))
+    qo, so = oracle.quantize_act_rows(x)
+    assert (host(s) == so).all()
+    assert (host(q) == qo).all()
+
+
 @pytest.mark.parametrize("case", kats.LAYERNORM, ids=[c[0] for c in kats.LAYERNORM])
 def test_layernorm_kats(ctx, case):
     from tenzor_b200 import ops
