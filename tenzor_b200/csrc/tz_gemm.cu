@@ -291,13 +291,6 @@ __device__ __forceinline__ void stage_chunk(const EpiParams& ep, uint32_t buf, i
 // no residual / op chain.  Everything else takes the general epilogue (FAST == 0).
 constexpr int F_ON = 1, F_GELU = 2, F_AMAX = 4, F_RSCALE = 8, F_CSCALE = 16;
 
-__device__ __forceinline__ float gelu_fast2(float x) {
-    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) with the cubic as x (k0 + k1 x^2)
-    const float inner = x * fmaf(0.7978845608f * 0.044715f, x * x, 0.7978845608f);
-    const float hx = 0.5f * x;
-    return fmaf(hx, tzp::tanh_approx(inner), hx);
-}
-
 template <int KIND, int BN, int STAGES, int EPI_WARPS, int FAST>
 __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -427,8 +420,8 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         // scales (into this warp's staging area, read back as broadcasts).  Then the NCH chunks of
         // 16 columns: TMEM load of chunk c+1 in flight while chunk c is converted and staged; the
         // accumulator is released as soon as its last chunk is in registers; one proxy fence and NCH
-        // TMA stores per tile.  |max| is taken on the f32 values (f16 rounding is monotonic, so the
-        // f16 of the max equals the max of the f16 values).
+        // TMA stores per tile.  The arithmetic runs on packed f32x2 instructions (bit-identical to
+        // the scalar forms) and |max| is taken on the packed f16 results.
         constexpr int CPW = C::COLS_PER_WARP;
         constexpr int NCH = CPW / CW;
         constexpr int BOX = 32 * CW * 2;  // one 32 x 16 f16 box
@@ -440,6 +433,9 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         float* cvb = reinterpret_cast<float*>(wst + NCH * BOX);
         float* cvs = cvb + CPW;
         const uint32_t wst_a = tzp::smem_u32(wst);
+        const uint64_t kG0 = tzp::f2_pack(0.7978845608f, 0.7978845608f);
+        const uint64_t kG1 = tzp::f2_pack(0.7978845608f * 0.044715f, 0.7978845608f * 0.044715f);
+        const uint64_t kHalf = tzp::f2_pack(0.5f, 0.5f);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -451,6 +447,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             const int cbase = n0 + slice * CPW;
             float rs = 1.0f;
             if constexpr ((FAST & F_RSCALE) != 0) rs = row_ok ? __ldg(ep.row_scale + row) : 1.0f;
+            const uint64_t rs2 = tzp::f2_pack(rs, rs);
             if (lane == 0) tzp::bulk_wait_read<0>();  // the previous tile's stores have read the boxes
             for (int i = lane; i < CPW; i += 32) {
                 cvb[i] = __ldg(ep.bias + cbase + i);
@@ -463,7 +460,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             uint32_t ra[CW], rb[CW];
             tzp::tmem_ld16(tcol, ra);
             tzp::tmem_ld_wait();
-            float amax = 0.0f;
+            __half2 amax2 = __float2half2_rn(0.0f);
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
                 uint32_t(&cur)[CW] = (c & 1) ? rb : ra;
@@ -475,46 +472,45 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                     __syncwarp();
                     if (lane == 0) tzp::mbar_arrive(&tempty[acc]);
                 }
-                float v[CW];
+                // dequantise (+ bias, GELU) two columns per packed f32x2 instruction; the f16 pairs
+                // feed both the staging and the row |max| (max |f16| is exact on the packed halves)
+                uint32_t h[CW / 2];
 #pragma unroll
-                for (int j = 0; j < CW; ++j) {
-                    if constexpr (KIND == KIND_I8)
-                        v[j] = __int2float_rn(static_cast<int>(cur[j]));
-                    else
-                        v[j] = __uint_as_float(cur[j]);
-                }
-#pragma unroll
-                for (int j = 0; j < CW; j += 4) {
-                    const float4 b = *reinterpret_cast<const float4*>(cvb + 16 * c + j);
-                    if constexpr ((FAST & F_RSCALE) != 0) {
-                        const float4 cs = *reinterpret_cast<const float4*>(cvs + 16 * c + j);
-                        v[j] = __fmul_rn(v[j], __fmul_rn(rs, cs.x));
-                        v[j + 1] = __fmul_rn(v[j + 1], __fmul_rn(rs, cs.y));
-                        v[j + 2] = __fmul_rn(v[j + 2], __fmul_rn(rs, cs.z));
-                        v[j + 3] = __fmul_rn(v[j + 3], __fmul_rn(rs, cs.w));
-                    } else if constexpr ((FAST & F_CSCALE) != 0) {
-                        const float4 cs = *reinterpret_cast<const float4*>(cvs + 16 * c + j);
-                        v[j] = __fmul_rn(v[j], cs.x);
-                        v[j + 1] = __fmul_rn(v[j + 1], cs.y);
-                        v[j + 2] = __fmul_rn(v[j + 2], cs.z);
-                        v[j + 3] = __fmul_rn(v[j + 3], cs.w);
+                for (int j = 0; j < CW / 2; ++j) {
+                    float lo, hi;
+                    if constexpr (KIND == KIND_I8) {
+                        lo = __int2float_rn(static_cast<int>(cur[2 * j]));
+                        hi = __int2float_rn(static_cast<int>(cur[2 * j + 1]));
+                    } else {
+                        lo = __uint_as_float(cur[2 * j]);
+                        hi = __uint_as_float(cur[2 * j + 1]);
                     }
-                    v[j] = __fadd_rn(v[j], b.x);
-                    v[j + 1] = __fadd_rn(v[j + 1], b.y);
-                    v[j + 2] = __fadd_rn(v[j + 2], b.z);
-                    v[j + 3] = __fadd_rn(v[j + 3], b.w);
-                }
-#pragma unroll
-                for (int j = 0; j < CW; ++j) {
-                    if constexpr ((FAST & F_GELU) != 0) v[j] = gelu_fast2(v[j]);
-                    if constexpr ((FAST & F_AMAX) != 0) amax = fmaxf(amax, fabsf(v[j]));
+                    uint64_t x = tzp::f2_pack(lo, hi);
+                    const uint64_t b2 = *reinterpret_cast<const uint64_t*>(cvb + 16 * c + 2 * j);
+                    if constexpr ((FAST & F_RSCALE) != 0)
+                        x = tzp::f2_mul(x, tzp::f2_mul(rs2, *reinterpret_cast<const uint64_t*>(cvs + 16 * c + 2 * j)));
+                    else if constexpr ((FAST & F_CSCALE) != 0)
+                        x = tzp::f2_mul(x, *reinterpret_cast<const uint64_t*>(cvs + 16 * c + 2 * j));
+                    x = tzp::f2_add(x, b2);
+                    if constexpr ((FAST & F_GELU) != 0) {
+                        // GELU (arctic.zig:750-756, hardware tanh): 0.5 x (1 + tanh(x (k0 + k1 x^2))) with
+                        // k0 = sqrt(2/pi), k1 = 0.044715 k0
+                        const uint64_t inner = tzp::f2_mul(x, tzp::f2_fma(tzp::f2_mul(x, x), kG1, kG0));
+                        const float2 in = tzp::f2_unpack(inner);
+                        const uint64_t th = tzp::f2_pack(tzp::tanh_approx(in.x), tzp::tanh_approx(in.y));
+                        const uint64_t hx = tzp::f2_mul(x, kHalf);
+                        x = tzp::f2_fma(hx, th, hx);
+                    }
+                    const float2 r = tzp::f2_unpack(x);
+                    h[j] = tzp::pack_half2(r.x, r.y);
+                    if constexpr ((FAST & F_AMAX) != 0)
+                        amax2 = __hmax2(amax2, __habs2(*reinterpret_cast<const __half2*>(&h[j])));
                 }
                 const uint32_t buf = wst_a + static_cast<uint32_t>(c * BOX);
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                     const uint32_t a = buf + lane * 32 + ((u ^ ((lane >> 2) & 1)) << 4);
-                    tzp::st_shared_v4(a, tzp::pack_half2(v[8 * u], v[8 * u + 1]), tzp::pack_half2(v[8 * u + 2], v[8 * u + 3]),
-                                      tzp::pack_half2(v[8 * u + 4], v[8 * u + 5]), tzp::pack_half2(v[8 * u + 6], v[8 * u + 7]));
+                    tzp::st_shared_v4(a, h[4 * u], h[4 * u + 1], h[4 * u + 2], h[4 * u + 3]);
                 }
                 if (c + 1 < NCH) tzp::tmem_ld_wait();
             }
@@ -526,7 +522,8 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                 tzp::bulk_commit();
             }
             if constexpr ((FAST & F_AMAX) != 0) {
-                if (row_ok) atomicMax(ep.row_absmax + row, __float_as_uint(__half2float(__float2half_rn(amax))));
+                if (row_ok)
+                    atomicMax(ep.row_absmax + row, __float_as_uint(fmaxf(__low2float(amax2), __high2float(amax2))));
             }
             if (++acc == 2) {
                 acc = 0;
