@@ -264,6 +264,34 @@ int tz_reduce(tz_ctx_t ctx, int reduce_op, const int* pre_ops, int n_pre, const 
 int tz_gather_rows(tz_ctx_t ctx, const float* table, int64_t table_rows, const uint32_t* ids,
                    int64_t n_ids, int cols, float* out, tz_stream_t stream);
 
+/* ---- LeNet-5 batch inference ------------------------------------------------------------------
+ * Replaces LeNet.forward (lenet.zig:262-268 -> forwardSequential 270-321 / forwardParallel
+ * 323-513): conv1 6@5x5 -> ReLU -> 2x2 maxpool -> conv2 16@5x5 -> ReLU -> 2x2 maxpool -> flatten
+ * (NHWC) -> FC 120 -> ReLU -> FC 84 -> ReLU -> FC 10.  Images are [n, 28, 28, 1] f32 (NHWC); conv
+ * weights [out, kh, kw, in] and FC weights [out, in] as LeNetWeights (lenet.zig:33-52).
+ *   TZ_LENET_REF:  lenet.zig as written: conv1 valid (24x24), FC1 in = 256, out = logits [n, 10].
+ *   TZ_LENET_PAD2: conv1 zero padding 2 (28x28), FC1 in = 400, out = softmax(logits) [n, 10]. */
+typedef struct tz_lenet_s* tz_lenet_t;
+enum { TZ_LENET_REF = 0, TZ_LENET_PAD2 = 1 };
+typedef struct {
+    const float *conv1_w, *conv1_b; /* [6,5,5,1], [6] */
+    const float *conv2_w, *conv2_b; /* [16,5,5,6], [16] */
+    const float *fc1_w, *fc1_b;     /* [120, 256 | 400], [120] */
+    const float *fc2_w, *fc2_b;     /* [84,120], [84] */
+    const float *fc3_w, *fc3_b;     /* [10,84], [10] */
+} tz_lenet_weights;
+/* Copies the host weights to the context's device (LeNet.init + initKaiming's caller-provided
+ * weights).  TZ_EMISSING when a pointer is NULL. */
+int tz_lenet_load(tz_ctx_t ctx, const tz_lenet_weights* w, int variant, tz_lenet_t* out);
+int tz_lenet_free(tz_lenet_t model);
+/* Pre-sizes the device scratch for n images (otherwise grown on demand, which synchronises). */
+int tz_lenet_reserve(tz_lenet_t model, int64_t n);
+/* Host images [n,784] -> host out [n,10]; synchronous (LeNet.forward's contract). */
+int tz_lenet_forward(tz_lenet_t model, const float* images, int64_t n, float* out);
+/* Device images (8-byte aligned) -> device out, asynchronous on `stream`. */
+int tz_lenet_forward_device(tz_lenet_t model, const float* images, int64_t n, float* out,
+                            tz_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

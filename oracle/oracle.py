@@ -68,6 +68,7 @@ def _declare(L):
     L.tzo_arctic_forward_dump.restype = C.c_int
     L.tzo_arctic_forward_dump.argtypes = [P, C.c_int, P, P, C.c_int, P, C.c_int, P]
     L.tzo_blas_status.restype = C.c_char_p
+    L.tzo_lenet_forward.argtypes = [P, C.c_int, P, C.c_int64, P, C.c_int]
 
 
 def ptr(a):
@@ -307,3 +308,23 @@ class OracleModel:
 
 def blas_status() -> str:
     return lib().tzo_blas_status().decode()
+
+
+# ---- LeNet-5 (tz_oracle_lenet.c) ----
+LENET_REF, LENET_PAD2 = 0, 1
+LENET_KEYS = ("conv1_w", "conv1_b", "conv2_w", "conv2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "fc3_w", "fc3_b")
+
+
+class _LenetWeights(C.Structure):
+    _fields_ = [(k, P) for k in LENET_KEYS]
+
+
+def lenet_forward(w: dict, variant: int, images: np.ndarray, nthreads: int = 0) -> np.ndarray:
+    """images [n, 28, 28, 1] (or [n, 784]) f32 -> [n, 10] (logits for LENET_REF, softmax for
+    LENET_PAD2); weights as in tz_oracle.h (NHWC conv weights [out, kh, kw, in])."""
+    keep = {k: c32(w[k]) for k in LENET_KEYS}
+    ws = _LenetWeights(*[ptr(keep[k]) for k in LENET_KEYS])
+    x = c32(images).reshape(-1, 784)
+    out = np.empty((x.shape[0], 10), np.float32)
+    lib().tzo_lenet_forward(C.byref(ws), variant, ptr(x), x.shape[0], ptr(out), nthreads)
+    return out

@@ -102,6 +102,21 @@ int tzo_arctic_forward_dump(const tzo_arctic_weights* w, int mode, const uint32_
                             float* dump);
 const char* tzo_blas_status(void);
 
+/* ---- LeNet-5 (lenet.zig), tz_oracle_lenet.c ---- */
+#define TZO_LENET_REF 0  /* lenet.zig: conv1 valid, FC1 in 256, logits */
+#define TZO_LENET_PAD2 1 /* benchmark variant: conv1 pad 2, FC1 in 400, softmax */
+/* NHWC activations; conv weights [out, kh, kw, in]; FC weights [out, in]. */
+typedef struct {
+    const float *conv1_w, *conv1_b; /* [6,5,5,1], [6] */
+    const float *conv2_w, *conv2_b; /* [16,5,5,6], [16] */
+    const float *fc1_w, *fc1_b;     /* [120, 256 or 400], [120] */
+    const float *fc2_w, *fc2_b;     /* [84,120], [84] */
+    const float *fc3_w, *fc3_b;     /* [10,84], [10] */
+} tzo_lenet_weights;
+void tzo_lenet_forward_one(const tzo_lenet_weights* w, int variant, const float* img, float* out);
+void tzo_lenet_forward(const tzo_lenet_weights* w, int variant, const float* images, int64_t n, float* out,
+                       int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

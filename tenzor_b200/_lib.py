@@ -28,7 +28,8 @@ EXPORTS = [
     "tz_softmax_last_axis", "tz_softmax_keylen", "tz_linear_f32", "tz_linear_w8a32",
     "tz_linear_w8a8", "tz_linear_w8a8_noalloc", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
     "tz_matmul_epilogue", "tz_ew_add_mul_exp", "tz_ew_program_run", "tz_ew_unary_chain", "tz_reduce",
-    "tz_gather_rows",
+    "tz_gather_rows", "tz_lenet_load", "tz_lenet_free", "tz_lenet_reserve", "tz_lenet_forward",
+    "tz_lenet_forward_device",
 ]
 
 
@@ -116,6 +117,8 @@ def _declare(L):
         "tz_ew_program_run": [P, C.POINTER(EwProgram), P, i64, i, P],
         "tz_reduce": [P, i, P, i, P, i64, P, P],
         "tz_gather_rows": [P, P, i64, P, i64, i, P, P],
+        "tz_lenet_load": [P, P, i, C.POINTER(P)], "tz_lenet_free": [P], "tz_lenet_reserve": [P, i64],
+        "tz_lenet_forward": [P, P, i64, P], "tz_lenet_forward_device": [P, P, i64, P, P],
     }
     for name, args in sig.items():
         f = getattr(L, name)

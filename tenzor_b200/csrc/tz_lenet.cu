@@ -1,0 +1,449 @@
+// tz_lenet.cu -- LeNet-5 batch inference on sm_100a (f32 CUDA-core arithmetic).
+//
+// Reference: LeNet.forward / forwardSequential, lenet.zig:262-321: conv1 6@5x5 -> ReLU -> 2x2
+// maxpool -> conv2 16@5x5 -> ReLU -> 2x2 maxpool -> flatten (NHWC) -> FC 120 -> ReLU -> FC 84 ->
+// ReLU -> FC 10, with conv2dForward (conv2d.zig:30-110), maxPool2dForward (maxpool.zig:25-78) and
+// linearForward (lenet.zig:874-898).  Layouts as in the reference: images [N, 28, 28, 1], conv
+// weights [out, kh, kw, in], FC weights [out, in].  Variant TZ_LENET_REF is lenet.zig itself
+// (conv1 valid, 256 features, logits); TZ_LENET_PAD2 is the benchmark configuration (conv1 zero
+// padding 2, 400 features, softmax over the logits).
+//
+// Two kernels.  lenet_conv_kernel: a persistent CTA walks groups of G images; each group is staged
+// in shared memory (zero border for the padding), conv1+ReLU+pool writes the pooled map (NHWC) to
+// shared memory, conv2+ReLU+pool writes the flattened features to global memory.  A thread owns one
+// pooled output position (all 6 channels for conv1; 8 of the 16 channels for conv2) and its four
+// pre-pool conv outputs, so every input value read feeds 24 (conv1) or 32 (conv2) FMAs and the
+// weights are warp-uniform shared-memory broadcasts.  lenet_fc_kernel: 64-image tiles; FC weights
+// staged through shared memory in K chunks (transposed so a thread's 8 outputs are contiguous),
+// 4 images x 8 outputs of register blocking per thread, ReLU fused, softmax per image at the end.
+// The work is FMA-bound (0.83 MFLOP per image for the padded variant), not HBM-bound (3 KB in).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+
+#include "tz_internal.h"
+
+struct tz_lenet_s {
+    tz_ctx_t ctx = nullptr;
+    int device = 0;
+    int variant = 0;
+    float* d_w = nullptr;     // all weights, one allocation
+    float* c1w = nullptr;     // [25][8]: conv1 weight by tap, channels padded to 8 (zeros)
+    float* c1b = nullptr;     // [8]
+    float* c2w = nullptr;     // [25][6][16]: conv2 weight by tap, input channel, output channel
+    float* c2b = nullptr;     // [16]
+    float *f1w = nullptr, *f1b = nullptr, *f2w = nullptr, *f2b = nullptr, *f3w = nullptr, *f3b = nullptr;
+    float* d_feat = nullptr;  // [cap, features] scratch between the two kernels
+    int64_t cap = 0;
+    float* d_io = nullptr;    // host-API staging: images [cap_io, 784] then logits [cap_io, 10]
+    int64_t cap_io = 0;
+};
+
+namespace tz {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int PAD>
+struct LenetShape {
+    static constexpr int PW = 28 + 2 * PAD;      // staged (padded) image width
+    static constexpr int C1 = PW - 4;            // conv1 output 24 / 28
+    static constexpr int P1 = C1 / 2;            // pool1 12 / 14
+    static constexpr int C2 = P1 - 4;            // conv2 output 8 / 10
+    static constexpr int P2 = C2 / 2;            // pool2 4 / 5
+    static constexpr int FEAT = P2 * P2 * 16;    // 256 / 400
+    static constexpr int G = PAD ? 5 : 8;        // images per group: G * P2 * P2 * 2 <= 256 conv2 items
+    static constexpr int SMEM_FLOATS = 25 * 8 + 8 + 25 * 6 * 16 + 16 + G * PW * PW + G * P1 * P1 * 6;
+};
+
+template <int PAD>
+__global__ void __launch_bounds__(kThreads)
+    lenet_conv_kernel(const float* __restrict__ images, int64_t n, const float* __restrict__ c1w,
+                      const float* __restrict__ c1b, const float* __restrict__ c2w, const float* __restrict__ c2b,
+                      float* __restrict__ feat) {
+    using S = LenetShape<PAD>;
+    extern __shared__ __align__(16) float sm[];
+    float* s_w1 = sm;                        // [25][8]
+    float* s_b1 = s_w1 + 25 * 8;             // [8]
+    float* s_w2 = s_b1 + 8;                  // [25][6][16]
+    float* s_b2 = s_w2 + 25 * 6 * 16;        // [16]
+    float* s_img = s_b2 + 16;                // [G][PW][PW]
+    float* s_p1 = s_img + S::G * S::PW * S::PW;  // [G][P1][P1][6]
+    const int tid = threadIdx.x;
+    for (int i = tid; i < 25 * 8 + 8; i += kThreads) s_w1[i] = i < 200 ? c1w[i] : c1b[i - 200];
+    for (int i = tid; i < 25 * 6 * 16 + 16; i += kThreads) s_w2[i] = i < 2400 ? c2w[i] : c2b[i - 2400];
+    for (int i = tid; i < S::G * S::PW * S::PW; i += kThreads) s_img[i] = 0.0f;  // the padding border stays 0
+    __syncthreads();
+
+    const int64_t groups = (n + S::G - 1) / S::G;
+    for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+        const int64_t img0 = grp * S::G;
+        const int gcount = static_cast<int>(n - img0 < S::G ? n - img0 : S::G);
+        // ---- stage the group's images (float2: rows start 8-byte aligned at column PAD) ----
+        for (int i = tid; i < gcount * 392; i += kThreads) {
+            const int g = i / 392, r = i % 392, y = r / 14, x2 = r % 14;
+            const float2 v = *reinterpret_cast<const float2*>(images + (img0 + g) * 784 + y * 28 + 2 * x2);
+            *reinterpret_cast<float2*>(s_img + (g * S::PW + y + PAD) * S::PW + PAD + 2 * x2) = v;
+        }
+        __syncthreads();
+        // ---- conv1 (6 channels) + ReLU + 2x2 max pool: one pooled position per item ----
+        for (int item = tid; item < gcount * S::P1 * S::P1; item += kThreads) {
+            const int g = item / (S::P1 * S::P1), r = item % (S::P1 * S::P1), py = r / S::P1, px = r % S::P1;
+            const float* src = s_img + (g * S::PW + 2 * py) * S::PW + 2 * px;
+            float patch[6][6];
+#pragma unroll
+            for (int a = 0; a < 6; ++a)
+#pragma unroll
+                for (int b = 0; b < 6; b += 2) {
+                    const float2 v = *reinterpret_cast<const float2*>(src + a * S::PW + b);
+                    patch[a][b] = v.x;
+                    patch[a][b + 1] = v.y;
+                }
+            float acc[4][6];
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+#pragma unroll
+                for (int c = 0; c < 6; ++c) acc[p][c] = 0.0f;
+#pragma unroll
+            for (int kh = 0; kh < 5; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 5; ++kw) {
+                    const float4 wa = *reinterpret_cast<const float4*>(s_w1 + (kh * 5 + kw) * 8);
+                    const float2 wb = *reinterpret_cast<const float2*>(s_w1 + (kh * 5 + kw) * 8 + 4);
+                    const float w[6] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y};
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) {
+                        const float x = patch[(p >> 1) + kh][(p & 1) + kw];
+#pragma unroll
+                        for (int c = 0; c < 6; ++c) acc[p][c] = fmaf(x, w[c], acc[p][c]);
+                    }
+                }
+            float* dst = s_p1 + ((g * S::P1 + py) * S::P1 + px) * 6;
+#pragma unroll
+            for (int c = 0; c < 6; c += 2) {
+                float m0 = 0.0f, m1 = 0.0f;  // max over ReLU outputs (all >= 0)
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    m0 = fmaxf(m0, s_b1[c] + acc[p][c]);
+                    m1 = fmaxf(m1, s_b1[c + 1] + acc[p][c + 1]);
+                }
+                *reinterpret_cast<float2*>(dst + c) = make_float2(m0, m1);
+            }
+        }
+        __syncthreads();
+        // ---- conv2 (8 of 16 channels per item) + ReLU + 2x2 max pool -> features ----
+        for (int item = tid; item < gcount * S::P2 * S::P2 * 2; item += kThreads) {
+            const int half = item & 1, pos = item >> 1;
+            const int g = pos / (S::P2 * S::P2), r = pos % (S::P2 * S::P2), py = r / S::P2, px = r % S::P2;
+            const float* src = s_p1 + ((g * S::P1 + 2 * py) * S::P1 + 2 * px) * 6;
+            float acc[4][8];
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[p][c] = 0.0f;
+#pragma unroll 1
+            for (int kh = 0; kh < 5; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 5; ++kw) {
+                    float x[4][6];
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) {
+                        const float* q = src + (((p >> 1) + kh) * S::P1 + (p & 1) + kw) * 6;
+#pragma unroll
+                        for (int ic = 0; ic < 6; ic += 2) {
+                            const float2 v = *reinterpret_cast<const float2*>(q + ic);
+                            x[p][ic] = v.x;
+                            x[p][ic + 1] = v.y;
+                        }
+                    }
+                    const float* wt = s_w2 + (kh * 5 + kw) * 96 + half * 8;
+#pragma unroll
+                    for (int ic = 0; ic < 6; ++ic) {
+                        const float4 wa = *reinterpret_cast<const float4*>(wt + ic * 16);
+                        const float4 wb = *reinterpret_cast<const float4*>(wt + ic * 16 + 4);
+                        const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                        for (int p = 0; p < 4; ++p)
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) acc[p][c] = fmaf(x[p][ic], w[c], acc[p][c]);
+                    }
+                }
+            float m[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float b = s_b2[half * 8 + c];
+                m[c] = fmaxf(fmaxf(fmaxf(0.0f, b + acc[0][c]), b + acc[1][c]), fmaxf(b + acc[2][c], b + acc[3][c]));
+            }
+            float* dst = feat + (img0 + g) * S::FEAT + (py * S::P2 + px) * 16 + half * 8;
+            *reinterpret_cast<float4*>(dst) = make_float4(m[0], m[1], m[2], m[3]);
+            *reinterpret_cast<float4*>(dst + 4) = make_float4(m[4], m[5], m[6], m[7]);
+        }
+        __syncthreads();
+    }
+}
+
+constexpr int kTile = 64;  // images per FC tile
+constexpr int kKC = 40;    // K chunk of staged FC weights
+
+// out[img][o] = act(b[o] + sum_k in[img][k] * W[o][k]) for the tile's 64 images.  Thread t: images
+// (t % 16) + 16 i (i < 4, odd row strides keep the reads conflict-free), outputs 8 (t / 16) .. + 7.
+template <int IN, int OUT, int LDI, int LDO, bool RELU>
+__device__ __forceinline__ void fc_layer(const float* s_in, const float* __restrict__ w, const float* __restrict__ b,
+                                         float* s_out, float* s_wc) {
+    constexpr int OUTP = (OUT + 7) / 8 * 8;
+    constexpr int LDW = OUTP + 4;
+    const int tid = threadIdx.x;
+    const int ig = tid & 15, og = tid >> 4;
+    const bool active = og * 8 < OUT;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < IN; k0 += kKC) {
+        __syncthreads();  // the previous chunk (or layer) is consumed
+        for (int i = tid; i < OUTP * kKC; i += kThreads) {
+            const int o = i / kKC, kk = i % kKC;
+            s_wc[kk * LDW + o] = (o < OUT && k0 + kk < IN) ? w[o * IN + k0 + kk] : 0.0f;
+        }
+        __syncthreads();
+        if (active) {
+            const int kn = IN - k0 < kKC ? IN - k0 : kKC;
+            for (int kk = 0; kk < kn; ++kk) {
+                const float4 wa = *reinterpret_cast<const float4*>(s_wc + kk * LDW + og * 8);
+                const float4 wb = *reinterpret_cast<const float4*>(s_wc + kk * LDW + og * 8 + 4);
+                const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float x = s_in[(ig + 16 * i) * LDI + k0 + kk];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(x, wv[j], acc[i][j]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (active) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int o = og * 8 + j;
+            if (o < OUT) {
+                const float bo = b[o];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float v = bo + acc[i][j];
+                    s_out[(ig + 16 * i) * LDO + o] = RELU ? fmaxf(v, 0.0f) : v;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+template <int FEAT, bool SOFTMAX>
+__global__ void __launch_bounds__(kThreads)
+    lenet_fc_kernel(const float* __restrict__ feat, int64_t n, const float* __restrict__ f1w,
+                    const float* __restrict__ f1b, const float* __restrict__ f2w, const float* __restrict__ f2b,
+                    const float* __restrict__ f3w, const float* __restrict__ f3b, float* __restrict__ out) {
+    constexpr int L0 = FEAT + 1, L1 = 121, L2 = 85, L3 = 11;
+    extern __shared__ __align__(16) float sm[];
+    float* s_x = sm;                  // [64][L0]
+    float* s_h1 = s_x + kTile * L0;   // [64][L1]
+    float* s_h2 = s_h1 + kTile * L1;  // [64][L2]
+    float* s_wc = s_h2 + kTile * L2;  // [kKC][128 + 4]
+    float* s_o = s_x;                 // [64][L3], reuses s_x after FC1
+    const int tid = threadIdx.x;
+    const int64_t tiles = (n + kTile - 1) / kTile;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int64_t base = t * kTile;
+        const int cnt = static_cast<int>(n - base < kTile ? n - base : kTile);
+        __syncthreads();
+        for (int i = tid; i < kTile * FEAT; i += kThreads) {
+            const int r = i / FEAT, k = i % FEAT;
+            s_x[r * L0 + k] = r < cnt ? feat[(base + r) * FEAT + k] : 0.0f;
+        }
+        fc_layer<FEAT, 120, L0, L1, true>(s_x, f1w, f1b, s_h1, s_wc);
+        fc_layer<120, 84, L1, L2, true>(s_h1, f2w, f2b, s_h2, s_wc);
+        fc_layer<84, 10, L2, L3, false>(s_h2, f3w, f3b, s_o, s_wc);
+        if (tid < cnt) {
+            float v[10];
+#pragma unroll
+            for (int j = 0; j < 10; ++j) v[j] = s_o[tid * L3 + j];
+            if (SOFTMAX) {  // softmax.zig:20-47: max, exp(x - max), divide by the sum
+                float m = v[0];
+#pragma unroll
+                for (int j = 1; j < 10; ++j) m = fmaxf(m, v[j]);
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 10; ++j) {
+                    v[j] = expf(v[j] - m);
+                    s += v[j];
+                }
+#pragma unroll
+                for (int j = 0; j < 10; ++j) v[j] = v[j] / s;
+            }
+            float* o = out + (base + tid) * 10;
+#pragma unroll
+            for (int j = 0; j < 10; ++j) o[j] = v[j];
+        }
+    }
+}
+
+template <int PAD>
+int launch_lenet(tz_lenet_s* m, const float* d_images, int64_t n, float* d_out, cudaStream_t s) {
+    using S = LenetShape<PAD>;
+    const int conv_smem = S::SMEM_FLOATS * 4;
+    constexpr int FEAT = S::FEAT;
+    const int fc_smem = (kTile * (FEAT + 1) + kTile * 121 + kTile * 85 + kKC * 132) * 4;
+    static unsigned set = 0;
+    const unsigned bit = 1u << (m->device & 31);
+    if (!(set & bit)) {
+        TZ_CUDA(cudaFuncSetAttribute(lenet_conv_kernel<PAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, conv_smem));
+        TZ_CUDA(cudaFuncSetAttribute(lenet_fc_kernel<FEAT, PAD != 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, fc_smem));
+        set |= bit;
+    }
+    const int sms = m->ctx->sm_count;
+    const int64_t groups = (n + S::G - 1) / S::G;
+    const int g1 = static_cast<int>(groups < 4LL * sms ? groups : 4LL * sms);
+    lenet_conv_kernel<PAD><<<g1, kThreads, conv_smem, s>>>(d_images, n, m->c1w, m->c1b, m->c2w, m->c2b, m->d_feat);
+    TZ_CUDA(cudaGetLastError());
+    const int64_t tiles = (n + kTile - 1) / kTile;
+    const int g2 = static_cast<int>(tiles < sms ? tiles : sms);
+    lenet_fc_kernel<FEAT, PAD != 0><<<g2, kThreads, fc_smem, s>>>(m->d_feat, n, m->f1w, m->f1b, m->f2w, m->f2b, m->f3w,
+                                                                  m->f3b, d_out);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int lenet_reserve(tz_lenet_s* m, int64_t n) {
+    if (n <= m->cap) return TZ_OK;
+    TZ_CUDA(cudaSetDevice(m->device));
+    TZ_CUDA(cudaDeviceSynchronize());
+    if (m->d_feat) cudaFree(m->d_feat);
+    m->d_feat = nullptr;
+    m->cap = 0;
+    const int feat = m->variant == TZ_LENET_PAD2 ? 400 : 256;
+    if (cudaMalloc(reinterpret_cast<void**>(&m->d_feat), sizeof(float) * feat * static_cast<size_t>(n)) != cudaSuccess)
+        return fail(TZ_ENOMEM, "tz_lenet: feature scratch for %lld images", static_cast<long long>(n));
+    m->cap = n;
+    return TZ_OK;
+}
+
+}  // namespace
+}  // namespace tz
+
+using namespace tz;
+
+extern "C" {
+
+int tz_lenet_load(tz_ctx_t ctx, const tz_lenet_weights* w, int variant, tz_lenet_t* out) {
+    TZ_CHECK(ctx && w && out && (variant == TZ_LENET_REF || variant == TZ_LENET_PAD2), TZ_EINVAL,
+             "tz_lenet_load: bad arguments");
+    *out = nullptr;
+    const float* req[] = {w->conv1_w, w->conv1_b, w->conv2_w, w->conv2_b, w->fc1_w,
+                          w->fc1_b,   w->fc2_w,   w->fc2_b,   w->fc3_w,   w->fc3_b};
+    for (const float* p : req) TZ_CHECK(p, TZ_EMISSING, "tz_lenet_load: a weight pointer is NULL");
+    const int feat = variant == TZ_LENET_PAD2 ? 400 : 256;
+    // device layout: conv1 [25][8] + [8], conv2 [25][6][16] + [16], FC weights as given
+    const size_t n_c1 = 25 * 8 + 8, n_c2 = 25 * 96 + 16, n_f1 = 120 * feat + 120, n_f2 = 84 * 120 + 84, n_f3 = 10 * 84 + 10;
+    const size_t total = n_c1 + n_c2 + n_f1 + n_f2 + n_f3;
+    float* h = new float[total];
+    std::memset(h, 0, sizeof(float) * total);
+    for (int tap = 0; tap < 25; ++tap)
+        for (int c = 0; c < 6; ++c) h[tap * 8 + c] = w->conv1_w[c * 25 + tap];  // [6,5,5,1] -> [tap][c]
+    for (int c = 0; c < 6; ++c) h[200 + c] = w->conv1_b[c];
+    float* c2 = h + n_c1;
+    for (int oc = 0; oc < 16; ++oc)
+        for (int tap = 0; tap < 25; ++tap)
+            for (int ic = 0; ic < 6; ++ic) c2[tap * 96 + ic * 16 + oc] = w->conv2_w[(oc * 25 + tap) * 6 + ic];
+    for (int oc = 0; oc < 16; ++oc) c2[2400 + oc] = w->conv2_b[oc];
+    float* f = c2 + n_c2;
+    std::memcpy(f, w->fc1_w, sizeof(float) * 120 * feat);
+    std::memcpy(f + 120 * feat, w->fc1_b, sizeof(float) * 120);
+    f += n_f1;
+    std::memcpy(f, w->fc2_w, sizeof(float) * 84 * 120);
+    std::memcpy(f + 84 * 120, w->fc2_b, sizeof(float) * 84);
+    f += n_f2;
+    std::memcpy(f, w->fc3_w, sizeof(float) * 840);
+    std::memcpy(f + 840, w->fc3_b, sizeof(float) * 10);
+
+    tz_lenet_s* m = new tz_lenet_s;
+    m->ctx = ctx;
+    m->device = ctx->device;
+    m->variant = variant;
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&m->d_w), sizeof(float) * total);
+    if (e == cudaSuccess) e = cudaMemcpy(m->d_w, h, sizeof(float) * total, cudaMemcpyHostToDevice);
+    delete[] h;
+    if (e != cudaSuccess) {
+        if (m->d_w) cudaFree(m->d_w);
+        delete m;
+        return cuda_fail(e, "tz_lenet_load");
+    }
+    m->c1w = m->d_w;
+    m->c1b = m->c1w + 200;
+    m->c2w = m->d_w + n_c1;
+    m->c2b = m->c2w + 2400;
+    m->f1w = m->c2w + n_c2;
+    m->f1b = m->f1w + 120 * feat;
+    m->f2w = m->f1w + n_f1;
+    m->f2b = m->f2w + 84 * 120;
+    m->f3w = m->f2w + n_f2;
+    m->f3b = m->f3w + 840;
+    *out = m;
+    return TZ_OK;
+}
+
+int tz_lenet_free(tz_lenet_t m) {
+    if (!m) return TZ_OK;
+    cudaSetDevice(m->device);
+    cudaDeviceSynchronize();
+    if (m->d_w) cudaFree(m->d_w);
+    if (m->d_feat) cudaFree(m->d_feat);
+    if (m->d_io) cudaFree(m->d_io);
+    delete m;
+    return TZ_OK;
+}
+
+int tz_lenet_reserve(tz_lenet_t m, int64_t n) {
+    TZ_CHECK(m && n >= 0, TZ_EINVAL, "tz_lenet_reserve: bad arguments");
+    return lenet_reserve(m, n);
+}
+
+int tz_lenet_forward_device(tz_lenet_t m, const float* images, int64_t n, float* out, tz_stream_t stream) {
+    TZ_CHECK(m && images && out && n >= 0, TZ_EINVAL, "tz_lenet_forward_device: bad arguments");
+    TZ_CHECK(reinterpret_cast<uintptr_t>(images) % 8 == 0, TZ_EINVAL, "tz_lenet_forward_device: images must be 8-byte aligned");
+    if (n == 0) return TZ_OK;
+    TZ_CUDA(cudaSetDevice(m->device));
+    int rc = lenet_reserve(m, n);
+    if (rc) return rc;
+    cudaStream_t s = pick_stream(m->ctx, stream);
+    return m->variant == TZ_LENET_PAD2 ? launch_lenet<2>(m, images, n, out, s) : launch_lenet<0>(m, images, n, out, s);
+}
+
+int tz_lenet_forward(tz_lenet_t m, const float* images, int64_t n, float* out) {
+    TZ_CHECK(m && images && out && n >= 0, TZ_EINVAL, "tz_lenet_forward: bad arguments");
+    if (n == 0) return TZ_OK;
+    TZ_CUDA(cudaSetDevice(m->device));
+    if (n > m->cap_io) {
+        TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+        if (m->d_io) cudaFree(m->d_io);
+        m->d_io = nullptr;
+        m->cap_io = 0;
+        if (cudaMalloc(reinterpret_cast<void**>(&m->d_io), sizeof(float) * 794 * static_cast<size_t>(n)) != cudaSuccess)
+            return fail(TZ_ENOMEM, "tz_lenet_forward: staging for %lld images", static_cast<long long>(n));
+        m->cap_io = n;
+    }
+    cudaStream_t s = m->ctx->stream;
+    float* d_img = m->d_io;
+    float* d_out = m->d_io + 784 * n;
+    TZ_CUDA(cudaMemcpyAsync(d_img, images, sizeof(float) * 784 * n, cudaMemcpyHostToDevice, s));
+    int rc = tz_lenet_forward_device(m, d_img, n, d_out, s);
+    if (rc) return rc;
+    TZ_CUDA(cudaMemcpyAsync(out, d_out, sizeof(float) * 10 * n, cudaMemcpyDeviceToHost, s));
+    TZ_CUDA(cudaStreamSynchronize(s));
+    return TZ_OK;
+}
+
+}  // extern "C"

@@ -132,3 +132,30 @@ def pack(ids: np.ndarray, lens: np.ndarray):
     cu[1:] = np.cumsum(lens)
     packed = np.concatenate([ids[b, : int(lens[b])] for b in range(len(lens))]).astype(np.uint32)
     return packed, cu
+
+
+# ---- LeNet-5 (lenet.zig) ----
+LENET_REF, LENET_PAD2 = 0, 1
+
+
+def lenet_weights(seed: int = 4321, variant: int = LENET_PAD2, random_bias: bool = False) -> dict:
+    """Kaiming-uniform LeNet-5 weights (init.zig:33-38: U(-a, a), a = sqrt(6 / fan_in)); biases 0
+    (initKaiming, lenet.zig:74-95) unless ``random_bias`` (parity tests).  Conv weights are
+    [out, kh, kw, in] (NHWC), FC weights [out, in]; FC1 takes 256 (lenet.zig) or 400 (pad-2
+    variant) features."""
+    feat = 400 if variant == LENET_PAD2 else 256
+    shapes = {"conv1_w": ((6, 5, 5, 1), 25), "conv2_w": ((16, 5, 5, 6), 150), "fc1_w": ((120, feat), feat),
+              "fc2_w": ((84, 120), 120), "fc3_w": ((10, 84), 84)}
+    w = {}
+    for i, (k, (shape, fan_in)) in enumerate(shapes.items()):
+        a = float(np.sqrt(6.0 / fan_in))
+        w[k] = uniform(seed * 101 + i, shape, -a, a)
+        b = k[:-2] + "_b"
+        n = shape[0]
+        w[b] = uniform(seed * 101 + 50 + i, (n,), -0.1, 0.1) if random_bias else np.zeros(n, np.float32)
+    return w
+
+
+def lenet_images(n: int, seed: int = 11) -> np.ndarray:
+    """n images [n, 28, 28, 1] f32, U[0, 1] pixels."""
+    return uniform(seed, (n, 28, 28, 1), 0.0, 1.0)
