@@ -13,7 +13,8 @@
 // shared memory, conv2+ReLU+pool writes the flattened features to global memory.  A thread owns one
 // pooled output position (all 6 channels for conv1; 8 of the 16 channels for conv2) and its four
 // pre-pool conv outputs, so every input value read feeds 24 (conv1) or 32 (conv2) FMAs and the
-// weights are warp-uniform shared-memory broadcasts.  lenet_fc_kernel: 64-image tiles; FC weights
+// weights are warp-uniform shared-memory broadcasts.  The inner products run on packed f32x2 FMAs
+// over output-channel pairs (each lane an IEEE fmaf).  lenet_fc_kernel: 64-image tiles; FC weights
 // staged through shared memory in K chunks (transposed so a thread's 8 outputs are contiguous),
 // 4 images x 8 outputs of register blocking per thread, ReLU fused, softmax per image at the end.
 // The work is FMA-bound (0.83 MFLOP per image for the padded variant), not HBM-bound (3 KB in).
@@ -23,6 +24,7 @@
 #include <cstring>
 
 #include "tz_internal.h"
+#include "tz_ptx.cuh"
 
 struct tz_lenet_s {
     tz_ctx_t ctx = nullptr;
@@ -91,44 +93,47 @@ __global__ void __launch_bounds__(kThreads)
         for (int item = tid; item < gcount * S::P1 * S::P1; item += kThreads) {
             const int g = item / (S::P1 * S::P1), r = item % (S::P1 * S::P1), py = r / S::P1, px = r % S::P1;
             const float* src = s_img + (g * S::PW + 2 * py) * S::PW + 2 * px;
-            float patch[6][6];
-#pragma unroll
-            for (int a = 0; a < 6; ++a)
-#pragma unroll
-                for (int b = 0; b < 6; b += 2) {
-                    const float2 v = *reinterpret_cast<const float2*>(src + a * S::PW + b);
-                    patch[a][b] = v.x;
-                    patch[a][b + 1] = v.y;
-                }
-            float acc[4][6];
+            uint64_t acc[4][3];  // channel pairs (0,1) (2,3) (4,5) of the four pre-pool positions
 #pragma unroll
             for (int p = 0; p < 4; ++p)
 #pragma unroll
-                for (int c = 0; c < 6; ++c) acc[p][c] = 0.0f;
+                for (int c = 0; c < 3; ++c) acc[p][c] = 0;
+#pragma unroll 1
+            for (int kh = 0; kh < 5; ++kh) {
+                float row[2][6];  // input rows 2py + kh and 2py + kh + 1, columns 2px .. 2px + 5
 #pragma unroll
-            for (int kh = 0; kh < 5; ++kh)
+                for (int a = 0; a < 2; ++a)
+#pragma unroll
+                    for (int b = 0; b < 6; b += 2) {
+                        const float2 v = *reinterpret_cast<const float2*>(src + (kh + a) * S::PW + b);
+                        row[a][b] = v.x;
+                        row[a][b + 1] = v.y;
+                    }
 #pragma unroll
                 for (int kw = 0; kw < 5; ++kw) {
-                    const float4 wa = *reinterpret_cast<const float4*>(s_w1 + (kh * 5 + kw) * 8);
-                    const float2 wb = *reinterpret_cast<const float2*>(s_w1 + (kh * 5 + kw) * 8 + 4);
-                    const float w[6] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y};
+                    const ulonglong2 wa = *reinterpret_cast<const ulonglong2*>(s_w1 + (kh * 5 + kw) * 8);
+                    const uint64_t wb = *reinterpret_cast<const uint64_t*>(s_w1 + (kh * 5 + kw) * 8 + 4);
 #pragma unroll
                     for (int p = 0; p < 4; ++p) {
-                        const float x = patch[(p >> 1) + kh][(p & 1) + kw];
-#pragma unroll
-                        for (int c = 0; c < 6; ++c) acc[p][c] = fmaf(x, w[c], acc[p][c]);
+                        const float x = row[p >> 1][(p & 1) + kw];
+                        const uint64_t xx = tzp::f2_pack(x, x);
+                        acc[p][0] = tzp::f2_fma(xx, wa.x, acc[p][0]);
+                        acc[p][1] = tzp::f2_fma(xx, wa.y, acc[p][1]);
+                        acc[p][2] = tzp::f2_fma(xx, wb, acc[p][2]);
                     }
                 }
+            }
             float* dst = s_p1 + ((g * S::P1 + py) * S::P1 + px) * 6;
 #pragma unroll
-            for (int c = 0; c < 6; c += 2) {
+            for (int c = 0; c < 3; ++c) {
                 float m0 = 0.0f, m1 = 0.0f;  // max over ReLU outputs (all >= 0)
 #pragma unroll
                 for (int p = 0; p < 4; ++p) {
-                    m0 = fmaxf(m0, s_b1[c] + acc[p][c]);
-                    m1 = fmaxf(m1, s_b1[c + 1] + acc[p][c + 1]);
+                    const float2 a = tzp::f2_unpack(acc[p][c]);
+                    m0 = fmaxf(m0, s_b1[2 * c] + a.x);
+                    m1 = fmaxf(m1, s_b1[2 * c + 1] + a.y);
                 }
-                *reinterpret_cast<float2*>(dst + c) = make_float2(m0, m1);
+                *reinterpret_cast<float2*>(dst + 2 * c) = make_float2(m0, m1);
             }
         }
         __syncthreads();
@@ -137,14 +142,14 @@ __global__ void __launch_bounds__(kThreads)
             const int half = item & 1, pos = item >> 1;
             const int g = pos / (S::P2 * S::P2), r = pos % (S::P2 * S::P2), py = r / S::P2, px = r % S::P2;
             const float* src = s_p1 + ((g * S::P1 + 2 * py) * S::P1 + 2 * px) * 6;
-            float acc[4][8];
+            uint64_t acc[4][4];  // output-channel pairs of the four pre-pool positions
 #pragma unroll
             for (int p = 0; p < 4; ++p)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[p][c] = 0.0f;
+                for (int c = 0; c < 4; ++c) acc[p][c] = 0;
 #pragma unroll 1
             for (int kh = 0; kh < 5; ++kh)
-#pragma unroll
+#pragma unroll 1
                 for (int kw = 0; kw < 5; ++kw) {
                     float x[4][6];
 #pragma unroll
@@ -160,20 +165,31 @@ __global__ void __launch_bounds__(kThreads)
                     const float* wt = s_w2 + (kh * 5 + kw) * 96 + half * 8;
 #pragma unroll
                     for (int ic = 0; ic < 6; ++ic) {
-                        const float4 wa = *reinterpret_cast<const float4*>(wt + ic * 16);
-                        const float4 wb = *reinterpret_cast<const float4*>(wt + ic * 16 + 4);
-                        const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                        const ulonglong2 wa = *reinterpret_cast<const ulonglong2*>(wt + ic * 16);
+                        const ulonglong2 wb = *reinterpret_cast<const ulonglong2*>(wt + ic * 16 + 4);
 #pragma unroll
-                        for (int p = 0; p < 4; ++p)
-#pragma unroll
-                            for (int c = 0; c < 8; ++c) acc[p][c] = fmaf(x[p][ic], w[c], acc[p][c]);
+                        for (int p = 0; p < 4; ++p) {
+                            const uint64_t xx = tzp::f2_pack(x[p][ic], x[p][ic]);
+                            acc[p][0] = tzp::f2_fma(xx, wa.x, acc[p][0]);
+                            acc[p][1] = tzp::f2_fma(xx, wa.y, acc[p][1]);
+                            acc[p][2] = tzp::f2_fma(xx, wb.x, acc[p][2]);
+                            acc[p][3] = tzp::f2_fma(xx, wb.y, acc[p][3]);
+                        }
                     }
                 }
             float m[8];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float b = s_b2[half * 8 + c];
-                m[c] = fmaxf(fmaxf(fmaxf(0.0f, b + acc[0][c]), b + acc[1][c]), fmaxf(b + acc[2][c], b + acc[3][c]));
+            for (int c = 0; c < 4; ++c) {
+                const float b0 = s_b2[half * 8 + 2 * c], b1 = s_b2[half * 8 + 2 * c + 1];
+                float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const float2 a = tzp::f2_unpack(acc[p][c]);
+                    m0 = fmaxf(m0, b0 + a.x);
+                    m1 = fmaxf(m1, b1 + a.y);
+                }
+                m[2 * c] = m0;
+                m[2 * c + 1] = m1;
             }
             float* dst = feat + (img0 + g) * S::FEAT + (py * S::P2 + px) * 16 + half * 8;
             *reinterpret_cast<float4*>(dst) = make_float4(m[0], m[1], m[2], m[3]);
