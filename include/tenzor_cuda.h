@@ -116,7 +116,9 @@ int tz_arctic_forward(tz_model_t model, const uint32_t* ids_packed, const int32_
 int tz_arctic_forward_padded(tz_model_t model, const uint32_t* ids, const int32_t* lengths,
                              int batch, int seq, float* out);
 /* Device-resident variant: all pointers on the device, asynchronous on `stream`.  total_tokens =
- * cu_seqlens[B] and max_len = max length must be passed by the caller (no host read-back).  The
+ * cu_seqlens[B] and max_len >= every length must be passed by the caller (no host read-back); a
+ * sequence longer than max_len is refused on the device (the bounds bit of the status word, so the
+ * next tz_cuda_check_status returns TZ_EINVAL) and its embedding is not valid.  The
  * launch sequence is captured into a CUDA graph on first use and replayed while the buffers, the
  * shape and the stream repeat (the legacy default stream is never captured). */
 int tz_arctic_forward_device(tz_model_t model, const uint32_t* d_ids_packed,

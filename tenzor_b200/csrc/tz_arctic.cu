@@ -137,8 +137,8 @@ __device__ __forceinline__ void emb_load(float (&v)[12], const float* f, const i
     }
 }
 
-// embeddingsImpl, arctic.zig:543-585: word[id] + pos[p] + type[0], then LayerNorm.  One CTA per
-// sequence, warp per token.  Ids >= vocab raise the bounds bit and embed row 0.
+// embeddingsImpl, arctic.zig:543-585: word[id] + pos[p] + type[0], then LayerNorm.  Grid (sequence,
+// 8-token chunk); one warp per token.  Ids >= vocab raise the bounds bit and embed row 0.
 template <int AUX>
 __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, EmbTables t,
                                 const float* __restrict__ g, const float* __restrict__ b, float* __restrict__ xo,
@@ -147,8 +147,9 @@ __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __r
     tzp::pdl_trigger();
     const int seq = blockIdx.x;
     const int s0 = cu[seq], L = cu[seq + 1] - s0;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int p = warp; p < L; p += nw) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p = blockIdx.y * (blockDim.x >> 5) + warp;  // this warp's token position
+    if (p < L) {
         const long long row = s0 + p;
         uint32_t id = ids[row];
         if (id >= static_cast<uint32_t>(kV)) {
@@ -523,10 +524,10 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
     if ((rc = prof_mark(m, P_EMBED, s))) return rc;
     const bool pdl = !m->profile;  // events between launches would break the programmatic edges anyway
     if (q8)
-        rc = launch_kernel(embed_ln_kernel<1>, dim3(B), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
+        rc = launch_kernel(embed_ln_kernel<1>, dim3(B, (maxL + 7) / 8), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
                            (const float*)m->emb_b, m->X, m->XA, m->xs, ctx->d_status);
     else
-        rc = launch_kernel(embed_ln_kernel<0>, dim3(B), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
+        rc = launch_kernel(embed_ln_kernel<0>, dim3(B, (maxL + 7) / 8), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
                            (const float*)m->emb_b, m->X, m->XA, (float*)nullptr, ctx->d_status);
     if (rc) return rc;
     if (m->keep_stages) TZ_CUDA(cudaMemcpyAsync(m->d_stages, m->X, sizeof(float) * T * kH, cudaMemcpyDeviceToDevice, s));

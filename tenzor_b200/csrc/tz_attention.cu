@@ -130,6 +130,10 @@ __global__ void __launch_bounds__(128)
     const int seq0 = cu_seqlens[b];
     const int L = cu_seqlens[b + 1] - seq0;
     const int q0 = blockIdx.x * kQTile;
+    if (L > lpad || L < 0) {  // the caller's max_len was too small: refuse rather than overrun shared memory
+        if (tid == 0 && blockIdx.x == 0) atomicOr(status, TZ_DEV_BOUNDS);
+        return;
+    }
     if (q0 >= L) return;  // uniform over the CTA
 
     const int kv_bytes = lpad * 64;

@@ -244,3 +244,26 @@ def test_device_forward_on_user_stream(models, c1):
                          s.cuda_stream)
     s.synchronize()
     assert (out.cpu().numpy() == ref).all()
+
+
+def test_device_forward_max_len_too_small_is_reported(ctx, models, c1):
+    """A caller's max_len below the longest sequence is caught on the device (status bounds bit)
+    instead of overrunning the attention kernel's shared memory; a correct call afterwards works."""
+    import torch
+    from tenzor_b200._lib import TenzorError
+    ids, lens, packed, cu = c1
+    m = models["w8a8"]
+    d_ids = torch.from_numpy(packed.view(np.int32)).cuda()
+    d_cu = torch.from_numpy(cu).cuda()
+    out = torch.empty((len(lens), 384), device="cuda")
+    s = torch.cuda.Stream()
+    assert lens.max() > 64  # max_len 32 sizes the attention staging for 64 keys
+    m.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), len(lens), int(cu[-1]), 32, out.data_ptr(), s.cuda_stream)
+    s.synchronize()
+    with pytest.raises(TenzorError):
+        ctx.check_status()
+    m.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), len(lens), int(cu[-1]), int(lens.max()), out.data_ptr(),
+                     s.cuda_stream)
+    s.synchronize()
+    ctx.check_status()
+    assert (out.cpu().numpy() == m.forward_packed(packed, cu)).all()
