@@ -183,10 +183,11 @@ __global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsi
     for (int col = lane * 8; col < cols; col += 256) {
         const uint4 raw = *reinterpret_cast<const uint4*>(xr + col);
         const __half* hv = reinterpret_cast<const __half*>(&raw);
-        const uint32_t w0 = pack_q4(quant1_bits(__half2float(hv[0]), inv), quant1_bits(__half2float(hv[1]), inv),
-                                    quant1_bits(__half2float(hv[2]), inv), quant1_bits(__half2float(hv[3]), inv));
-        const uint32_t w1 = pack_q4(quant1_bits(__half2float(hv[4]), inv), quant1_bits(__half2float(hv[5]), inv),
-                                    quant1_bits(__half2float(hv[6]), inv), quant1_bits(__half2float(hv[7]), inv));
+        const uint64_t inv2 = tzp::f2_pack(inv, inv);  // the row's own |max|: the fused gemm_ln arithmetic
+        const uint32_t w0 = __byte_perm(quant2_own_max(__half2float(hv[0]), __half2float(hv[1]), inv2),
+                                        quant2_own_max(__half2float(hv[2]), __half2float(hv[3]), inv2), 0x5410);
+        const uint32_t w1 = __byte_perm(quant2_own_max(__half2float(hv[4]), __half2float(hv[5]), inv2),
+                                        quant2_own_max(__half2float(hv[6]), __half2float(hv[7]), inv2), 0x5410);
         *reinterpret_cast<uint2*>(qr + col) = make_uint2(w0, w1);
     }
     __syncwarp();

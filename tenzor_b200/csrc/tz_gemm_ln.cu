@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float sc = (mx == 0.0f) ? 1.0f : __fdiv_rn(mx, 127.0f);
                     inv = __fdiv_rn(1.0f, sc);
                 }
+                const uint64_t inv2 = tzp::f2_pack(inv, inv);  // rows carry their own |max|: quant2_own_max applies
                 const uint4* src = reinterpret_cast<const uint4*>(p.a16 + static_cast<long long>(cok ? grow : 0) * p.lda16 + qq * 32);
                 uint4 x[4], x1[4];  // K blocks kb and kb + 1 in flight
 #pragma unroll
@@ -295,8 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 2; ++j) {
                             const float2 f0 = __half22float2(hp[2 * j]);
                             const float2 f1 = __half22float2(hp[2 * j + 1]);
-                            w[2 * i + j] = pack_q4(quant1_bits(f0.x, inv), quant1_bits(f0.y, inv), quant1_bits(f1.x, inv),
-                                                   quant1_bits(f1.y, inv));
+                            w[2 * i + j] = __byte_perm(quant2_own_max(f0.x, f0.y, inv2), quant2_own_max(f1.x, f1.y, inv2), 0x5410);
                         }
                     }
                     const uint32_t rowa = tzp::smem_u32(smem + cstage * C::STAGE_BYTES) + static_cast<uint32_t>(crow * 128);

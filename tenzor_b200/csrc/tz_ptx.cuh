@@ -165,6 +165,12 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+// Round toward -infinity (each lane an IEEE __fadd_rd).
+__device__ __forceinline__ uint64_t f2_add_rd(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));

@@ -150,7 +150,17 @@ __global__ void quant_rows_kernel(const float* x, int8_t* q, void* scale, long l
     }
     const float inv = __fdiv_rn(1.0f, s);
     int8_t* qr = q + row * cols;
-    for (int c = lane; c < cols; c += 32) qr[c] = quant1(xr[c], inv);
+    if constexpr (F16SCALE) {  // weights: the f16-rounded scale can put |x / s| a little past 127
+        for (int c = lane; c < cols; c += 32) qr[c] = quant1(xr[c], inv);
+    } else {  // activations: quantised against their own |max| (the form the fused GEMM path uses)
+        const uint64_t inv2 = tzp::f2_pack(inv, inv);
+        for (int c = 2 * lane; c < cols; c += 64) {
+            const float x1 = c + 1 < cols ? xr[c + 1] : 0.0f;
+            const uint32_t b = quant2_own_max(xr[c], x1, inv2);
+            qr[c] = static_cast<int8_t>(b & 0xFFu);
+            if (c + 1 < cols) qr[c + 1] = static_cast<int8_t>((b >> 8) & 0xFFu);
+        }
+    }
 }
 
 // ---- converters ---------------------------------------------------------------------------------

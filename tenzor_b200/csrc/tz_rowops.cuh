@@ -4,6 +4,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include "tz_ptx.cuh"
+
 #include "../../include/tenzor_cuda.h"
 
 namespace tz {
@@ -38,6 +40,21 @@ __device__ __forceinline__ uint32_t quant1_bits(float x, float inv) {
 
 __device__ __forceinline__ int8_t quant1(float x, float inv) {
     return static_cast<int8_t>(quant1_bits(x, inv) & 0xFFu);
+}
+
+// quant1 of two values at once on packed f32x2 instructions, for a row quantised against its own
+// |max| (|x| <= max, so |x * inv| exceeds 127 by at most one rounding and quant1's clamp cannot
+// act: the same bytes as quant1 for every finite x; a NaN gives 0 where quant1 gives -127).  The
+// two int8 results are returned in bytes 0 and 1.
+__device__ __forceinline__ uint32_t quant2_own_max(float x0, float x1, uint64_t inv2) {
+    const uint64_t half2 = 0x3F0000003F000000ull;   // (0.5, 0.5)
+    const uint64_t two23 = 0x4B0000004B000000ull;   // (2^23, 2^23)
+    const uint64_t magic = 0x4B4000004B400000ull;   // (1.5 * 2^23, 1.5 * 2^23)
+    const uint64_t v = tzp::f2_mul(tzp::f2_pack(x0, x1), inv2);
+    const uint64_t a = v & 0x7FFFFFFF7FFFFFFFull;
+    const uint64_t f = tzp::f2_sub(tzp::f2_add_rd(tzp::f2_add_rd(a, half2), two23), two23);
+    const uint64_t u = tzp::f2_add(f | (v & 0x8000000080000000ull), magic);
+    return __byte_perm(static_cast<uint32_t>(u), static_cast<uint32_t>(u >> 32), 0x0040) & 0xFFFFu;
 }
 
 // Low bytes of four quant1_bits results packed little-endian into one word.
