@@ -329,7 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 
             // ---- pass A: x = dequant(acc) + bias + residual -> TMEM; row sum ----
-            float sum = 0.f;
+            const uint64_t rs2 = tzp::f2_pack(rs, rs);
+            uint64_t sum2 = 0;  // (even columns, odd columns)
             bool bad = false;
 #pragma unroll
             for (int c = 0; c < kSlice / 16; ++c) {
@@ -354,60 +355,56 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tzp::tmem_ld_wait();
                 const int col = c0 + 16 * c;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float v[4] = {acc_to_f<KIND>(r[4 * j]), acc_to_f<KIND>(r[4 * j + 1]), acc_to_f<KIND>(r[4 * j + 2]),
-                                  acc_to_f<KIND>(r[4 * j + 3])};
-                    if (AQ || p.row_scale) {
-                        const float4 cs = *reinterpret_cast<const float4*>(sv_cs + col + 4 * j);
-                        v[0] = __fmul_rn(v[0], __fmul_rn(rs, cs.x));
-                        v[1] = __fmul_rn(v[1], __fmul_rn(rs, cs.y));
-                        v[2] = __fmul_rn(v[2], __fmul_rn(rs, cs.z));
-                        v[3] = __fmul_rn(v[3], __fmul_rn(rs, cs.w));
-                    } else if (p.col_scale) {
-                        const float4 cs = *reinterpret_cast<const float4*>(sv_cs + col + 4 * j);
-                        v[0] = __fmul_rn(v[0], cs.x);
-                        v[1] = __fmul_rn(v[1], cs.y);
-                        v[2] = __fmul_rn(v[2], cs.z);
-                        v[3] = __fmul_rn(v[3], cs.w);
-                    }
-                    const float4 bv = *reinterpret_cast<const float4*>(sv_bias + col + 4 * j);
-                    v[0] = __fadd_rn(__fadd_rn(v[0], bv.x), cur[j].x);
-                    v[1] = __fadd_rn(__fadd_rn(v[1], bv.y), cur[j].y);
-                    v[2] = __fadd_rn(__fadd_rn(v[2], bv.z), cur[j].z);
-                    v[3] = __fadd_rn(__fadd_rn(v[3], bv.w), cur[j].w);
-                    sum += (v[0] + v[1]) + (v[2] + v[3]);
-                    r[4 * j] = __float_as_uint(v[0]);
-                    r[4 * j + 1] = __float_as_uint(v[1]);
-                    r[4 * j + 2] = __float_as_uint(v[2]);
-                    r[4 * j + 3] = __float_as_uint(v[3]);
+                for (int j = 0; j < 8; ++j) {  // column pairs on packed f32x2 arithmetic
+                    uint64_t x = tzp::f2_pack(acc_to_f<KIND>(r[2 * j]), acc_to_f<KIND>(r[2 * j + 1]));
+                    const uint64_t cs2 = *reinterpret_cast<const uint64_t*>(sv_cs + col + 2 * j);
+                    if (AQ || p.row_scale)
+                        x = tzp::f2_mul(x, tzp::f2_mul(rs2, cs2));
+                    else if (p.col_scale)
+                        x = tzp::f2_mul(x, cs2);
+                    const uint64_t b2 = *reinterpret_cast<const uint64_t*>(sv_bias + col + 2 * j);
+                    const uint64_t res2 = reinterpret_cast<const uint64_t*>(cur)[j];
+                    x = tzp::f2_add(tzp::f2_add(x, b2), res2);
+                    sum2 = tzp::f2_add(sum2, x);
+                    const float2 v = tzp::f2_unpack(x);
+                    r[2 * j] = __float_as_uint(v.x);
+                    r[2 * j + 1] = __float_as_uint(v.y);
                 }
                 tzp::tmem_st16(tbase + 16 * c, r);
             }
             if (bad) break;
             tzp::tmem_st_wait();
-            red_sum[slice * 128 + rloc] = sum;
+            {
+                const float2 sp = tzp::f2_unpack(sum2);
+                red_sum[slice * 128 + rloc] = sp.x + sp.y;
+            }
             if (!epi_sync(&red_bar[0], tphase, lane, status)) break;
             const float mean =
                 ((red_sum[rloc] + red_sum[128 + rloc]) + (red_sum[256 + rloc] + red_sum[384 + rloc])) / static_cast<float>(kN);
 
             // ---- pass B: sum of squared deviations ----
-            float ssq = 0.f;
+            const uint64_t mean2 = tzp::f2_pack(mean, mean);
+            uint64_t ssq2 = 0;
 #pragma unroll
             for (int c = 0; c < kSlice / 16; ++c) {
                 uint32_t r[16];
                 tzp::tmem_ld16(tbase + 16 * c, r);
                 tzp::tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const float d = __uint_as_float(r[j]) - mean;
-                    ssq += d * d;
+                for (int j = 0; j < 8; ++j) {
+                    const uint64_t d = tzp::f2_sub(tzp::f2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), mean2);
+                    ssq2 = tzp::f2_fma(d, d, ssq2);
                 }
             }
-            red_ssq[slice * 128 + rloc] = ssq;
+            {
+                const float2 sp = tzp::f2_unpack(ssq2);
+                red_ssq[slice * 128 + rloc] = sp.x + sp.y;
+            }
             if (!epi_sync(&red_bar[1], tphase, lane, status)) break;
             const float var =
                 ((red_ssq[rloc] + red_ssq[128 + rloc]) + (red_ssq[256 + rloc] + red_ssq[384 + rloc])) / static_cast<float>(kN);
             const float inv_std = 1.0f / sqrtf(var + p.eps);
+            const uint64_t istd2 = tzp::f2_pack(inv_std, inv_std);
 
             // ---- pass C: normalise, store x_out (+ f16 aux, or y -> TMEM and |max|) ----
             float amax = 0.f;
@@ -419,13 +416,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int col = c0 + 16 * c;
                 float y[16];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float4 g = *reinterpret_cast<const float4*>(sv_g + col + 4 * j);
-                    const float4 bb = *reinterpret_cast<const float4*>(sv_b + col + 4 * j);
-                    y[4 * j] = (__uint_as_float(r[4 * j]) - mean) * inv_std * g.x + bb.x;
-                    y[4 * j + 1] = (__uint_as_float(r[4 * j + 1]) - mean) * inv_std * g.y + bb.y;
-                    y[4 * j + 2] = (__uint_as_float(r[4 * j + 2]) - mean) * inv_std * g.z + bb.z;
-                    y[4 * j + 3] = (__uint_as_float(r[4 * j + 3]) - mean) * inv_std * g.w + bb.w;
+                for (int j = 0; j < 8; ++j) {  // y = (x - mean) * inv_std * gamma + beta on column pairs
+                    const uint64_t x = tzp::f2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                    const uint64_t g2 = *reinterpret_cast<const uint64_t*>(sv_g + col + 2 * j);
+                    const uint64_t b2 = *reinterpret_cast<const uint64_t*>(sv_b + col + 2 * j);
+                    const float2 v = tzp::f2_unpack(tzp::f2_fma(tzp::f2_mul(tzp::f2_sub(x, mean2), istd2), g2, b2));
+                    y[2 * j] = v.x;
+                    y[2 * j + 1] = v.y;
                 }
                 {  // x_out chunks in pairs -> the two staging boxes (64-byte swizzle) -> one proxy fence and two
                    // TMA stores per pair (rows >= M are clipped)
@@ -473,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float m = fmaxf(fmaxf(red_max[rloc], red_max[128 + rloc]), fmaxf(red_max[256 + rloc], red_max[384 + rloc]));
                 const float sc = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
                 const float inv = __fdiv_rn(1.0f, sc);
+                const uint64_t inv2 = tzp::f2_pack(inv, inv);
                 // this warp's 32 x 96 int8 block, row-major (96-byte rows) in its staging boxes once the
                 // x_out stores have read them, then one TMA store
                 if (lane == 0) tzp::bulk_wait_read<0>();
@@ -483,11 +481,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t r[16];
                     tzp::tmem_ld16(tbase + 16 * c, r);
                     tzp::tmem_ld_wait();
-                    uint32_t w[4];
+                    uint32_t w[4];  // rows quantised against their own |max|: the packed form applies
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        w[j] = pack_q4(quant1_bits(__uint_as_float(r[4 * j]), inv), quant1_bits(__uint_as_float(r[4 * j + 1]), inv),
-                                       quant1_bits(__uint_as_float(r[4 * j + 2]), inv), quant1_bits(__uint_as_float(r[4 * j + 3]), inv));
+                        w[j] = __byte_perm(quant2_own_max(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), inv2),
+                                           quant2_own_max(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]), inv2), 0x5410);
                     *reinterpret_cast<uint4*>(qrow + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
                 tzp::fence_proxy_async();
