@@ -71,7 +71,7 @@ __device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __res
         v[4 * c + 1] = (v[4 * c + 1] - mean) * inv_std * gg.y + bb.y;
         v[4 * c + 2] = (v[4 * c + 2] - mean) * inv_std * gg.z + bb.z;
         v[4 * c + 3] = (v[4 * c + 3] - mean) * inv_std * gg.w + bb.w;
-        *reinterpret_cast<float4*>(xo + row * kH + col) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        *reinterpret_cast<float4*>(xo + xblk(row, col)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[4 * c]), fabsf(v[4 * c + 1])), fmaxf(fabsf(v[4 * c + 2]), fabsf(v[4 * c + 3]))));
     }
     if constexpr (AUX == 0) {
@@ -205,12 +205,12 @@ __global__ void pool_l2_kernel(const float* __restrict__ x, const int* __restric
     const int seq = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (seq >= batch) return;
-    const float* r = x + static_cast<long long>(cu[seq]) * kH;
+    const long long row = cu[seq];  // the CLS token (position 0) of the sequence
     float v[12];
     float s = 0.f;
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
-        const float4 t = *reinterpret_cast<const float4*>(r + c * 128 + lane * 4);
+        const float4 t = *reinterpret_cast<const float4*>(x + xblk(row, c * 128 + lane * 4));
         v[4 * c] = t.x;
         v[4 * c + 1] = t.y;
         v[4 * c + 2] = t.z;
@@ -444,7 +444,7 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
     };
     A(sizeof(uint32_t) * T, reinterpret_cast<void**>(&m->d_ids));
     A(sizeof(int) * (nb + 1), reinterpret_cast<void**>(&m->d_cu));
-    A(sizeof(float) * T * kH, reinterpret_cast<void**>(&m->X));
+    A(sizeof(float) * xblk_rows(static_cast<long long>(T)) * kH, reinterpret_cast<void**>(&m->X));  // blocked (xblk)
     A(sizeof(__half) * T * 3 * kH, &m->QKV);
     A(sizeof(float) * nb * kH, reinterpret_cast<void**>(&m->out));
     if (m->mode == TZ_QUANT_W8A8) {
@@ -465,7 +465,7 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
         A(sizeof(__half) * T * kF, &m->Hh);
     }
     if (m->keep_stages) {
-        A(sizeof(float) * 7 * T * kH, reinterpret_cast<void**>(&m->d_stages));
+        A(sizeof(float) * 7 * xblk_rows(static_cast<long long>(T)) * kH, reinterpret_cast<void**>(&m->d_stages));
         if (m->mode == TZ_QUANT_W8A8)
             for (int i = 0; i < 4; ++i) {
                 A(T * (i == 3 ? kF : kH), reinterpret_cast<void**>(&m->d_opq[i]));
@@ -531,7 +531,8 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         rc = launch_kernel(embed_ln_kernel<0>, dim3(B, (maxL + 7) / 8), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
                            (const float*)m->emb_b, m->X, m->XA, (float*)nullptr, ctx->d_status);
     if (rc) return rc;
-    if (m->keep_stages) TZ_CUDA(cudaMemcpyAsync(m->d_stages, m->X, sizeof(float) * T * kH, cudaMemcpyDeviceToDevice, s));
+    if (m->keep_stages)
+        TZ_CUDA(cudaMemcpyAsync(m->d_stages, m->X, sizeof(float) * xblk_rows(T) * kH, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < kLayers; ++l) {
         const DevLayer& L = m->layers[l];
         GemmArgs g;
@@ -594,7 +595,8 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if ((rc = prof_mark(m, P_FFN2, s))) return rc;
         if ((rc = launch_gemm_ln(ctx, f2, s))) return rc;
         if (m->keep_stages)
-            TZ_CUDA(cudaMemcpyAsync(m->d_stages + static_cast<size_t>(l + 1) * m->cap_tokens * kH, m->X, sizeof(float) * T * kH,
+            TZ_CUDA(cudaMemcpyAsync(m->d_stages + static_cast<size_t>(l + 1) * xblk_rows(m->cap_tokens) * kH, m->X,
+                                    sizeof(float) * xblk_rows(T) * kH,
                                     cudaMemcpyDeviceToDevice, s));
     }
     if ((rc = prof_mark(m, P_POOL, s))) return rc;
@@ -843,9 +845,13 @@ int tz_arctic_debug_hidden(tz_model_t m, int stage, float* out, int64_t T) {
         return fail(TZ_EINVAL, "stage capture was off; it is on from the next forward");
     }
     TZ_CHECK(m->d_stages && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
-    TZ_CUDA(cudaMemcpyAsync(out, m->d_stages + static_cast<size_t>(stage) * m->cap_tokens * kH, sizeof(float) * T * kH,
-                            cudaMemcpyDeviceToHost, m->ctx->stream));
+    // the device copy is in the blocked layout of xblk: download it whole and reorder into [T, 384]
+    std::vector<float> blk(static_cast<size_t>(xblk_rows(T)) * kH);
+    TZ_CUDA(cudaMemcpyAsync(blk.data(), m->d_stages + static_cast<size_t>(stage) * xblk_rows(m->cap_tokens) * kH,
+                            sizeof(float) * blk.size(), cudaMemcpyDeviceToHost, m->ctx->stream));
     TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    for (int64_t r = 0; r < T; ++r)
+        for (int c = 0; c < kH; ++c) out[static_cast<size_t>(r) * kH + c] = blk[static_cast<size_t>(xblk(r, c))];
     return TZ_OK;
 }
 

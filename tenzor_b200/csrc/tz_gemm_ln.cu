@@ -14,9 +14,9 @@
 // warps 2..17 epilogue: warp w reads TMEM lane quarter (w % 4) and a 96-column slice.  Per row:
 // pass A dequantises, adds bias and residual, writes x back into TMEM and sums; pass B sums squared
 // deviations; pass C normalises and stores x_out (+ f16 aux, or y back to TMEM and |max|); pass D
-// (AUX = 1) quantises.  Residual tiles arrive and x_out tiles leave as 32-row x 16-column TMA boxes
-// (double-buffered per warp), so no thread touches a residual or output row in global memory
-// directly.  The four slices of a row combine their partial sums through shared memory
+// (AUX = 1) quantises.  The residual stream is in the blocked layout of xblk (tz_internal.h): a
+// warp's 32 x 16 residual chunk is 2 KB contiguous and arrives by one 1-D bulk copy (two in flight
+// per warp), and its x_out chunk leaves as four coalesced 512-byte stores.  The four slices of a row combine their partial sums through shared memory
 // at mbarriers (bounded waits, one phase per tile).  No separate LayerNorm launch and no round trip
 // of the pre-LN activations.
 #include <cuda.h>
@@ -31,7 +31,7 @@ namespace tz {
 namespace {
 
 constexpr int kN = 384, kHalf = 192, kStages = 2, kEpiWarps = 16, kThreads = 64 + 32 * kEpiWarps;
-constexpr int kBox = 32 * 16 * 4;  // one 32-row x 16-column f32 tile: a TMA box of the residual / output
+constexpr int kBox = 32 * 16 * 4;  // one 32-row x 16-column f32 chunk of the residual (2 KB, contiguous in xblk form)
 constexpr int kSlice = kN / 4;  // 96 columns per epilogue warp
 
 struct LnParams {
@@ -89,7 +89,6 @@ __device__ __forceinline__ float acc_to_f(uint32_t r) {
 template <int KIND, int AUX, int AQ>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmX,
                    const __grid_constant__ CUtensorMap tmAux, int M, int K,
                    LnParams p, int* status) {
     using C = LnCfg<KIND>;
@@ -132,8 +131,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tzp::fence_mbar_init();
         tzp::tma_prefetch_desc(&tmA);
         tzp::tma_prefetch_desc(&tmB);
-        tzp::tma_prefetch_desc(&tmRes);
-        tzp::tma_prefetch_desc(&tmX);
         if (AUX == 1) tzp::tma_prefetch_desc(&tmAux);
     }
     if (warp == 1) {
@@ -246,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tzp::bulk_wait_read<0>();
                 for (int b = 0; b < 2; ++b) {
                     tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
-                    tzp::tma_load_2d(box[b], &tmRes, c0 + 16 * b, row0, &rbar[b]);
+                    tzp::bulk_load_1d(box[b], p.residual + xblk(row0, c0 + 16 * b), kBox, &rbar[b]);
                 }
             }
             __syncwarp();
@@ -346,11 +343,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float4 cur[4];  // this row's 16 residual values (64-byte swizzle of the TMA box)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    cur[j] = *reinterpret_cast<const float4*>(box[b] + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
+                    cur[j] = *reinterpret_cast<const float4*>(box[b] + j * 512 + lane * 16);  // quad j, this row
                 __syncwarp();
                 if (lane == 0 && c + 2 < kSlice / 16) {  // refill this box with chunk c + 2
                     tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
-                    tzp::tma_load_2d(box[b], &tmRes, c0 + 16 * (c + 2), row0, &rbar[b]);
+                    tzp::bulk_load_1d(box[b], p.residual + xblk(row0, c0 + 16 * (c + 2)), kBox, &rbar[b]);
                 }
                 tzp::tmem_ld_wait();
                 const int col = c0 + 16 * c;
@@ -424,26 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     y[2 * j] = v.x;
                     y[2 * j + 1] = v.y;
                 }
-                {  // x_out chunks in pairs -> the two staging boxes (64-byte swizzle) -> one proxy fence and two
-                   // TMA stores per pair (rows >= M are clipped)
-                    const int b = c & 1;
-                    if (b == 0) {
-                        if (lane == 0) tzp::bulk_wait_read<0>();  // the previous pair's stores have read both boxes
-                        __syncwarp();
-                    }
+                {  // x_out: four coalesced 512-byte stores (blocked layout; padding rows of the last tile too)
+                    float* xq = p.x_out + xblk(row0, col) + lane * 4;
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        *reinterpret_cast<float4*>(box[b] + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
-                            make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-                    if (b == 1) {
-                        tzp::fence_proxy_async();
-                        __syncwarp();
-                        if (lane == 0) {
-                            tzp::tma_store_2d(&tmX, box[0], col - 16, row0);
-                            tzp::tma_store_2d(&tmX, box[1], col, row0);
-                            tzp::bulk_commit();
-                        }
-                    }
+                        *reinterpret_cast<float4*>(xq + j * 128) = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
                 }
                 if constexpr (AUX == 0) {
                     if (ok) {
@@ -545,14 +527,7 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     rc = encode_tmap_2d(&tb, dtype_of(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.K), kN,
                         static_cast<uint64_t>(g.ldb) * C::ELEM, C::BK, kHalf);
     if (rc) return rc;
-    CUtensorMap tr, tx;
-    rc = encode_tmap_2d_swz(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.residual, kN, static_cast<uint64_t>(g.M), kN * 4, 16, 32,
-                            CU_TENSOR_MAP_SWIZZLE_64B);
-    if (rc) return rc;
-    rc = encode_tmap_2d_swz(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.x_out, kN, static_cast<uint64_t>(g.M), kN * 4, 16, 32,
-                            CU_TENSOR_MAP_SWIZZLE_64B);
-    if (rc) return rc;
-    CUtensorMap tq = tx;  // AUX = 1: the int8 LayerNorm output [M, 384], one 96 x 32 box per epilogue warp
+    CUtensorMap tq = tb;  // AUX = 1: the int8 LayerNorm output [M, 384], one 96 x 32 box per epilogue warp
     if (AUX == 1) {
         rc = encode_tmap_2d_swz(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.aux, kN, static_cast<uint64_t>(g.M), kN, kSlice, 32,
                                 CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -564,7 +539,7 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     const int tiles = (g.M + 127) / 128;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
-    return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, tr, tx, tq, g.M, g.K, p, ctx->d_status);
+    return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, tq, g.M, g.K, p, ctx->d_status);
 }
 
 }  // namespace
@@ -575,6 +550,8 @@ int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     TZ_CHECK(g.a && g.b && g.bias && g.residual && g.gamma && g.beta && g.x_out && g.aux, TZ_EINVAL, "gemm_ln: null operand");
     TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm_ln: row_scale needs col_scale");
     TZ_CHECK(g.aux_int8 == (g.aux_scale != nullptr), TZ_EINVAL, "gemm_ln: int8 aux needs its scale vector");
+    TZ_CHECK(reinterpret_cast<uintptr_t>(g.residual) % 16 == 0 && reinterpret_cast<uintptr_t>(g.x_out) % 16 == 0, TZ_EINVAL,
+             "gemm_ln: the blocked residual stream must be 16-byte aligned");
     if (g.a_absmax) {
         TZ_CHECK(g.kind == KIND_I8 && g.aux_int8 && !g.row_scale && g.col_scale, TZ_EINVAL,
                  "gemm_ln: in-kernel A quantisation needs the int8 kind, int8 aux, column scales and no row scales");

@@ -113,6 +113,15 @@ struct GemmArgs {
 int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s);
 
 // GEMM with N = 384 whose epilogue adds bias + residual and applies LayerNorm (tz_gemm_ln.cu).
+// The model's residual stream X [rows, 384] f32 in blocked form: per group of 32 rows, 96 column
+// quads, each quad 32 rows x 4 floats (512 contiguous bytes).  A warp that owns 32 rows (one per
+// lane) reads or writes a 16-column chunk as four fully coalesced 512-byte accesses.  Buffers hold
+// whole 128-row tiles (rows rounded up to a multiple of 128).
+__host__ __device__ __forceinline__ long long xblk(long long row, int col) {
+    return (((row >> 5) * 96 + (col >> 2)) << 7) + ((row & 31) << 2) + (col & 3);
+}
+inline long long xblk_rows(long long rows) { return (rows + 127) / 128 * 128; }
+
 struct GemmLnArgs {
     int kind = KIND_F16;
     const void* a = nullptr;  // [M, K]
@@ -122,11 +131,11 @@ struct GemmLnArgs {
     const float* bias = nullptr;       // [384]
     const float* col_scale = nullptr;  // [384]
     const float* row_scale = nullptr;  // [M]
-    const float* residual = nullptr;   // [M, 384] f32 (may alias x_out)
+    const float* residual = nullptr;   // [M, 384] f32, blocked (xblk), may alias x_out
     const float* gamma = nullptr;
     const float* beta = nullptr;
     float eps = 1e-12f;
-    float* x_out = nullptr;            // [M, 384] f32
+    float* x_out = nullptr;            // [M, 384] f32, blocked (xblk)
     void* aux = nullptr;               // [M, 384] f16 or int8
     float* aux_scale = nullptr;        // [M] when aux is int8
     bool aux_int8 = false;
