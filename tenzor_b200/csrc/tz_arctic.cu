@@ -48,8 +48,12 @@ constexpr float kEps = 1e-12f;  // arctic.zig:37
 
 // AUX: 0 = f16 copy, 1 = int8 + per-token scale.
 template <int AUX>
+// LayerNorm of one row held as 12 values per lane (columns lane*4 + 128c .. +3); the f32 result
+// goes to `xrow` (a 384-float shared-memory row whose 16-byte quads are XOR-swizzled by row % 8, so
+// the column-quad reads of 8 consecutive rows hit distinct banks), the next GEMM's operand (f16, or
+// int8 + scale) to global memory.
 __device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __restrict__ g, const float* __restrict__ b,
-                                              float* xo, void* aux, float* aux_s, long long row, int lane) {
+                                              float* xrow, void* aux, float* aux_s, long long row, int lane) {
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < 12; ++i) s += v[i];
@@ -71,7 +75,8 @@ __device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __res
         v[4 * c + 1] = (v[4 * c + 1] - mean) * inv_std * gg.y + bb.y;
         v[4 * c + 2] = (v[4 * c + 2] - mean) * inv_std * gg.z + bb.z;
         v[4 * c + 3] = (v[4 * c + 3] - mean) * inv_std * gg.w + bb.w;
-        *reinterpret_cast<float4*>(xo + xblk(row, col)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        *reinterpret_cast<float4*>(xrow + (((col >> 2) ^ static_cast<int>(row & 7)) << 2)) =
+            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[4 * c]), fabsf(v[4 * c + 1])), fmaxf(fabsf(v[4 * c + 2]), fabsf(v[4 * c + 3]))));
     }
     if constexpr (AUX == 0) {
@@ -137,20 +142,35 @@ __device__ __forceinline__ void emb_load(float (&v)[12], const float* f, const i
     }
 }
 
-// embeddingsImpl, arctic.zig:543-585: word[id] + pos[p] + type[0], then LayerNorm.  Grid (sequence,
-// 8-token chunk); one warp per token.  Ids >= vocab raise the bounds bit and embed row 0.
+// embeddingsImpl, arctic.zig:543-585: word[id] + pos[p] + type[0], then LayerNorm.  CTA = one
+// 32-row group of the packed tokens (8 warps x 4 tokens); a token's sequence (for its
+// position) comes from a binary search of cu_seqlens.  The LayerNorm rows are assembled in shared
+// memory and leave in the blocked layout of xblk as coalesced 512-byte stores; rows past the batch
+// are written as zeros.  Ids >= vocab raise the bounds bit and embed row 0.
 template <int AUX>
-__global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, EmbTables t,
-                                const float* __restrict__ g, const float* __restrict__ b, float* __restrict__ xo,
-                                void* aux, float* aux_s, int* status) {
+__global__ void __launch_bounds__(256)
+    embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, int batch, long long total, EmbTables t,
+                    const float* __restrict__ g, const float* __restrict__ b, float* __restrict__ xo, void* aux,
+                    float* aux_s, int* status) {
+    __shared__ __align__(16) float tile[32 * kH];
     tzp::pdl_wait();
     tzp::pdl_trigger();
-    const int seq = blockIdx.x;
-    const int s0 = cu[seq], L = cu[seq + 1] - s0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int p = blockIdx.y * (blockDim.x >> 5) + warp;  // this warp's token position
-    if (p < L) {
-        const long long row = s0 + p;
+    const long long g0 = static_cast<long long>(blockIdx.x) * 32;
+    for (int i = 0; i < 4; ++i) {
+        const int r = warp * 4 + i;
+        const long long row = g0 + r;
+        float* xrow = tile + r * kH;
+        if (row >= total) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) *reinterpret_cast<float4*>(xrow + c * 128 + lane * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+        int lo = 0, hi = batch;  // the sequence s with cu[s] <= row < cu[s + 1]
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (cu[mid] <= row) lo = mid; else hi = mid;
+        }
+        const int p = static_cast<int>(row - cu[lo]);
         uint32_t id = ids[row];
         if (id >= static_cast<uint32_t>(kV)) {
             if (lane == 0) atomicOr(status, TZ_DEV_BOUNDS);
@@ -161,8 +181,14 @@ __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __r
         emb_load(v, t.word_f, t.word_q, t.word_s, static_cast<int>(id), lane, false);
         emb_load(v, t.pos_f, t.pos_q, t.pos_s, pos, lane, true);
         emb_load(v, t.type_f, nullptr, nullptr, 0, lane, true);
-        ln_finish_row<AUX>(v, g, b, xo, aux, aux_s, row, lane);
+        ln_finish_row<AUX>(v, g, b, xrow, aux, aux_s, row, lane);
+        }
     }
+    __syncthreads();
+    // blocked write-out: quad q of the group is 32 rows x 16 bytes, contiguous; lane = row
+    float* dst = xo + xblk(g0, 0);
+    for (int q = warp; q < kH / 4; q += 8)
+        *reinterpret_cast<float4*>(dst + q * 128 + lane * 4) = *reinterpret_cast<const float4*>(tile + lane * kH + ((q ^ (lane & 7)) << 2));
 }
 
 // W8A8 per-token requantisation of an f16 activation X [rows, cols] whose row |max| (float bits) was
@@ -525,10 +551,12 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
     if ((rc = prof_mark(m, P_EMBED, s))) return rc;
     const bool pdl = !m->profile;  // events between launches would break the programmatic edges anyway
     if (q8)
-        rc = launch_kernel(embed_ln_kernel<1>, dim3(B, (maxL + 7) / 8), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
+        rc = launch_kernel(embed_ln_kernel<1>, dim3(static_cast<unsigned>((T + 31) / 32)), dim3(256), 0, s, pdl, d_ids, d_cu, B,
+                           static_cast<long long>(T), m->emb, (const float*)m->emb_g,
                            (const float*)m->emb_b, m->X, m->XA, m->xs, ctx->d_status);
     else
-        rc = launch_kernel(embed_ln_kernel<0>, dim3(B, (maxL + 7) / 8), dim3(256), 0, s, pdl, d_ids, d_cu, m->emb, (const float*)m->emb_g,
+        rc = launch_kernel(embed_ln_kernel<0>, dim3(static_cast<unsigned>((T + 31) / 32)), dim3(256), 0, s, pdl, d_ids, d_cu, B,
+                           static_cast<long long>(T), m->emb, (const float*)m->emb_g,
                            (const float*)m->emb_b, m->X, m->XA, (float*)nullptr, ctx->d_status);
     if (rc) return rc;
     if (m->keep_stages)
