@@ -114,6 +114,12 @@ struct Cfg {
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int SLICES = EPI_WARPS / 4;             // warps sharing one TMEM lane quarter
     static constexpr int COLS_PER_WARP = BN / SLICES;
+    // The specialised epilogue: two sets of a warp's f16 output boxes (tile t's stores drain while
+    // tile t+1 is staged) + its column vectors.
+    // (rounded to 256 bytes: every box starts on a whole 32-byte-swizzle atom)
+    static constexpr int FAST_WARP_BYTES = (2 * (COLS_PER_WARP / CW) * (32 * CW * 2) + 2 * COLS_PER_WARP * 4 + 255) / 256 * 256;
+    static constexpr int FAST_STAGING = EPI_WARPS * FAST_WARP_BYTES;
+    static constexpr int SMEM_FAST = STAGES * STAGE_BYTES + FAST_STAGING + BAR_BYTES + 1024;
     static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
     static_assert(EPI_WARPS % 4 == 0 && COLS_PER_WARP % CW == 0, "epilogue split");
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     const uint32_t raw_addr = tzp::smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + (FAST != 0 ? C::FAST_STAGING : C::STAGING));
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -420,19 +426,19 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         // scales (into this warp's staging area, read back as broadcasts).  Then the NCH chunks of
         // 16 columns: TMEM load of chunk c+1 in flight while chunk c is converted and staged; the
         // accumulator is released as soon as its last chunk is in registers; one proxy fence and NCH
-        // TMA stores per tile.  The arithmetic runs on packed f32x2 instructions (bit-identical to
+        // TMA stores per tile, staged in one of two box sets so that they drain while the next tile
+        // is staged (three operand stages leave room for the second set).  The arithmetic runs on packed f32x2 instructions (bit-identical to
         // the scalar forms) and |max| is taken on the packed f16 results.
         constexpr int CPW = C::COLS_PER_WARP;
         constexpr int NCH = CPW / CW;
         constexpr int BOX = 32 * CW * 2;  // one 32 x 16 f16 box
-        static_assert(NCH * BOX + 2 * CPW * 4 <= 2 * C::EPI_BUF, "fast epilogue staging");
         const int e = warp - 2;
         const int q = warp & 3;
         const int slice = e >> 2;
-        uint8_t* wst = staging + e * 2 * C::EPI_BUF;
-        float* cvb = reinterpret_cast<float*>(wst + NCH * BOX);
+        uint8_t* wst = staging + e * C::FAST_WARP_BYTES;  // [2 box sets][NCH boxes] + column vectors
+        float* cvb = reinterpret_cast<float*>(wst + 2 * NCH * BOX);
         float* cvs = cvb + CPW;
-        const uint32_t wst_a = tzp::smem_u32(wst);
+        int pb = 0;  // box set of this tile
         const uint64_t kG0 = tzp::f2_pack(0.7978845608f, 0.7978845608f);
         const uint64_t kG1 = tzp::f2_pack(0.7978845608f * 0.044715f, 0.7978845608f * 0.044715f);
         const uint64_t kHalf = tzp::f2_pack(0.5f, 0.5f);
@@ -448,7 +454,9 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             float rs = 1.0f;
             if constexpr ((FAST & F_RSCALE) != 0) rs = row_ok ? __ldg(ep.row_scale + row) : 1.0f;
             const uint64_t rs2 = tzp::f2_pack(rs, rs);
-            if (lane == 0) tzp::bulk_wait_read<0>();  // the previous tile's stores have read the boxes
+            if (lane == 0) tzp::bulk_wait_read<1>();  // the stores of two tiles ago have read this box set
+            uint8_t* wbox = wst + pb * NCH * BOX;
+            const uint32_t wst_a = tzp::smem_u32(wbox);
             for (int i = lane; i < CPW; i += 32) {
                 cvb[i] = __ldg(ep.bias + cbase + i);
                 if constexpr ((FAST & (F_RSCALE | F_CSCALE)) != 0) cvs[i] = __ldg(ep.col_scale + cbase + i);
@@ -518,9 +526,10 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             __syncwarp();
             if (lane == 0) {
 #pragma unroll
-                for (int c = 0; c < NCH; ++c) tzp::tma_store_2d(&tmOut, wst + c * BOX, cbase + 16 * c, row0);
+                for (int c = 0; c < NCH; ++c) tzp::tma_store_2d(&tmOut, wbox + c * BOX, cbase + 16 * c, row0);
                 tzp::bulk_commit();
             }
+            pb ^= 1;
             if constexpr ((FAST & F_AMAX) != 0) {
                 if (row_ok)
                     atomicMax(ep.row_absmax + row, __float_as_uint(fmaxf(__low2float(amax2), __high2float(amax2))));
@@ -616,11 +625,13 @@ template <int KIND, int BN, int STAGES, int EPI_WARPS, int FAST = 0>
 int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     using C = Cfg<KIND, BN, STAGES, EPI_WARPS>;
     auto kern = gemm_tc_kernel<KIND, BN, STAGES, EPI_WARPS, FAST>;
+    constexpr int SMEM = FAST != 0 ? C::SMEM_FAST : C::SMEM;
+    static_assert(SMEM <= 227 * 1024, "shared memory");
     static unsigned attr_set = 0;  // one bit per device
     int dev = 0;
     TZ_CUDA(cudaGetDevice(&dev));
     if (!(attr_set & (1u << (dev & 31)))) {
-        TZ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        TZ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         attr_set |= 1u << (dev & 31);
     }
     CUtensorMap ta, tb, to;
@@ -669,7 +680,7 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     const int tiles = ((g.M + 127) / 128) * n_tiles;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
-    return launch_kernel(kern, dim3(grid), dim3(C::THREADS), C::SMEM, s, g.pdl, ta, tb, to, g.M, g.N, g.K, ep, use_tma,
+    return launch_kernel(kern, dim3(grid), dim3(C::THREADS), SMEM, s, g.pdl, ta, tb, to, g.M, g.N, g.K, ep, use_tma,
                          ctx->d_status);
 }
 
@@ -694,7 +705,7 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
         const int f = F_ON | (g.gelu == 1 ? F_GELU : 0) | (g.row_absmax ? F_AMAX : 0) |
                       (g.row_scale ? F_RSCALE : (g.col_scale ? F_CSCALE : 0));
 #define TZ_FAST_CASE(K_, F_) \
-    case F_: return launch_impl<K_, 192, 4, 16, F_>(ctx, g, s);
+    case F_: return launch_impl<K_, 192, 3, 16, F_>(ctx, g, s);
 #define TZ_FAST_KIND(K_)                                                                                       \
     switch (f) {                                                                                               \
         TZ_FAST_CASE(K_, F_ON)                                                                                 \
