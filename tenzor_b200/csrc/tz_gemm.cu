@@ -342,7 +342,9 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     __syncthreads();
     tzp::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    tzp::pdl_wait();  // everything above is independent of the previous kernel's output
+    // Programmatic launch: each role waits for the previous grid (griddepcontrol.wait) before it
+    // touches that grid's output; the producer first requests the B (weight) tiles of its first
+    // stages, which the model's previous kernel never writes.
 
     const int n_tiles = (N + BN - 1) / BN;
     const int num_tiles = ((M + 127) / 128) * n_tiles;
@@ -351,6 +353,16 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer ----
+            int pre = 0;  // K blocks of the first tile whose B tile is already requested
+            if (static_cast<int>(blockIdx.x) < num_tiles) {
+                pre = kblocks < STAGES ? kblocks : STAGES;
+                for (int kb = 0; kb < pre; ++kb) {
+                    tzp::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+                    tzp::tma_load_2d(smem + kb * C::STAGE_BYTES + C::A_BYTES, &tmB, kb * C::BK,
+                                     (blockIdx.x % n_tiles) * BN, &full[kb]);
+                }
+            }
+            tzp::pdl_wait();
             int stage = 0;
             uint32_t phase = 0, armed = 0, armed_par = 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -363,9 +375,10 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                         break;
                     }
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
-                    tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    const bool b_done = tile == static_cast<int>(blockIdx.x) && kb < pre;
+                    if (!b_done) tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
                     tzp::tma_load_2d(sa, &tmA, kb * C::BK, m0, &full[stage]);
-                    tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, n0, &full[stage]);
+                    if (!b_done) tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, n0, &full[stage]);
                     armed |= 1u << stage;
                     armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -421,6 +434,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             tzp::mbar_wait(drain, 0, status, nullptr);
         }
     } else if constexpr (FAST != 0) {
+        tzp::pdl_wait();
         // ---- specialised epilogue: straight-line code per tile ----
         // Per tile, before the accumulator is ready: this row's scale and the slice's bias / column
         // scales (into this warp's staging area, read back as broadcasts).  Then the NCH chunks of
@@ -541,6 +555,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         }
         if (lane == 0) tzp::bulk_wait_all();
     } else {
+        tzp::pdl_wait();
         // ---- epilogue warps: warp e reads TMEM lane quarter (warp % 4), column slice e / 4 ----
         const int e = warp - 2;
         const int q = warp & 3;

@@ -149,13 +149,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tzp::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    tzp::pdl_wait();
+    // Programmatic launch: the producer requests the weight tiles of its first stages before it
+    // waits for the previous grid (griddepcontrol.wait); the epilogue warps wait before they read
+    // the activations, row scales or residual that grid wrote.  The MMA warp reads no global memory.
 
     const int num_tiles = (M + 127) / 128;
     const int kblocks = (K + C::BK - 1) / C::BK;
+    constexpr uint32_t kExpect = AQ ? C::B_BYTES : C::STAGE_BYTES;
 
     if (warp == 0) {
         if (lane == 0) {
+            int pre = 0;  // K blocks of the first tile whose B tiles are already requested
+            if (static_cast<int>(blockIdx.x) < num_tiles) {
+                pre = kblocks < kStages ? kblocks : kStages;
+                for (int kb = 0; kb < pre; ++kb) {
+                    uint8_t* sb = smem + kb * C::STAGE_BYTES + C::A_BYTES;
+                    tzp::mbar_arrive_expect_tx(&full[kb], kExpect);
+                    tzp::tma_load_2d(sb, &tmB, kb * C::BK, 0, &full[kb]);
+                    tzp::tma_load_2d(sb + kHalf * 128, &tmB, kb * C::BK, kHalf, &full[kb]);
+                }
+            }
+            tzp::pdl_wait();
             int stage = 0;
             uint32_t phase = 0, armed = 0, armed_par = 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -166,10 +180,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
-                    tzp::mbar_arrive_expect_tx(&full[stage], AQ ? C::B_BYTES : C::STAGE_BYTES);
+                    const bool b_done = tile == static_cast<int>(blockIdx.x) && kb < pre;
+                    if (!b_done) tzp::mbar_arrive_expect_tx(&full[stage], kExpect);
                     if constexpr (!AQ) tzp::tma_load_2d(sa, &tmA, kb * C::BK, tile * 128, &full[stage]);
-                    tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, 0, &full[stage]);
-                    tzp::tma_load_2d(sa + C::A_BYTES + kHalf * 128, &tmB, kb * C::BK, kHalf, &full[stage]);
+                    if (!b_done) {
+                        tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, 0, &full[stage]);
+                        tzp::tma_load_2d(sa + C::A_BYTES + kHalf * 128, &tmB, kb * C::BK, kHalf, &full[stage]);
+                    }
                     armed |= 1u << stage;
                     armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == kStages) {
@@ -224,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tzp::mbar_wait(drain, 0, status, nullptr);
         }
     } else {
+        tzp::pdl_wait();
         const int e = warp - 2;
         const int q = warp & 3;
         const int slice = e >> 2;
