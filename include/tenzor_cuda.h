@@ -38,6 +38,7 @@ typedef enum {
 
 typedef struct tz_ctx_s* tz_ctx_t;     /* one device + one default stream + scratch arena */
 typedef struct tz_model_s* tz_model_t; /* device-resident Arctic-embed-xs weights + workspace */
+typedef struct tz_tokenizer_s* tz_tokenizer_t; /* WordPiece vocabulary (host) */
 typedef void* tz_stream_t;             /* a cudaStream_t; NULL = the context's stream */
 
 /* Message of the last failing call on this thread ("" if none).  SPEC.md:876 tz_get_last_error. */
@@ -293,6 +294,44 @@ int tz_lenet_forward(tz_lenet_t model, const float* images, int64_t n, float* ou
 /* Device images (8-byte aligned) -> device out, asynchronous on `stream`. */
 int tz_lenet_forward_device(tz_lenet_t model, const float* images, int64_t n, float* out,
                             tz_stream_t stream);
+
+/* ---- text -> device ids -> embeddings ------------------------------------------------------
+ * The WordPiece tokenizer of src/io/tokenizer.zig (host code: string work) and the embed CLI's two
+ * text paths of main.zig on the device.  Special ids are [UNK] 100, [CLS] 101, [SEP] 102
+ * (tokenizer.zig:11-13) unless changed with tz_tokenizer_set_special. */
+/* Tokenizer.init / deinit (tokenizer.zig:17-31). */
+int tz_tokenizer_create(tz_tokenizer_t* out);
+int tz_tokenizer_free(tz_tokenizer_t tok);
+/* The public fields unk_id / cls_id / sep_id of Tokenizer (tokenizer.zig:11-13). */
+int tz_tokenizer_set_special(tz_tokenizer_t tok, uint32_t unk_id, uint32_t cls_id, uint32_t sep_id);
+/* Tokenizer.loadVocab / loadVocabFromBytes (tokenizer.zig:34-74): one token per line, id = line
+ * index.  tz_tokenizer_put is vocab.put(token, id) (the reference's tests build vocabularies so). */
+int tz_tokenizer_load_vocab(tz_tokenizer_t tok, const char* path);
+int tz_tokenizer_load_vocab_bytes(tz_tokenizer_t tok, const char* data, int64_t len);
+int tz_tokenizer_put(tz_tokenizer_t tok, const char* token, int64_t len, uint32_t id);
+int tz_tokenizer_vocab_size(tz_tokenizer_t tok, int64_t* n);
+/* Tokenizer.encode (tokenizer.zig:77-121): [CLS] ids [SEP] into out[cap] (cap >= 2); *n = count. */
+int tz_tokenizer_encode(tz_tokenizer_t tok, const char* text, int64_t len, uint32_t* out, int64_t cap,
+                        int64_t* n);
+/* Tokenizer.encodeRaw (tokenizer.zig:123-200): ids without markers.  *n = the full count; out may
+ * be NULL (size query); a non-NULL out with cap < *n fails with TZ_EINVAL. */
+int tz_tokenizer_encode_raw(tz_tokenizer_t tok, const char* text, int64_t len, uint32_t* out, int64_t cap,
+                            int64_t* n);
+/* encode of every text into a max_len buffer (main.zig:939-950 uses [512]u32), packed as
+ * (ids_packed, cu_seqlens[n_texts + 1]) for tz_arctic_forward; host threads for large batches. */
+int tz_tokenizer_encode_batch(tz_tokenizer_t tok, const char* const* texts, const int64_t* lens, int n_texts,
+                              int max_len, uint32_t* ids_packed, int32_t* cu_seqlens, int64_t cap_tokens);
+/* Short texts (main.zig:934-980): encode each into 512 ids, forward the batch -> out[n_texts, 384]. */
+int tz_arctic_embed_texts(tz_model_t model, tz_tokenizer_t tok, const char* const* texts, const int64_t* lens,
+                          int n_texts, float* out);
+/* Chunks a document of `tokens` raw ids takes (main.zig:806-809: 510-id chunks, 50 overlap; the
+ * reference's count formula, whose last chunk can end before the document does, is kept). */
+int64_t tz_doc_chunk_count(int64_t tokens);
+/* Long documents (main.zig:796-925): encodeRaw, [CLS] chunk [SEP] per chunk, every chunk of every
+ * document forwarded as one packed batch, then per document the mean of its chunk embeddings and
+ * an L2 normalisation on the device -> out[n_docs, 384]. */
+int tz_arctic_embed_documents(tz_model_t model, tz_tokenizer_t tok, const char* const* texts, const int64_t* lens,
+                              int n_docs, float* out);
 
 #ifdef __cplusplus
 }

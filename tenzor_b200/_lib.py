@@ -29,7 +29,10 @@ EXPORTS = [
     "tz_linear_w8a8", "tz_linear_w8a8_noalloc", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
     "tz_matmul_epilogue", "tz_ew_add_mul_exp", "tz_ew_program_run", "tz_ew_unary_chain", "tz_reduce",
     "tz_gather_rows", "tz_lenet_load", "tz_lenet_free", "tz_lenet_reserve", "tz_lenet_forward",
-    "tz_lenet_forward_device",
+    "tz_lenet_forward_device", "tz_tokenizer_create", "tz_tokenizer_free", "tz_tokenizer_set_special",
+    "tz_tokenizer_load_vocab", "tz_tokenizer_load_vocab_bytes", "tz_tokenizer_put", "tz_tokenizer_vocab_size",
+    "tz_tokenizer_encode", "tz_tokenizer_encode_raw", "tz_tokenizer_encode_batch", "tz_arctic_embed_texts",
+    "tz_doc_chunk_count", "tz_arctic_embed_documents",
 ]
 
 
@@ -119,11 +122,22 @@ def _declare(L):
         "tz_gather_rows": [P, P, i64, P, i64, i, P, P],
         "tz_lenet_load": [P, P, i, C.POINTER(P)], "tz_lenet_free": [P], "tz_lenet_reserve": [P, i64],
         "tz_lenet_forward": [P, P, i64, P], "tz_lenet_forward_device": [P, P, i64, P, P],
+        "tz_tokenizer_create": [C.POINTER(P)], "tz_tokenizer_free": [P],
+        "tz_tokenizer_set_special": [P, C.c_uint32, C.c_uint32, C.c_uint32],
+        "tz_tokenizer_load_vocab": [P, C.c_char_p], "tz_tokenizer_load_vocab_bytes": [P, C.c_char_p, i64],
+        "tz_tokenizer_put": [P, C.c_char_p, i64, C.c_uint32], "tz_tokenizer_vocab_size": [P, C.POINTER(i64)],
+        "tz_tokenizer_encode": [P, C.c_char_p, i64, P, i64, C.POINTER(i64)],
+        "tz_tokenizer_encode_raw": [P, C.c_char_p, i64, P, i64, C.POINTER(i64)],
+        "tz_tokenizer_encode_batch": [P, P, P, i, i, P, P, i64],
+        "tz_arctic_embed_texts": [P, P, P, P, i, P],
+        "tz_arctic_embed_documents": [P, P, P, P, i, P],
     }
     for name, args in sig.items():
         f = getattr(L, name)
         f.argtypes = args
         f.restype = C.c_int
+    L.tz_doc_chunk_count.argtypes = [i64]
+    L.tz_doc_chunk_count.restype = i64
 
 
 def check(rc: int):

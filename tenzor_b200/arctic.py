@@ -180,6 +180,27 @@ class ArcticModel:
         """forward (arctic.zig:874): one sequence -> its L2-normalised CLS embedding [384]."""
         return self.forward_batch([token_ids])[0]
 
+    def embed_texts(self, tokenizer, texts) -> np.ndarray:
+        """The embed CLI's text batch (main.zig:934-980): each text encoded into 512 ids
+        ([CLS] ... [SEP]), one batched forward -> [n, 384]."""
+        from .tokenizer import text_args
+        bufs, ptrs, lens = text_args(texts)
+        out = np.empty((len(bufs), 384), np.float32)
+        L.check(L.lib().tz_arctic_embed_texts(self.handle, tokenizer.handle, C.cast(ptrs, C.c_void_p),
+                                              lens.ctypes.data, len(bufs), out.ctypes.data))
+        return out
+
+    def embed_documents(self, tokenizer, documents) -> np.ndarray:
+        """The embed CLI's long-document path (main.zig:796-925) for many documents at once:
+        510-id chunks with 50 overlap, every chunk forwarded in one packed batch, the per-document
+        mean of chunk embeddings L2-normalised on the device -> [n, 384]."""
+        from .tokenizer import text_args
+        bufs, ptrs, lens = text_args(documents)
+        out = np.empty((len(bufs), 384), np.float32)
+        L.check(L.lib().tz_arctic_embed_documents(self.handle, tokenizer.handle, C.cast(ptrs, C.c_void_p),
+                                                  lens.ctypes.data, len(bufs), out.ctypes.data))
+        return out
+
     def forward_device(self, d_ids, d_cu, batch: int, total_tokens: int, max_len: int, d_out,
                        stream=None):
         """Device-pointer variant (integers or torch tensors' data_ptr()), async on `stream` (a raw

@@ -258,6 +258,35 @@ __global__ void pool_l2_kernel(const float* __restrict__ x, const int* __restric
     }
 }
 
+// Long-document pooling of the embed CLI (main.zig:909-925): per document the chunk embeddings are
+// summed in chunk order, scaled by 1/n_chunks, then divided by their L2 norm when it is positive.
+// CTA of 128 threads per document, three columns per thread; the squared norm is a block sum.
+__global__ void doc_mean_l2_kernel(const float* __restrict__ emb, const int* __restrict__ doc_off, float* __restrict__ out) {
+    __shared__ float part[4];
+    const int d = blockIdx.x;
+    const int c0 = doc_off[d], c1 = doc_off[d + 1];
+    const float scale = 1.0f / static_cast<float>(c1 - c0);
+    float v[3];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int j = threadIdx.x + 128 * k;
+        float acc = 0.f;
+        for (int c = c0; c < c1; ++c) acc = __fadd_rn(acc, emb[static_cast<long long>(c) * kH + j]);
+        v[k] = __fmul_rn(acc, scale);
+        ss = __fadd_rn(ss, __fmul_rn(v[k], v[k]));
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    const float norm = sqrtf((part[0] + part[1]) + (part[2] + part[3]));
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int j = threadIdx.x + 128 * k;
+        out[static_cast<long long>(d) * kH + j] = norm > 0.f ? __fdiv_rn(v[k], norm) : v[k];
+    }
+}
+
 inline int rows_grid(long long rows) { return static_cast<int>((rows * 32 + 255) / 256); }
 
 }  // namespace
@@ -649,6 +678,28 @@ int check_lengths(const int32_t* cu, int B, int64_t* T, int* maxL) {
     return TZ_OK;
 }
 
+// Host ids -> the model's device output rows (m->out), enqueued on the context's stream without
+// a graph and without waiting; the caller reads m->out after synchronising.
+int forward_to_device(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B) {
+    int64_t T = 0;
+    int maxL = 0;
+    int rc = check_lengths(cu, B, &T, &maxL);
+    if (rc) return rc;
+    for (int64_t i = 0; i < T; ++i)
+        TZ_CHECK(ids[i] < static_cast<uint32_t>(kV), TZ_EINVAL, "token id %u at %lld is >= vocab %d", ids[i],
+                 static_cast<long long>(i), kV);
+    if ((rc = reserve(m, B, T))) return rc;
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    cudaStream_t s = m->ctx->stream;
+    TZ_CUDA(cudaStreamSynchronize(s));  // the pinned staging may still feed an earlier forward
+    memcpy(m->h_ids, ids, sizeof(uint32_t) * T);
+    memcpy(m->h_cu, cu, sizeof(int) * (B + 1));
+    TZ_CUDA(cudaMemcpyAsync(m->d_ids, m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
+    TZ_CUDA(cudaMemcpyAsync(m->d_cu, m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s));
+    m->last_T = T;
+    return enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
+}
+
 int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, float* out) {
     int64_t T = 0;
     int maxL = 0;
@@ -936,6 +987,69 @@ int tz_arctic_debug_operand(tz_model_t m, int which, int8_t* q_out, float* scale
     TZ_CUDA(cudaMemcpyAsync(scale_out, m->d_ops[which], sizeof(float) * T, cudaMemcpyDeviceToHost, m->ctx->stream));
     TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
     return TZ_OK;
+}
+
+int tz_arctic_embed_texts(tz_model_t m, tz_tokenizer_t tok, const char* const* texts, const int64_t* lens, int n,
+                          float* out) {
+    TZ_CHECK(m && tok && n >= 0 && (n == 0 || (texts && lens && out)), TZ_EINVAL, "tz_arctic_embed_texts: bad arguments");
+    if (n == 0) return TZ_OK;
+    std::vector<uint32_t> ids(static_cast<size_t>(n) * kP);
+    std::vector<int32_t> cu(static_cast<size_t>(n) + 1);
+    int rc = tz_tokenizer_encode_batch(tok, texts, lens, n, kP, ids.data(), cu.data(), static_cast<int64_t>(ids.size()));
+    if (rc) return rc;
+    return forward_host(m, ids.data(), cu.data(), n, out);
+}
+
+int64_t tz_doc_chunk_count(int64_t tokens) {
+    constexpr int64_t kChunk = 510, kOverlap = 50;  // main.zig:784-785
+    if (tokens <= kChunk) return 1;
+    return 1 + (tokens - kChunk + kOverlap - 1) / (kChunk - kOverlap);
+}
+
+int tz_arctic_embed_documents(tz_model_t m, tz_tokenizer_t tok, const char* const* texts, const int64_t* lens, int n,
+                              float* out) {
+    TZ_CHECK(m && tok && n >= 0 && (n == 0 || (texts && lens && out)), TZ_EINVAL,
+             "tz_arctic_embed_documents: bad arguments");
+    if (n == 0) return TZ_OK;
+    constexpr int64_t kChunk = 510, kStride = 510 - 50;
+    const uint32_t cls = tokenizer_cls(tok), sep = tokenizer_sep(tok);
+    std::vector<uint32_t> ids, raw;
+    std::vector<int32_t> cu(1, 0);
+    std::vector<int> doc_off(1, 0);
+    for (int d = 0; d < n; ++d) {
+        int rc = tokenize_raw(tok, texts[d], lens[d], &raw);
+        if (rc) return rc;
+        const int64_t T = static_cast<int64_t>(raw.size());
+        const int64_t nc = tz_doc_chunk_count(T);
+        for (int64_t c = 0; c < nc; ++c) {  // main.zig:869-878: [CLS] ids[start, min(start + 510, T)) [SEP]
+            const int64_t a = c * kStride, b = std::min(a + kChunk, T);
+            ids.push_back(cls);
+            ids.insert(ids.end(), raw.begin() + a, raw.begin() + b);
+            ids.push_back(sep);
+            TZ_CHECK(ids.size() < (size_t(1) << 31), TZ_EINVAL, "tz_arctic_embed_documents: too many ids in one call");
+            cu.push_back(static_cast<int32_t>(ids.size()));
+        }
+        doc_off.push_back(static_cast<int>(cu.size() - 1));
+    }
+    const int chunks = static_cast<int>(cu.size() - 1);
+    int rc = forward_to_device(m, ids.data(), cu.data(), chunks);
+    if (rc) return rc;
+    cudaStream_t s = m->ctx->stream;
+    int* d_off = nullptr;  // stream-ordered scratch for the document offsets and results
+    float* d_doc = nullptr;
+    TZ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d_off), sizeof(int) * (n + 1), s));
+    TZ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d_doc), sizeof(float) * static_cast<size_t>(n) * kH, s));
+    cudaError_t e = cudaMemcpyAsync(d_off, doc_off.data(), sizeof(int) * (n + 1), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        doc_mean_l2_kernel<<<n, 128, 0, s>>>(m->out, d_off, d_doc);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d_doc, sizeof(float) * static_cast<size_t>(n) * kH, cudaMemcpyDeviceToHost, s);
+    cudaFreeAsync(d_off, s);
+    cudaFreeAsync(d_doc, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tz_arctic_embed_documents");
+    TZ_CUDA(cudaStreamSynchronize(s));
+    return read_status(m->ctx, s);
 }
 
 }  // extern "C"

@@ -458,6 +458,25 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         const uint64_t kHalf = tzp::f2_pack(0.5f, 0.5f);
         int acc = 0;
         uint32_t acc_phase = 0;
+        // The next tile's row scale and column vectors are fetched into registers while this tile
+        // waits and is converted, so no tile starts on a global-memory round trip.
+        constexpr int VPL = (CPW + 31) / 32;
+        float nrs = 1.0f, nb[VPL], ns[VPL];
+        auto fetch = [&](int t) {
+            if (t >= num_tiles) return;
+            const int r = (t / n_tiles) * 128 + q * 32 + lane;
+            const int cb = (t % n_tiles) * BN + slice * CPW;
+            if constexpr ((FAST & F_RSCALE) != 0) nrs = r < M ? __ldg(ep.row_scale + r) : 1.0f;
+#pragma unroll
+            for (int v = 0; v < VPL; ++v) {
+                const int i = lane + 32 * v;
+                if (i < CPW) {
+                    nb[v] = __ldg(ep.bias + cb + i);
+                    if constexpr ((FAST & (F_RSCALE | F_CSCALE)) != 0) ns[v] = __ldg(ep.col_scale + cb + i);
+                }
+            }
+        };
+        fetch(blockIdx.x);
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int m0 = (tile / n_tiles) * 128;
             const int n0 = (tile % n_tiles) * BN;
@@ -465,17 +484,21 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             const int row = row0 + lane;
             const bool row_ok = row < M;
             const int cbase = n0 + slice * CPW;
-            float rs = 1.0f;
-            if constexpr ((FAST & F_RSCALE) != 0) rs = row_ok ? __ldg(ep.row_scale + row) : 1.0f;
+            const float rs = nrs;
             const uint64_t rs2 = tzp::f2_pack(rs, rs);
             if (lane == 0) tzp::bulk_wait_read<1>();  // the stores of two tiles ago have read this box set
             uint8_t* wbox = wst + pb * NCH * BOX;
             const uint32_t wst_a = tzp::smem_u32(wbox);
-            for (int i = lane; i < CPW; i += 32) {
-                cvb[i] = __ldg(ep.bias + cbase + i);
-                if constexpr ((FAST & (F_RSCALE | F_CSCALE)) != 0) cvs[i] = __ldg(ep.col_scale + cbase + i);
+#pragma unroll
+            for (int v = 0; v < VPL; ++v) {  // the previous tile's reads of cvb / cvs are behind this warp
+                const int i = lane + 32 * v;
+                if (i < CPW) {
+                    cvb[i] = nb[v];
+                    if constexpr ((FAST & (F_RSCALE | F_CSCALE)) != 0) cvs[i] = ns[v];
+                }
             }
             __syncwarp();
+            fetch(tile + gridDim.x);
             if (!tzp::mbar_wait(&tfull[acc], acc_phase, status, abort_flag)) break;
             tzp::tc_fence_after();
             const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + slice * CPW);

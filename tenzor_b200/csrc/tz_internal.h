@@ -55,6 +55,11 @@ int scratch_reserve(tz_ctx_t ctx, size_t bytes, void** out);
 // Reads and clears the device status word; TZ_ETIMEOUT / TZ_EINVAL when a bit was set.
 int read_status(tz_ctx_t ctx, cudaStream_t s);
 
+// The tokenizer's encodeRaw (tz_tokenizer.cpp) for the document path of tz_arctic_embed_documents.
+int tokenize_raw(tz_tokenizer_t tok, const char* text, int64_t len, std::vector<uint32_t>* ids);
+uint32_t tokenizer_cls(tz_tokenizer_t tok);
+uint32_t tokenizer_sep(tz_tokenizer_t tok);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,

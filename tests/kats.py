@@ -84,3 +84,38 @@ GATHER = [
 # arctic.zig:1032-1057
 GELU_MODEL = [("gelu(0)=0", 0.0, 0.0, 1e-6), ("gelu(3)~3", 3.0, 3.0, 0.01)]
 L2 = ([3.0, 4.0], [0.6, 0.8], 1e-6)
+
+
+# tokenizer.zig:291-439 -- the reference's inline tokenizer tests: (name, vocabulary put into the
+# hash map, text, expected encode output).
+TOKENIZER = [
+    ("basic", {"[PAD]": 0, "[UNK]": 100, "[CLS]": 101, "[SEP]": 102, "hello": 7592, "world": 2088, "##ing": 2075,
+               "test": 3231, "##s": 1055}, "hello world", [101, 7592, 2088, 102]),
+    ("wordpiece split", {"[UNK]": 100, "[CLS]": 101, "[SEP]": 102, "test": 3231, "##ing": 2075}, "testing",
+     [101, 3231, 2075, 102]),
+    ("unknown word", {"[UNK]": 100, "[CLS]": 101, "[SEP]": 102, "hello": 7592}, "xyz", [101, 100, 102]),
+    ("punctuation", {"[UNK]": 100, "[CLS]": 101, "[SEP]": 102, "hello": 7592, ",": 1010, "world": 2088},
+     "hello, world", [101, 7592, 1010, 2088, 102]),
+    ("lowercase", {"[UNK]": 100, "[CLS]": 101, "[SEP]": 102, "hello": 7592}, "HELLO", [101, 7592, 102]),
+]
+
+# src/tests/tokenizer_parity_test.zig:15-31 -- HuggingFace token ids of the real arctic-embed-xs
+# vocab.txt (absent here).  Tests derive the vocabulary entries these cases imply (texts whose basic
+# tokens map one-to-one onto the expected ids) and pin the tokenizer on those cases.
+TOKENIZER_HF = [
+    ("Hello world", [101, 7592, 2088, 102]),
+    ("hello world", [101, 7592, 2088, 102]),
+    ("HELLO WORLD", [101, 7592, 2088, 102]),
+    ("Hello, world!", [101, 7592, 1010, 2088, 999, 102]),
+    ("The quick brown fox jumps over the lazy dog.", [101, 1996, 4248, 2829, 4419, 14523, 2058, 1996, 13971, 3899, 1012, 102]),
+    ("What is machine learning?", [101, 2054, 2003, 3698, 4083, 1029, 102]),
+    ("testing", [101, 5604, 102]),
+    ("embeddings", [101, 7861, 8270, 4667, 2015, 102]),
+    ("I love programming in Zig!", [101, 1045, 2293, 4730, 1999, 1062, 8004, 999, 102]),
+    ("", [101, 102]),
+    ("a", [101, 1037, 102]),
+    ("123", [101, 13138, 102]),
+    ("hello-world", [101, 7592, 1011, 2088, 102]),
+    ("don't", [101, 2123, 1005, 1056, 102]),
+    ("   spaces   ", [101, 7258, 102]),
+]
