@@ -482,20 +482,39 @@ def run_micro(a):
     hbm, bf16, bf16_sus, src = peaks()
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
 
-    def timed(fn):
+    def timed(fn, flush_l2=True):
+        # The K iterations (flush, start event, op, end event) are captured into one CUDA graph and
+        # replayed, so the device runs them back to back and the host's per-call overhead (Python,
+        # ctypes, tensor-map encoding) never lands between an op's two events.  flush_l2=False for
+        # ops whose inputs rotate over more than L2 holds (126 MB): no flush write-backs then
+        # compete with the op's own traffic.
         for _ in range(a.warmup):
             fn()
         torch.cuda.synchronize()
-        tot = 0.0
-        for _ in range(a.steps):
-            flush.zero_()
-            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s_.record(stream)
-            fn()
-            e_.record(stream)
-            e_.synchronize()
-            tot += s_.elapsed_time(e_)
-        return tot / a.steps
+        # external=True: captured as event-record nodes, which keep their timestamps
+        evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+               for _ in range(a.steps)]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            if flush_l2:  # events around each launch, a flush before each
+                for s_, e_ in evs:
+                    flush.zero_()
+                    s_.record()
+                    fn()
+                    e_.record()
+            else:  # the K launches back to back between one pair of events
+                evs[0][0].record()
+                for _ in evs:
+                    fn()
+                evs[0][1].record()
+        g.replay()
+        torch.cuda.synchronize()
+        if flush_l2:
+            t = sum(s_.elapsed_time(e_) for s_, e_ in evs) / a.steps
+        else:
+            t = evs[0][0].elapsed_time(evs[0][1]) / a.steps
+        del g
+        return t
 
     def u(seed, shape):
         return torch.from_numpy(S.uniform(seed, shape, -1.0, 1.0)).cuda()
@@ -514,19 +533,28 @@ def run_micro(a):
     a_, b_, c_ = u(4, (16384, 4096)), u(5, (4096,)), u(6, (16384, 4096))
     e = E.tensor(a_).add(b_).mul(c_).exp()
     out = torch.empty_like(a_)
-    ms = timed(lambda: ops.ew_add_mul_exp(ctx, a_, b_, c_, out=out))
+    ms = timed(lambda: ops.ew_add_mul_exp(ctx, a_, b_, c_, out=out), flush_l2=False)  # 768 MB touched per launch
     byts = 3 * 64 * 2 ** 20 * 4 + 4096 * 4
     lines.append({"metric": "elementwise chain a.add(b).mul(c).exp() 64M elems GB/s", "value": byts / ms / 1e6,
                   "unit": "GB/s", "ms": ms, "plan": E.analyze(e),
                   "roofline": {"bound": "hbm", "peak": hbm, "frac": byts / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy"}})
     del a_, c_, out
-    # (c) LayerNorm [32768, 384]
-    x, g, bb = u(7, (32768, 384)), torch.ones(384, device="cuda"), torch.zeros(384, device="cuda")
-    y = torch.empty_like(x)
-    ms = timed(lambda: ops.layer_norm_last_dim(ctx, x, g, bb, 1e-5, out=y))
+    # (c) LayerNorm [32768, 384]; three input/output sets round-robin (300 MB > L2)
+    g, bb = torch.ones(384, device="cuda"), torch.zeros(384, device="cuda")
+    lx = [u(7 + i, (32768, 384)) for i in range(3)]
+    ly = [torch.empty_like(t) for t in lx]
+    lit = [0]
+
+    def ln():
+        i = lit[0] % 3
+        lit[0] += 1
+        ops.layer_norm_last_dim(ctx, lx[i], g, bb, 1e-5, out=ly[i])
+    ms = timed(ln, flush_l2=False)
     byts = 2 * 32768 * 384 * 4 + 2 * 384 * 4
     lines.append({"metric": "LayerNorm [32768,384] GB/s", "value": byts / ms / 1e6, "unit": "GB/s", "ms": ms,
-                  "roofline": {"bound": "hbm", "peak": hbm, "frac": byts / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy"}})
+                  "roofline": {"bound": "hbm", "peak": hbm, "frac": byts / ms / 1e6 / hbm,
+                               "peak_source": f"{src} HBM copy; 3 distinct 100 MB buffer sets round-robin"}})
+    del lx, ly
     # (c) masked softmax [96, 128, 128], key lengths U{16..128}; 32 distinct buffers round-robin (> L2)
     nb = 32
     xs = [u(100 + i, (96, 128, 128)) for i in range(nb)]
@@ -538,13 +566,19 @@ def run_micro(a):
         i = it[0] % nb
         it[0] += 1
         ops.softmax_keylen(ctx, xs[i], kl, out=ys[i])
-    ms = timed(sm)
+    ms = timed(sm, flush_l2=False)
     byts = 2 * 96 * 128 * 128 * 4
     lines.append({"metric": "masked softmax [96,128,128] GB/s", "value": byts / ms / 1e6, "unit": "GB/s", "ms": ms,
                   "roofline": {"bound": "hbm", "peak": hbm, "frac": byts / ms / 1e6 / hbm,
                                "peak_source": f"{src} HBM copy; 32 distinct 6.3 MB buffers round-robin"}})
     for ln in lines:
-        ln.update({"steps": a.steps, "warmup": a.warmup, "data": "synthetic U[-1,1]", "config": {"workload": "configs[2]"}})
+        ln.update({"steps": a.steps, "warmup": a.warmup, "data": "synthetic U[-1,1]",
+                   "config": {"workload": "configs[2]",
+                              "l2": "flushed (256 MB write) before each launch" if "matmul" in ln["metric"]
+                              else "inputs rotate over more than L2 (no flush)",
+                              "timing": "K launches captured in one CUDA graph; CUDA events around each launch"
+                              if "matmul" in ln["metric"] else
+                              "K launches back to back in one CUDA graph between two CUDA events, divided by K"}})
         print(json.dumps(ln), flush=True)
     ctx.close()
     return 0

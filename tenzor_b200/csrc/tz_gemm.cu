@@ -46,6 +46,18 @@ struct EpiParams {
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// The fusion GELU (simd.zig:168-178: tanh(z) = 2 sigmoid(2z) - 1) for the fixed epilogue of the f32 /
+// tf32 GEMMs: tanh(z) = 1 - 2 / (1 + exp(2z)) with the fast exponential (ex2.approx on a pre-scaled
+// argument) and the approximate reciprocal (no slow path: an infinite or huge denominator gives 0,
+// so tanh -> 1; exp underflowing to 0 gives -1).  A few 1e-7 relative from the expf /
+// IEEE-division form, far inside the tf32 GEMM's own rounding.
+__device__ __forceinline__ float gelu_sigmoid_fast(float x) {
+    const float inner = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+    const float t = fmaf(-2.0f, __fdividef(1.0f, 1.0f + __expf(2.0f * inner)), 1.0f);
+    const float hx = 0.5f * x;
+    return fmaf(hx, t, hx);
+}
+
 // Unary op table of codegen.zig:228-244 (simd.zig scalar ops); TZ_OP_* codes.
 __device__ __forceinline__ float apply_op(int op, float x) {
     switch (op) {
@@ -200,7 +212,7 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[CW
             for (int j = 0; j < CW; ++j) v[j] = gelu_fast(v[j]);
         } else if (ep.gelu == 2) {
 #pragma unroll
-            for (int j = 0; j < CW; ++j) v[j] = apply_op(TZ_OP_GELU, v[j]);
+            for (int j = 0; j < CW; ++j) v[j] = gelu_sigmoid_fast(v[j]);
         } else if (ep.gelu == 3) {
 #pragma unroll
             for (int j = 0; j < CW; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
@@ -226,7 +238,7 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[CW
                     x = __fmul_rn(x, ep.col_scale[col]);
                 if (ep.bias) x = __fadd_rn(x, ep.bias[col]);
                 if (ep.gelu == 1) x = gelu_fast(x);
-                else if (ep.gelu == 2) x = apply_op(TZ_OP_GELU, x);
+                else if (ep.gelu == 2) x = gelu_sigmoid_fast(x);
                 else if (ep.gelu == 3) x = x > 0.0f ? x : 0.0f;
                 if (ep.residual && row_ok) x = __fadd_rn(x, ep.residual[static_cast<long long>(row) * ep.ldr + col]);
             }

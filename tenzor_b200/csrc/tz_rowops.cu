@@ -14,44 +14,56 @@ namespace tz {
 namespace {
 
 // ---- LayerNorm (layernorm.zig:26-116) ----------------------------------------------------------
-// Warp per row; VPL float4 per lane kept in registers (cols == VPL*128).
-template <int VPL>
+// Warp per R rows; VPL float4 per lane and row kept in registers (cols == VPL*128).  The R rows'
+// loads are all issued before the first reduction, so a warp keeps R x 512 x VPL bytes in flight
+// and the grid needs fewer waves.
+template <int VPL, int R>
 __global__ void ln_rows_reg_kernel(const float* __restrict__ x, const float* __restrict__ g,
                                    const float* __restrict__ b, float* y, long long rows, int cols,
                                    float eps) {
-    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long row0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * R;
     const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
-    float4 v[VPL];
-    float s = 0.f;
+    if (row0 >= rows) return;
+    float4 v[R][VPL];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-        v[i] = xr[lane + 32 * i];
-        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    }
-    s = warp_sum(s);
-    const float mean = s / static_cast<float>(cols);
-    float q = 0.f;
+    for (int r = 0; r < R; ++r) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (row0 + r) * cols);
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-        const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-        q += (a * a + bb * bb) + (c * c + d * d);
+        for (int i = 0; i < VPL; ++i) v[r][i] = (row0 + r < rows) ? xr[lane + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    q = warp_sum(q);
-    const float inv_std = 1.0f / sqrtf(q / static_cast<float>(cols) + eps);
-    float4* yr = reinterpret_cast<float4*>(y + row * cols);
+    float mean[R], inv_std[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) s += (v[r][i].x + v[r][i].y) + (v[r][i].z + v[r][i].w);
+        mean[r] = warp_sum(s) / static_cast<float>(cols);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const float a = v[r][i].x - mean[r], bb = v[r][i].y - mean[r], c = v[r][i].z - mean[r], d = v[r][i].w - mean[r];
+            q += (a * a + bb * bb) + (c * c + d * d);
+        }
+        inv_std[r] = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(cols) + eps);
+    }
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         const int c4 = lane + 32 * i;
         const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + c4);
         const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + c4);
-        float4 o;
-        o.x = (v[i].x - mean) * inv_std * gg.x + bb.x;
-        o.y = (v[i].y - mean) * inv_std * gg.y + bb.y;
-        o.z = (v[i].z - mean) * inv_std * gg.z + bb.z;
-        o.w = (v[i].w - mean) * inv_std * gg.w + bb.w;
-        yr[c4] = o;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if (row0 + r >= rows) continue;
+            float4 o;
+            o.x = (v[r][i].x - mean[r]) * inv_std[r] * gg.x + bb.x;
+            o.y = (v[r][i].y - mean[r]) * inv_std[r] * gg.y + bb.y;
+            o.z = (v[r][i].z - mean[r]) * inv_std[r] * gg.z + bb.z;
+            o.w = (v[r][i].w - mean[r]) * inv_std[r] * gg.w + bb.w;
+            reinterpret_cast<float4*>(y + (row0 + r) * cols)[c4] = o;
+        }
     }
 }
 
@@ -101,32 +113,45 @@ __global__ void softmax_rows_kernel(const float* x, const float* mask, const int
         yr[c] = (c < valid) ? expf((mr ? xr[c] + mr[c] : xr[c]) - mx) * inv : 0.0f;
 }
 
-// Fast path for cols == 128 (the Arctic attention shape at S=128): a row is one float4 per lane.
+// Fast path for cols == 128 (the Arctic attention shape at S=128): a row is one float4 per lane;
+// a warp takes R rows and issues all their loads before the first reduction.
+template <int R>
 __global__ void softmax_rows128_kernel(const float* x, const float* mask, const int* key_len,
                                        int rows_per_group, float* y, long long rows) {
-    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long row0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * R;
     const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    float4 v = reinterpret_cast<const float4*>(x + row * 128)[lane];
-    if (mask) {
-        const float4 m = reinterpret_cast<const float4*>(mask + row * 128)[lane];
-        v.x += m.x; v.y += m.y; v.z += m.z; v.w += m.w;
+    if (row0 >= rows) return;
+    float4 v[R];
+    int valid[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const long long row = row0 + r;
+        const bool in = row < rows;
+        v[r] = in ? reinterpret_cast<const float4*>(x + row * 128)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (mask && in) {
+            const float4 m = reinterpret_cast<const float4*>(mask + row * 128)[lane];
+            v[r].x += m.x; v[r].y += m.y; v[r].z += m.z; v[r].w += m.w;
+        }
+        valid[r] = (key_len && in) ? min(max(key_len[static_cast<int>(row / rows_per_group)], 0), 128) : 128;
     }
-    const int valid = key_len ? min(max(key_len[row / rows_per_group], 0), 128) : 128;
     const int c = lane * 4;
-    if (c + 0 >= valid) v.x = -INFINITY;
-    if (c + 1 >= valid) v.y = -INFINITY;
-    if (c + 2 >= valid) v.z = -INFINITY;
-    if (c + 3 >= valid) v.w = -INFINITY;
-    const float mx = warp_max(fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
-    float4 e;
-    e.x = (c + 0 < valid) ? expf(v.x - mx) : 0.f;
-    e.y = (c + 1 < valid) ? expf(v.y - mx) : 0.f;
-    e.z = (c + 2 < valid) ? expf(v.z - mx) : 0.f;
-    e.w = (c + 3 < valid) ? expf(v.w - mx) : 0.f;
-    const float inv = 1.0f / warp_sum((e.x + e.y) + (e.z + e.w));
-    e.x *= inv; e.y *= inv; e.z *= inv; e.w *= inv;
-    reinterpret_cast<float4*>(y + row * 128)[lane] = e;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const long long row = row0 + r;
+        if (c + 0 >= valid[r]) v[r].x = -INFINITY;
+        if (c + 1 >= valid[r]) v[r].y = -INFINITY;
+        if (c + 2 >= valid[r]) v[r].z = -INFINITY;
+        if (c + 3 >= valid[r]) v[r].w = -INFINITY;
+        const float mx = warp_max(fmaxf(fmaxf(v[r].x, v[r].y), fmaxf(v[r].z, v[r].w)));
+        float4 e;
+        e.x = (c + 0 < valid[r]) ? expf(v[r].x - mx) : 0.f;
+        e.y = (c + 1 < valid[r]) ? expf(v[r].y - mx) : 0.f;
+        e.z = (c + 2 < valid[r]) ? expf(v[r].z - mx) : 0.f;
+        e.w = (c + 3 < valid[r]) ? expf(v[r].w - mx) : 0.f;
+        const float inv = 1.0f / warp_sum((e.x + e.y) + (e.z + e.w));
+        e.x *= inv; e.y *= inv; e.z *= inv; e.w *= inv;
+        if (row < rows) reinterpret_cast<float4*>(y + row * 128)[lane] = e;
+    }
 }
 
 // ---- quantisers ---------------------------------------------------------------------------------
@@ -319,6 +344,7 @@ inline int ew_grid(tz_ctx_t ctx, long long work, int threads) {
 }
 
 inline int warp_rows_grid(long long rows) { return static_cast<int>((rows * 32 + 255) / 256); }
+inline int warp_rows_grid_r(long long rows, int r) { return warp_rows_grid((rows + r - 1) / r); }
 
 }  // namespace
 
@@ -362,17 +388,17 @@ int tz_layernorm_last_dim(tz_ctx_t ctx, const float* x, const float* gamma, cons
                     reinterpret_cast<uintptr_t>(gamma) % 16 == 0 && reinterpret_cast<uintptr_t>(beta) % 16 == 0;
     const int g = warp_rows_grid(rows);
     if (al && cols == 384)
-        ln_rows_reg_kernel<3><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+        ln_rows_reg_kernel<3, 2><<<warp_rows_grid_r(rows, 2), 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
     else if (al && cols == 128)
-        ln_rows_reg_kernel<1><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+        ln_rows_reg_kernel<1, 2><<<warp_rows_grid_r(rows, 2), 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
     else if (al && cols == 256)
-        ln_rows_reg_kernel<2><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+        ln_rows_reg_kernel<2, 2><<<warp_rows_grid_r(rows, 2), 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
     else if (al && cols == 512)
-        ln_rows_reg_kernel<4><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+        ln_rows_reg_kernel<4, 2><<<warp_rows_grid_r(rows, 2), 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
     else if (al && cols == 768)
-        ln_rows_reg_kernel<6><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+        ln_rows_reg_kernel<6, 1><<<warp_rows_grid_r(rows, 1), 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
     else if (al && cols == 1024)
-        ln_rows_reg_kernel<8><<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
+        ln_rows_reg_kernel<8, 1><<<warp_rows_grid_r(rows, 1), 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
     else
         ln_rows_any_kernel<<<g, 256, 0, s>>>(x, gamma, beta, y, rows, cols, eps);
     TZ_CUDA(cudaGetLastError());
@@ -387,7 +413,7 @@ int tz_softmax_last_axis(tz_ctx_t ctx, const float* x, const float* mask, float*
     const bool al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
                     (!mask || reinterpret_cast<uintptr_t>(mask) % 16 == 0);
     if (cols == 128 && al)
-        softmax_rows128_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, mask, nullptr, 1, y, rows);
+        softmax_rows128_kernel<4><<<warp_rows_grid_r(rows, 4), 256, 0, s>>>(x, mask, nullptr, 1, y, rows);
     else
         softmax_rows_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, mask, nullptr, 1, y, rows, cols);
     TZ_CUDA(cudaGetLastError());
@@ -403,7 +429,7 @@ int tz_softmax_keylen(tz_ctx_t ctx, const float* x, const int32_t* key_len, floa
     cudaStream_t s = pick_stream(ctx, stream);
     const bool al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
     if (cols == 128 && al)
-        softmax_rows128_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows);
+        softmax_rows128_kernel<4><<<warp_rows_grid_r(rows, 4), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows);
     else
         softmax_rows_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows, cols);
     TZ_CUDA(cudaGetLastError());
