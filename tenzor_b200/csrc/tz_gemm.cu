@@ -305,9 +305,28 @@ __device__ __forceinline__ void stage_chunk(const EpiParams& ep, uint32_t buf, i
     }
 }
 
-// Flags of the specialised epilogue (FAST != 0): f16 output through TMA, full column tiles, bias,
-// no residual / op chain.  Everything else takes the general epilogue (FAST == 0).
+// Flags of the specialised epilogue (FAST & F_ON): f16 output through TMA, full column tiles, bias,
+// no residual / op chain.  Everything else takes the general epilogue.
 constexpr int F_ON = 1, F_GELU = 2, F_AMAX = 4, F_RSCALE = 8, F_CSCALE = 16;
+// F_BMN (general epilogue, tf32 only): B arrives N-major, B[k, n] row-major as `A @ B` has it, and the
+// MMA reads it through an MN-major descriptor: no transpose of B first.  Each stage's B tile is
+// BN / 32 TMA boxes of 32 columns (128 bytes) x BK rows, BK * 128 bytes apart.  MN-major tf32
+// operands take the 128-byte swizzle with 32-byte atoms (TMA's SWIZZLE_128B_ATOM_32B): 32-byte
+// chunk c of 128-byte row r at c ^ (r % 4), 4-row K groups.
+constexpr int F_BMN = 32;
+
+// Shared-memory descriptor of such an MN-major tile: 128-byte rows along MN (32 tf32 elements),
+// 4-row K groups 512 bytes apart (SBO), MN blocks of 32 elements `lbo` bytes apart (LBO), layout
+// type SWIZZLE_128B_BASE32B (1).
+__device__ __forceinline__ uint64_t sdesc_mn128_b32(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(lbo >> 4) << 16;
+    d |= static_cast<uint64_t>(512 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(1) << 61;
+    return d;
+}
 
 template <int KIND, int BN, int STAGES, int EPI_WARPS, int FAST>
 __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
@@ -319,7 +338,10 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     const uint32_t raw_addr = tzp::smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + (FAST != 0 ? C::FAST_STAGING : C::STAGING));
+    constexpr bool kFastEpi = (FAST & F_ON) != 0;
+    constexpr bool kBmn = (FAST & F_BMN) != 0;
+    static_assert(!kBmn || (KIND == KIND_TF32 && !kFastEpi), "N-major B: tf32, general epilogue");
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + (kFastEpi ? C::FAST_STAGING : C::STAGING));
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -370,8 +392,14 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                 pre = kblocks < STAGES ? kblocks : STAGES;
                 for (int kb = 0; kb < pre; ++kb) {
                     tzp::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
-                    tzp::tma_load_2d(smem + kb * C::STAGE_BYTES + C::A_BYTES, &tmB, kb * C::BK,
-                                     (blockIdx.x % n_tiles) * BN, &full[kb]);
+                    uint8_t* sb = smem + kb * C::STAGE_BYTES + C::A_BYTES;
+                    const int nb = (blockIdx.x % n_tiles) * BN;
+                    if constexpr (kBmn) {
+#pragma unroll
+                        for (int j = 0; j < BN / 32; ++j) tzp::tma_load_2d(sb + j * C::BK * 128, &tmB, nb + 32 * j, kb * C::BK, &full[kb]);
+                    } else {
+                        tzp::tma_load_2d(sb, &tmB, kb * C::BK, nb, &full[kb]);
+                    }
                 }
             }
             tzp::pdl_wait();
@@ -390,7 +418,15 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                     const bool b_done = tile == static_cast<int>(blockIdx.x) && kb < pre;
                     if (!b_done) tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
                     tzp::tma_load_2d(sa, &tmA, kb * C::BK, m0, &full[stage]);
-                    if (!b_done) tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, n0, &full[stage]);
+                    if (!b_done) {
+                        if constexpr (kBmn) {
+#pragma unroll
+                            for (int j = 0; j < BN / 32; ++j)
+                                tzp::tma_load_2d(sa + C::A_BYTES + j * C::BK * 128, &tmB, n0 + 32 * j, kb * C::BK, &full[stage]);
+                        } else {
+                            tzp::tma_load_2d(sa + C::A_BYTES, &tmB, kb * C::BK, n0, &full[stage]);
+                        }
+                    }
                     armed |= 1u << stage;
                     armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -407,8 +443,8 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ---- MMA issuer ----
-            constexpr uint32_t idesc =
-                tzp::make_idesc(KindTraits<KIND>::c_fmt, KindTraits<KIND>::ab_fmt, 128, BN);
+            constexpr uint32_t idesc = tzp::make_idesc(KindTraits<KIND>::c_fmt, KindTraits<KIND>::ab_fmt, 128, BN) |
+                                       (kBmn ? (1u << 16) : 0u);  // bit 16: B is MN-major
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -424,10 +460,14 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                     tzp::tc_fence_after();
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
                     const uint64_t ad = tzp::sdesc_k128(tzp::smem_u32(sa));
-                    const uint64_t bd = tzp::sdesc_k128(tzp::smem_u32(sa + C::A_BYTES));
+                    const uint64_t bd = kBmn ? sdesc_mn128_b32(tzp::smem_u32(sa + C::A_BYTES), C::BK * 128)
+                                             : tzp::sdesc_k128(tzp::smem_u32(sa + C::A_BYTES));
+                    // 4 MMA K steps per 128-byte K block: A advances 32 bytes; B advances 32 bytes
+                    // (K-major) or 8 rows, 1024 bytes (MN-major)
+                    constexpr uint32_t kBstep = kBmn ? 1024u >> 4 : 2u;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)  // 4 x 32 bytes of K per 128-byte block
-                        tzp::umma<KIND>(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < 4; ++k)
+                        tzp::umma<KIND>(d, ad + 2u * k, bd + kBstep * k, idesc, (kb | k) != 0 ? 1u : 0u);
                     tzp::umma_commit(&empty[stage]);
                     if (++stage == STAGES) {
                         stage = 0;
@@ -445,7 +485,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             tzp::umma_commit(drain);
             tzp::mbar_wait(drain, 0, status, nullptr);
         }
-    } else if constexpr (FAST != 0) {
+    } else if constexpr (kFastEpi) {
         tzp::pdl_wait();
         // ---- specialised epilogue: straight-line code per tile ----
         // Per tile, before the accumulator is ready: this row's scale and the slice's bias / column
@@ -675,7 +715,7 @@ template <int KIND, int BN, int STAGES, int EPI_WARPS, int FAST = 0>
 int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     using C = Cfg<KIND, BN, STAGES, EPI_WARPS>;
     auto kern = gemm_tc_kernel<KIND, BN, STAGES, EPI_WARPS, FAST>;
-    constexpr int SMEM = FAST != 0 ? C::SMEM_FAST : C::SMEM;
+    constexpr int SMEM = (FAST & F_ON) != 0 ? C::SMEM_FAST : C::SMEM;
     static_assert(SMEM <= 227 * 1024, "shared memory");
     static unsigned attr_set = 0;  // one bit per device
     int dev = 0;
@@ -689,8 +729,13 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     int rc = encode_tmap_2d(&ta, tmap_dtype(KIND), C::ELEM, g.a, static_cast<uint64_t>(g.K), a_rows,
                             static_cast<uint64_t>(g.lda) * C::ELEM, C::BK, 128);
     if (rc) return rc;
-    rc = encode_tmap_2d(&tb, tmap_dtype(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.K),
-                        static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.ldb) * C::ELEM, C::BK, BN);
+    if constexpr ((FAST & F_BMN) != 0)  // B [K, N] row-major: 32-column x BK-row boxes
+        rc = encode_tmap_2d_swz(&tb, tmap_dtype(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.N),
+                                static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.ldb) * C::ELEM, 32, C::BK,
+                                CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    else
+        rc = encode_tmap_2d(&tb, tmap_dtype(KIND), C::ELEM, g.b, static_cast<uint64_t>(g.K),
+                            static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.ldb) * C::ELEM, C::BK, BN);
     if (rc) return rc;
     EpiParams ep{};
     ep.bias = g.bias;
@@ -725,7 +770,7 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     } else {
         to = tb;  // unused
     }
-    if (FAST != 0 && !use_tma) return fail(TZ_EINVAL, "gemm: specialised epilogue without TMA store");
+    if ((FAST & F_ON) != 0 && !use_tma) return fail(TZ_EINVAL, "gemm: specialised epilogue without TMA store");
     const int n_tiles = (g.N + BN - 1) / BN;
     const int tiles = ((g.M + 127) / 128) * n_tiles;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
@@ -785,7 +830,11 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
         // byte of A staged than BN = 128, and no partial tiles.
         case KIND_F16: return g.N % 192 == 0 ? launch_impl<KIND_F16, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_F16, 128, 4, 16>(ctx, g, s);
         case KIND_BF16: return launch_impl<KIND_BF16, 128, 4, 16>(ctx, g, s);
-        case KIND_TF32: return g.N % 192 == 0 ? launch_impl<KIND_TF32, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_TF32, 128, 4, 16>(ctx, g, s);
+        case KIND_TF32:
+            if (g.b_mn)
+                return g.N % 192 == 0 ? launch_impl<KIND_TF32, 192, 4, 16, F_BMN>(ctx, g, s)
+                                      : launch_impl<KIND_TF32, 128, 4, 16, F_BMN>(ctx, g, s);
+            return g.N % 192 == 0 ? launch_impl<KIND_TF32, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_TF32, 128, 4, 16>(ctx, g, s);
         case KIND_I8: return g.N % 192 == 0 ? launch_impl<KIND_I8, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_I8, 128, 4, 16>(ctx, g, s);
         default: return fail(TZ_EINVAL, "gemm: unknown kind %d", g.kind);
     }

@@ -112,6 +112,7 @@ struct GemmArgs {
                                        // (tanh = 2 sigmoid(2x) - 1), 3 ReLU
     unsigned* row_absmax = nullptr;    // [M] atomicMax of |stored value| (float bits)
     int n_ops = -1;                    // >= 0: generic op chain instead of the fixed epilogue
+    bool b_mn = false;                 // tf32 only: b is [K, N] row-major (ldb >= N), read N-major
     int ops[8] = {0};
     bool pdl = false;                  // programmatic dependent launch (inside the model forward)
 };

@@ -99,17 +99,21 @@ int tz_matmul_epilogue(tz_ctx_t ctx, const float* a, const float* b, int trans_b
     for (int i = 0; i < n_ops; ++i)
         TZ_CHECK(ops[i] >= TZ_OP_ADD && ops[i] <= TZ_OP_GELU_ERF, TZ_EINVAL, "tz_matmul_epilogue: bad op %d", ops[i]);
     cudaStream_t s = pick_stream(ctx, stream);
-    const float* bt = b;
-    if (!trans_b) {
-        void* t = nullptr;
-        int rc = scratch_reserve(ctx, sizeof(float) * static_cast<size_t>(k) * n, &t);
-        if (rc) return rc;
-        if ((rc = launch_transpose(b, static_cast<float*>(t), k, n, s))) return rc;  // [k,n] -> [n,k]
-        bt = static_cast<const float*>(t);
-    }
     GemmArgs g;
     g.kind = KIND_TF32;
-    g.a = a; g.lda = k; g.b = bt; g.ldb = k; g.M = m; g.N = n; g.K = k;
+    g.a = a; g.lda = k; g.b = b; g.ldb = k; g.M = m; g.N = n; g.K = k;
+    if (!trans_b) {
+        if (n % 4 == 0) {  // B [k, n] read N-major by the MMA (16-byte rows for TMA)
+            g.b_mn = true;
+            g.ldb = n;
+        } else {
+            void* t = nullptr;
+            int rc = scratch_reserve(ctx, sizeof(float) * static_cast<size_t>(k) * n, &t);
+            if (rc) return rc;
+            if ((rc = launch_transpose(b, static_cast<float*>(t), k, n, s))) return rc;  // [k,n] -> [n,k]
+            g.b = static_cast<const float*>(t);
+        }
+    }
     g.out = c; g.ldo = n; g.out_type = OUT_F32;
     // Chains the fixed epilogue does natively (bias, then one activation) skip the op interpreter.
     const bool has_add = n_ops >= 1 && ops[0] == TZ_OP_ADD;

@@ -95,7 +95,7 @@ int encode_tmap_2d_swz(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
     TZ_CHECK(inner_bytes % 16 == 0 && box_inner <= 256 && box_outer <= 256, TZ_EINVAL,
              "TMA box inner extent must be a multiple of 16 bytes (at most 256 x 256 elements)");
     if (swz != CU_TENSOR_MAP_SWIZZLE_NONE) {
-        const uint32_t span = swz == CU_TENSOR_MAP_SWIZZLE_128B ? 128 : swz == CU_TENSOR_MAP_SWIZZLE_64B ? 64 : 32;
+        const uint32_t span = swz == CU_TENSOR_MAP_SWIZZLE_64B ? 64 : swz == CU_TENSOR_MAP_SWIZZLE_32B ? 32 : 128;
         TZ_CHECK(inner_bytes <= span, TZ_EINVAL, "TMA box too wide for its swizzle");
     }
     cuuint64_t dims[2] = {inner, outer < 1 ? 1 : outer};

@@ -112,6 +112,21 @@ def test_matmul_epilogue_bias_gelu(ctx, oracle, trans_b):
     assert np.abs(c - ref).max() <= 4e-3 * scale
 
 
+@pytest.mark.parametrize("m,k,n", [(77, 40, 260), (129, 64, 128), (1, 96, 4), (300, 384, 200)])
+def test_matmul_epilogue_n_major_b_ragged(ctx, oracle, m, k, n):
+    """B [k, n] read N-major by the tf32 MMA: ragged M, K not a multiple of the 32-element K block,
+    N a multiple of 4 but not of the tile width."""
+    from tenzor_b200 import ops
+    rng = np.random.default_rng(m * 1000 + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    bias = rng.uniform(-1, 1, n).astype(np.float32)
+    for chain, codes in ((["add"], [1]), (["add", "gelu"], [1, 3])):
+        c = host(ops.matmul_epilogue(ctx, dev(a), dev(b), dev(bias), chain))
+        ref = oracle.matmul_epilogue(a, b, bias, codes)
+        assert np.abs(c - ref).max() <= 4e-3 * np.sqrt(k) * 0.6, chain
+
+
 def test_quantize_weight_rows_bit_exact(ctx, oracle):
     from tenzor_b200 import ops
     rng = np.random.default_rng(11)
