@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             uint32_t ra[CW], rb[CW];
             tzp::tmem_ld16(tcol, ra);
             tzp::tmem_ld_wait();
-            __half2 amax2 = __float2half2_rn(0.0f);
+            uint32_t amax2 = 0u;  // packed f16 pair; only the magnitudes are meaningful (xorsign max)
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
                 uint32_t(&cur)[CW] = (c & 1) ? rb : ra;
@@ -572,6 +572,18 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                 // dequantise (+ bias, GELU) two columns per packed f32x2 instruction; the f16 pairs
                 // feed both the staging and the row |max| (max |f16| is exact on the packed halves)
                 uint32_t h[CW / 2];
+                uint64_t bv[CW / 2], sv[CW / 2];  // this chunk's bias / column-scale pairs, 16-byte loads
+#pragma unroll
+                for (int q2 = 0; q2 < CW / 4; ++q2) {
+                    const ulonglong2 tb = *reinterpret_cast<const ulonglong2*>(cvb + 16 * c + 4 * q2);
+                    bv[2 * q2] = tb.x;
+                    bv[2 * q2 + 1] = tb.y;
+                    if constexpr ((FAST & (F_RSCALE | F_CSCALE)) != 0) {
+                        const ulonglong2 ts = *reinterpret_cast<const ulonglong2*>(cvs + 16 * c + 4 * q2);
+                        sv[2 * q2] = ts.x;
+                        sv[2 * q2 + 1] = ts.y;
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < CW / 2; ++j) {
                     float lo, hi;
@@ -583,11 +595,11 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                         hi = __uint_as_float(cur[2 * j + 1]);
                     }
                     uint64_t x = tzp::f2_pack(lo, hi);
-                    const uint64_t b2 = *reinterpret_cast<const uint64_t*>(cvb + 16 * c + 2 * j);
+                    const uint64_t b2 = bv[j];
                     if constexpr ((FAST & F_RSCALE) != 0)
-                        x = tzp::f2_mul(x, tzp::f2_mul(rs2, *reinterpret_cast<const uint64_t*>(cvs + 16 * c + 2 * j)));
+                        x = tzp::f2_mul(x, tzp::f2_mul(rs2, sv[j]));
                     else if constexpr ((FAST & F_CSCALE) != 0)
-                        x = tzp::f2_mul(x, *reinterpret_cast<const uint64_t*>(cvs + 16 * c + 2 * j));
+                        x = tzp::f2_mul(x, sv[j]);
                     x = tzp::f2_add(x, b2);
                     if constexpr ((FAST & F_GELU) != 0) {
                         // GELU (arctic.zig:750-756, hardware tanh): 0.5 x (1 + tanh(x (k0 + k1 x^2))) with
@@ -601,7 +613,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                     const float2 r = tzp::f2_unpack(x);
                     h[j] = tzp::pack_half2(r.x, r.y);
                     if constexpr ((FAST & F_AMAX) != 0)
-                        amax2 = __hmax2(amax2, __habs2(*reinterpret_cast<const __half2*>(&h[j])));
+                        amax2 = tzp::hmax2_xorsign_abs(amax2, h[j]);
                 }
                 const uint32_t buf = wst_a + static_cast<uint32_t>(c * BOX);
 #pragma unroll
@@ -621,7 +633,8 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             pb ^= 1;
             if constexpr ((FAST & F_AMAX) != 0) {
                 if (row_ok)
-                    atomicMax(ep.row_absmax + row, __float_as_uint(fmaxf(__low2float(amax2), __high2float(amax2))));
+                    atomicMax(ep.row_absmax + row, __float_as_uint(fmaxf(fabsf(__low2float(*reinterpret_cast<const __half2*>(&amax2))),
+                                                                         fabsf(__high2float(*reinterpret_cast<const __half2*>(&amax2))))));
             }
             if (++acc == 2) {
                 acc = 0;

@@ -194,6 +194,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// Per f16 half: magnitude max(|a|, |b|), sign sign(a) ^ sign(b) (max.xorsign.abs).  Folding values into
+// a running pair keeps the running |max| in the magnitudes with one instruction per pair.
+__device__ __forceinline__ uint32_t hmax2_xorsign_abs(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 __device__ __forceinline__ float tanh_approx(float x) {
     float y;
     asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
