@@ -325,9 +325,10 @@ struct tz_model_s {
     void *XA = nullptr, *QKV = nullptr, *OA = nullptr, *Hh = nullptr, *HQ = nullptr;
     unsigned* hmax = nullptr;
     unsigned* omax = nullptr;
-    uint32_t* h_ids = nullptr;  // pinned staging
+    uint32_t* h_ids = nullptr;  // pinned staging (used when the caller's buffers are pageable)
     int* h_cu = nullptr;
     float* h_out = nullptr;
+    int* h_status = nullptr;    // pinned slot: the device status word, read back with the output
     // padded-input staging
     uint32_t* d_pad_ids = nullptr;
     int* d_pad_lens = nullptr;
@@ -473,9 +474,11 @@ void free_workspace(tz_model_s* m) {
     if (m->h_ids) cudaFreeHost(m->h_ids);
     if (m->h_cu) cudaFreeHost(m->h_cu);
     if (m->h_out) cudaFreeHost(m->h_out);
+    if (m->h_status) cudaFreeHost(m->h_status);
     m->h_ids = nullptr;
     m->h_cu = nullptr;
     m->h_out = nullptr;
+    m->h_status = nullptr;
     m->cap_batch = 0;
     m->cap_tokens = 0;
     m->d_stages = nullptr;
@@ -536,6 +539,7 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
     TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_ids), sizeof(uint32_t) * T, cudaHostAllocDefault));
     TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_cu), sizeof(int) * (nb + 1), cudaHostAllocDefault));
     TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_out), sizeof(float) * nb * kH, cudaHostAllocDefault));
+    TZ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->h_status), sizeof(int), cudaHostAllocDefault));
     m->cap_batch = nb;
     m->cap_tokens = nt;
     return TZ_OK;
@@ -700,19 +704,44 @@ int forward_to_device(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int
     return enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
 }
 
+bool host_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+// The synchronous host-pointer forward.  The forward itself replays a CUDA graph (keyed by batch,
+// tokens and longest sequence); the copies sit outside it, so page-locked caller buffers are read
+// and written directly and only pageable ones go through the pinned staging.  The device status
+// word comes back with the output: one synchronisation per call.
 int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, float* out) {
     int64_t T = 0;
     int maxL = 0;
     int rc = check_lengths(cu, B, &T, &maxL);
     if (rc) return rc;
-    for (int64_t i = 0; i < T; ++i)
-        TZ_CHECK(ids[i] < static_cast<uint32_t>(kV), TZ_EINVAL, "token id %u at %lld is >= vocab %d", ids[i],
-                 static_cast<long long>(i), kV);
     if ((rc = reserve(m, B, T))) return rc;
     TZ_CUDA(cudaSetDevice(m->ctx->device));
     cudaStream_t s = m->ctx->stream;
-    memcpy(m->h_ids, ids, sizeof(uint32_t) * T);
-    memcpy(m->h_cu, cu, sizeof(int) * (B + 1));
+    const bool ids_pin = host_pinned(ids), cu_pin = host_pinned(cu), out_pin = host_pinned(out);
+    uint32_t bad = 0;  // ids >= vocab, checked in the same pass as the staging copy
+    if (ids_pin) {
+        for (int64_t i = 0; i < T; ++i) bad |= ids[i] >= static_cast<uint32_t>(kV) ? 1u : 0u;
+    } else {
+        for (int64_t i = 0; i < T; ++i) {
+            const uint32_t v = ids[i];
+            bad |= v >= static_cast<uint32_t>(kV) ? 1u : 0u;
+            m->h_ids[i] = v;
+        }
+    }
+    if (bad) {
+        for (int64_t i = 0; i < T; ++i)
+            TZ_CHECK(ids[i] < static_cast<uint32_t>(kV), TZ_EINVAL, "token id %u at %lld is >= vocab %d", ids[i],
+                     static_cast<long long>(i), kV);
+    }
+    if (!cu_pin) memcpy(m->h_cu, cu, sizeof(int) * (B + 1));
     const bool graph_ok = m->use_graph && !m->keep_stages;
     if (graph_ok && !(m->graph && m->g_batch == B && m->g_tokens == T && m->g_maxlen == maxL)) {
         if (m->graph) {
@@ -721,36 +750,34 @@ int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, f
         }
         cudaGraph_t gr = nullptr;
         TZ_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-        int crc = TZ_OK;
-        cudaError_t ce = cudaMemcpyAsync(m->d_ids, m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s);
-        if (ce == cudaSuccess) ce = cudaMemcpyAsync(m->d_cu, m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s);
-        if (ce == cudaSuccess) crc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
-        if (ce == cudaSuccess && !crc) ce = cudaMemcpyAsync(m->h_out, m->out, sizeof(float) * B * kH, cudaMemcpyDeviceToHost, s);
-        cudaError_t ee = cudaStreamEndCapture(s, &gr);
-        if (ce != cudaSuccess) return cuda_fail(ce, "forward capture");
+        const int crc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
+        const cudaError_t ee = cudaStreamEndCapture(s, &gr);
         if (crc) {
             if (gr) cudaGraphDestroy(gr);
             return crc;
         }
         if (ee != cudaSuccess) return cuda_fail(ee, "cudaStreamEndCapture");
-        ce = cudaGraphInstantiate(&m->graph, gr, 0);
+        const cudaError_t ce = cudaGraphInstantiate(&m->graph, gr, 0);
         cudaGraphDestroy(gr);
         if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
         m->g_batch = B;
         m->g_tokens = T;
         m->g_maxlen = maxL;
     }
+    TZ_CUDA(cudaMemcpyAsync(m->d_ids, ids_pin ? ids : m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
+    TZ_CUDA(cudaMemcpyAsync(m->d_cu, cu_pin ? cu : m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s));
     if (graph_ok) {
         TZ_CUDA(cudaGraphLaunch(m->graph, s));
-    } else {
-        TZ_CUDA(cudaMemcpyAsync(m->d_ids, m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
-        TZ_CUDA(cudaMemcpyAsync(m->d_cu, m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s));
-        if ((rc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s))) return rc;
-        TZ_CUDA(cudaMemcpyAsync(m->h_out, m->out, sizeof(float) * B * kH, cudaMemcpyDeviceToHost, s));
+    } else if ((rc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s))) {
+        return rc;
     }
+    TZ_CUDA(cudaMemcpyAsync(out_pin ? out : m->h_out, m->out, sizeof(float) * B * kH, cudaMemcpyDeviceToHost, s));
+    TZ_CUDA(cudaMemcpyAsync(m->h_status, m->ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, s));
     TZ_CUDA(cudaStreamSynchronize(s));
-    if ((rc = read_status(m->ctx, s))) return rc;
-    memcpy(out, m->h_out, sizeof(float) * B * kH);
+    if (*m->h_status) {
+        if ((rc = read_status(m->ctx, s))) return rc;
+    }
+    if (!out_pin) memcpy(out, m->h_out, sizeof(float) * B * kH);
     m->last_T = T;
     return TZ_OK;
 }
