@@ -94,11 +94,12 @@ __device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __res
         const float sc = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
         const float inv = __fdiv_rn(1.0f, sc);
         int8_t* a = static_cast<int8_t*>(aux) + row * kH;
+        const uint64_t inv2 = tzp::f2_pack(inv, inv);  // the row against its own |max|: the packed quantiser applies
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             const int col = c * 128 + lane * 4;
-            *reinterpret_cast<uint32_t*>(a + col) = pack_q4(quant1_bits(v[4 * c], inv), quant1_bits(v[4 * c + 1], inv),
-                                                            quant1_bits(v[4 * c + 2], inv), quant1_bits(v[4 * c + 3], inv));
+            *reinterpret_cast<uint32_t*>(a + col) = __byte_perm(quant2_own_max(v[4 * c], v[4 * c + 1], inv2),
+                                                                quant2_own_max(v[4 * c + 2], v[4 * c + 3], inv2), 0x5410);
         }
         if (lane == 0) aux_s[row] = sc;
     }
@@ -143,12 +144,16 @@ __device__ __forceinline__ void emb_load(float (&v)[12], const float* f, const i
 }
 
 // embeddingsImpl, arctic.zig:543-585: word[id] + pos[p] + type[0], then LayerNorm.  CTA = one
-// 32-row group of the packed tokens (8 warps x 4 tokens); a token's sequence (for its
-// position) comes from a binary search of cu_seqlens.  The LayerNorm rows are assembled in shared
-// memory and leave in the blocked layout of xblk as coalesced 512-byte stores; rows past the batch
-// are written as zeros.  Ids >= vocab raise the bounds bit and embed row 0.
+// 32-row group of the packed tokens (8 warps x 4 tokens).  A token's position needs its sequence: a
+// warp-cooperative search of cu_seqlens finds the group's first sequence (each round probes 32
+// evenly spaced entries, so B <= 32^k sequences take k dependent loads), then one load of the next
+// 32 sequence ends places every row (a ballot per row).  Each warp then requests the word /
+// position / type rows of two tokens at a time before their LayerNorms.  The LayerNorm
+// rows are assembled in shared memory and leave in the blocked layout of xblk as coalesced 512-byte
+// stores; rows past the batch are written as zeros.  Ids >= vocab raise the bounds bit and embed
+// row 0.
 template <int AUX>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
     embed_ln_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, int batch, long long total, EmbTables t,
                     const float* __restrict__ g, const float* __restrict__ b, float* __restrict__ xo, void* aux,
                     float* aux_s, int* status) {
@@ -157,31 +162,58 @@ __global__ void __launch_bounds__(256)
     tzp::pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long g0 = static_cast<long long>(blockIdx.x) * 32;
-    for (int i = 0; i < 4; ++i) {
-        const int r = warp * 4 + i;
-        const long long row = g0 + r;
-        float* xrow = tile + r * kH;
-        if (row >= total) {
+    // the sequence s0 with cu[s0] <= g0 < cu[s0 + 1]: search [lo, hi) by 32-way probes (every warp
+    // runs the same search; the probes hit L1 after the first warp)
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+        const int step = (hi - lo + 31) >> 5;
+        const int idx = lo + lane * step;
+        const bool le = idx < hi && cu[idx] <= g0;  // cu ascending: the probes <= g0 form a prefix
+        const unsigned m = __ballot_sync(0xffffffffu, le);
+        const int k = 31 - __clz(m);                  // last probe <= g0 (probe 0 = cu[lo] always is)
+        lo += k * step;
+        hi = min(lo + step, hi);
+    }
+    // rows g0 .. g0+31 meet at most 32 sequences from s0: lane j holds the end of sequence s0 + j; a
+    // row's sequence is s0 + the number of those ends at or before it
+    const int sj = lo + lane;
+    const int end_j = sj < batch ? cu[sj + 1] : 0x7fffffff;
+    int tid[4], tpos[4];
 #pragma unroll
-            for (int c = 0; c < 3; ++c) *reinterpret_cast<float4*>(xrow + c * 128 + lane * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-        int lo = 0, hi = batch;  // the sequence s with cu[s] <= row < cu[s + 1]
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (cu[mid] <= row) lo = mid; else hi = mid;
-        }
-        const int p = static_cast<int>(row - cu[lo]);
-        uint32_t id = ids[row];
+    for (int i = 0; i < 4; ++i) {
+        const long long row = g0 + warp * 4 + i;
+        const bool in = row < total;
+        const int seq = lo + __popc(__ballot_sync(0xffffffffu, end_j <= row));
+        const int start = (in && seq < batch) ? cu[seq] : 0;
+        uint32_t id = in ? ids[row] : 0u;
         if (id >= static_cast<uint32_t>(kV)) {
             if (lane == 0) atomicOr(status, TZ_DEV_BOUNDS);
             id = 0;
         }
-        const int pos = p < kP ? p : kP - 1;
-        float v[12];
-        emb_load(v, t.word_f, t.word_q, t.word_s, static_cast<int>(id), lane, false);
-        emb_load(v, t.pos_f, t.pos_q, t.pos_s, pos, lane, true);
-        emb_load(v, t.type_f, nullptr, nullptr, 0, lane, true);
-        ln_finish_row<AUX>(v, g, b, xrow, aux, aux_s, row, lane);
+        const long long p = row - start;
+        tid[i] = static_cast<int>(id);
+        tpos[i] = p < kP ? static_cast<int>(p) : kP - 1;
+    }
+#pragma unroll
+    for (int h = 0; h < 4; h += 2) {  // two tokens' gathers in flight together (registers: 4 CTAs per SM)
+        float v[2][12];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            emb_load(v[i], t.word_f, t.word_q, t.word_s, tid[h + i], lane, false);
+            emb_load(v[i], t.pos_f, t.pos_q, t.pos_s, tpos[h + i], lane, true);
+            emb_load(v[i], t.type_f, nullptr, nullptr, 0, lane, true);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int r = warp * 4 + h + i;
+            const long long row = g0 + r;
+            float* xrow = tile + r * kH;
+            if (row >= total) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c) *reinterpret_cast<float4*>(xrow + c * 128 + lane * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                ln_finish_row<AUX>(v[i], g, b, xrow, aux, aux_s, row, lane);
+            }
         }
     }
     __syncthreads();

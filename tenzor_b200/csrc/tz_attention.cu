@@ -123,12 +123,14 @@ __global__ void __launch_bounds__(128)
         tzp::fence_mbar_init();
         tzp::tma_prefetch_desc(&tmQKV);
     }
-    __syncthreads();
-    tzp::pdl_wait();
+    // cu_seqlens is a forward input, written before the forward's first kernel: read it while the
+    // previous kernel (QKV) may still run; Q/K/V are read only after griddepcontrol.wait.
     const int b = blockIdx.z;
     const int h = blockIdx.y;
     const int seq0 = cu_seqlens[b];
     const int L = cu_seqlens[b + 1] - seq0;
+    __syncthreads();
+    tzp::pdl_wait();
     const int q0 = blockIdx.x * kQTile;
     if (L > lpad || L < 0) {  // the caller's max_len was too small: refuse rather than overrun shared memory
         if (tid == 0 && blockIdx.x == 0) atomicOr(status, TZ_DEV_BOUNDS);
