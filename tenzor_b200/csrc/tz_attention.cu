@@ -7,7 +7,7 @@
 // the masked-batch form with key mask = (position < length).
 //
 // CTA = (64-query block, head, sequence); 4 warps x 16 query rows.  K_h and V_h for every key of
-// the sequence and the CTA's Q rows arrive in shared memory as 16-row TMA boxes (32 f16 columns,
+// the sequence and the CTA's Q rows arrive in shared memory as 64- and 16-row TMA boxes (32 f16 columns,
 // 64-byte swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3), so ldmatrix is conflict-free),
 // issued by one thread and completed on one mbarrier; V rows past the sequence's end are zeroed.  S = Q K^T and
 // O = P V run on mma.sync m16n8k16 (f16 in, f32 accumulate) with an online softmax over 64-key
@@ -112,7 +112,8 @@ __device__ __forceinline__ void attend_block(int kb, int L, uint32_t kaddr, uint
 // 86 registers unbounded (5 CTAs = 20 warps per SM); capped for 7 CTAs per SM.
 // 80 registers: 6 CTAs (24 warps) per SM.
 __global__ void __launch_bounds__(128)
-    attention_kernel(const __grid_constant__ CUtensorMap tmQKV, const int* __restrict__ cu_seqlens, int lpad,
+    attention_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmQKV64,
+                     const int* __restrict__ cu_seqlens, int lpad,
                      __half* __restrict__ out, unsigned* __restrict__ row_absmax, int* status) {
     extern __shared__ uint8_t sm_raw[];
     __shared__ uint64_t bar;
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(128)
         tzp::mbar_init(&bar, 1);
         tzp::fence_mbar_init();
         tzp::tma_prefetch_desc(&tmQKV);
+        tzp::tma_prefetch_desc(&tmQKV64);
     }
     // cu_seqlens is a forward input, written before the forward's first kernel: read it while the
     // previous kernel (QKV) may still run; Q/K/V are read only after griddepcontrol.wait.
@@ -144,13 +146,22 @@ __global__ void __launch_bounds__(128)
     uint8_t* qs = sm + 2 * kv_bytes;
     const int nk16 = (L + 15) >> 4;                                  // 16-key boxes of K and of V
     const int nq16 = ((L - q0 < kQTile ? L - q0 : kQTile) + 15) >> 4;  // 16-row boxes of Q
-    if (tid == 0) {
+    if (tid == 0) {  // 64-row boxes where they fit, 16-row boxes for the rest (same shared layout)
         tzp::mbar_arrive_expect_tx(&bar, static_cast<uint32_t>((2 * nk16 + nq16) * 16 * 64));
-        for (int i = 0; i < nk16; ++i) {
+        int i = 0;
+        for (; i + 4 <= nk16; i += 4) {
+            tzp::tma_load_2d(ks + i * 1024, &tmQKV64, kHidden + h * kHd, seq0 + 16 * i, &bar);
+            tzp::tma_load_2d(vs + i * 1024, &tmQKV64, 2 * kHidden + h * kHd, seq0 + 16 * i, &bar);
+        }
+        for (; i < nk16; ++i) {
             tzp::tma_load_2d(ks + i * 1024, &tmQKV, kHidden + h * kHd, seq0 + 16 * i, &bar);
             tzp::tma_load_2d(vs + i * 1024, &tmQKV, 2 * kHidden + h * kHd, seq0 + 16 * i, &bar);
         }
-        for (int i = 0; i < nq16; ++i) tzp::tma_load_2d(qs + i * 1024, &tmQKV, h * kHd, seq0 + q0 + 16 * i, &bar);
+        if (nq16 == 4) {
+            tzp::tma_load_2d(qs, &tmQKV64, h * kHd, seq0 + q0, &bar);
+        } else {
+            for (int j = 0; j < nq16; ++j) tzp::tma_load_2d(qs + j * 1024, &tmQKV, h * kHd, seq0 + q0 + 16 * j, &bar);
+        }
     }
     const bool landed = tzp::mbar_wait(&bar, 0, status, nullptr);
     // Keys in [L, 16 * nk16) are masked to -inf, but their V rows (the next sequence's tokens) still
@@ -244,12 +255,15 @@ int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const 
                                      static_cast<int>(attention_smem_bytes(512))));
         set |= 1u << (dev & 31);
     }
-    CUtensorMap tm;  // QKV f16 [T, 1152]: 16-row x 32-column boxes, 64-byte swizzle; rows >= T read as 0
+    CUtensorMap tm, tm64;  // QKV f16 [T, 1152]: 16- and 64-row x 32-column boxes, 64-byte swizzle; rows >= T read as 0
     int rc = encode_tmap_2d_swz(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens),
                                 kQKV * 2, kHd, 16, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
+    rc = encode_tmap_2d_swz(&tm64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens),
+                            kQKV * 2, kHd, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
     dim3 grid((max_len + kQTile - 1) / kQTile, kHeads, batch);
-    return launch_kernel(attention_kernel, grid, dim3(128), smem, s, pdl, tm, cu_seqlens, lpad, static_cast<__half*>(out),
+    return launch_kernel(attention_kernel, grid, dim3(128), smem, s, pdl, tm, tm64, cu_seqlens, lpad, static_cast<__half*>(out),
                          row_absmax, ctx->d_status);
 }
 
