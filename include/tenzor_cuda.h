@@ -56,6 +56,10 @@ int tz_cuda_synchronize(tz_ctx_t ctx);
  * check fired (bit 1) since the last call.  Reading clears it. */
 int tz_cuda_check_status(tz_ctx_t ctx);
 int tz_cuda_sm_count(tz_ctx_t ctx);
+/* Failure-detection self-test: runs a kernel whose bounded device wait (the one every kernel's
+ * mbarrier waits use) can never be satisfied, so it expires after ~1 s and the kernel returns.
+ * Returns TZ_ETIMEOUT (and clears the status word); the context stays usable. */
+int tz_cuda_selftest_wait(tz_ctx_t ctx);
 
 /* ---- device memory (SPEC.md:834-845 tz_tensor_from_data / copy_to_host) ------------------- */
 int tz_alloc(tz_ctx_t ctx, size_t bytes, void** dptr);

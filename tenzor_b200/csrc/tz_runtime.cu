@@ -113,6 +113,22 @@ int encode_tmap_2d_swz(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
 
 using namespace tz;
 
+namespace {
+// The bounded-wait self-test: one thread waits on an mbarrier that nothing ever arrives on, through
+// the same wait every kernel uses (mbar_wait: globaltimer-bounded, 1 s).  The wait expires, sets
+// the timeout bit of the status word and returns; the kernel exits normally.
+__global__ void selftest_wait_kernel(int* status) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        tzp::mbar_init(&bar, 1);
+        tzp::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) tzp::mbar_wait(&bar, 0, status, nullptr);
+    __syncthreads();
+}
+}  // namespace
+
 extern "C" {
 
 const char* tz_get_last_error(void) { return g_last_error; }
@@ -170,6 +186,15 @@ int tz_cuda_check_status(tz_ctx_t ctx) {
 }
 
 int tz_cuda_sm_count(tz_ctx_t ctx) { return ctx ? ctx->sm_count : 0; }
+
+int tz_cuda_selftest_wait(tz_ctx_t ctx) {
+    TZ_CHECK(ctx, TZ_EINVAL, "null context");
+    TZ_CUDA(cudaSetDevice(ctx->device));
+    selftest_wait_kernel<<<1, 32, 0, ctx->stream>>>(ctx->d_status);
+    TZ_CUDA(cudaGetLastError());
+    TZ_CUDA(cudaStreamSynchronize(ctx->stream));
+    return read_status(ctx, ctx->stream);
+}
 
 int tz_alloc(tz_ctx_t ctx, size_t bytes, void** dptr) {
     TZ_CHECK(ctx && dptr, TZ_EINVAL, "tz_alloc: null argument");

@@ -254,3 +254,22 @@ def test_gather(ctx):
         ctx.check_status()
     assert (host(y)[1] == 0).all()
     ctx.check_status()  # cleared by the read
+
+
+def test_bounded_device_wait_expires_and_context_stays_usable(ctx, oracle):
+    """Failure detection without a GPU fault: a kernel waits on an mbarrier nothing arrives on; its
+    bounded wait (the one every kernel uses) expires after ~1 s, the kernel returns, the host reads
+    TZ_ETIMEOUT from the status word, and the same context keeps computing correctly."""
+    import time
+    from tenzor_b200 import _lib as L, ops
+    t0 = time.perf_counter()
+    rc = L.lib().tz_cuda_selftest_wait(ctx.handle)
+    dt = time.perf_counter() - t0
+    assert rc == L.TZ_ETIMEOUT, rc
+    assert 0.5 < dt < 30
+    assert L.lib().tz_cuda_check_status(ctx.handle) == L.TZ_OK  # the status word was cleared
+    rng = np.random.default_rng(5)
+    x = rng.normal(0, 1, (64, 384)).astype(np.float32)
+    g, b = np.ones(384, np.float32), np.zeros(384, np.float32)
+    y = host(ops.layer_norm_last_dim(ctx, dev(x), dev(g), dev(b), 1e-12))
+    assert np.abs(y - oracle.layernorm(x, g, b, 1e-12)).max() < 2e-5
