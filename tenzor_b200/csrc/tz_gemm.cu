@@ -314,6 +314,9 @@ constexpr int F_ON = 1, F_GELU = 2, F_AMAX = 4, F_RSCALE = 8, F_CSCALE = 16;
 // operands take the 128-byte swizzle with 32-byte atoms (TMA's SWIZZLE_128B_ATOM_32B): 32-byte
 // chunk c of 128-byte row r at c ^ (r % 4), 4-row K groups.
 constexpr int F_BMN = 32;
+// F_3X (general epilogue, tf32 only): the split-operand product of GemmArgs::a3x; the producer maps
+// K block kb of the MMA's K = 3P onto A's [hi | lo] row as hi, hi, lo (P = K / 3).
+constexpr int F_3X = 64;
 
 // Shared-memory descriptor of such an MN-major tile: 128-byte rows along MN (32 tf32 elements),
 // 4-row K groups 512 bytes apart (SBO), MN blocks of 32 elements `lbo` bytes apart (LBO), layout
@@ -340,7 +343,10 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
     constexpr bool kFastEpi = (FAST & F_ON) != 0;
     constexpr bool kBmn = (FAST & F_BMN) != 0;
+    constexpr bool k3x = (FAST & F_3X) != 0;
     static_assert(!kBmn || (KIND == KIND_TF32 && !kFastEpi), "N-major B: tf32, general epilogue");
+    static_assert(!k3x || (KIND == KIND_TF32 && !kFastEpi && !kBmn), "split tf32: tf32, general epilogue");
+    const int part3 = K / 3;  // F_3X: elements of one part
     uint64_t* full = reinterpret_cast<uint64_t*>(staging + (kFastEpi ? C::FAST_STAGING : C::STAGING));
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
@@ -417,7 +423,9 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
                     const bool b_done = tile == static_cast<int>(blockIdx.x) && kb < pre;
                     if (!b_done) tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-                    tzp::tma_load_2d(sa, &tmA, kb * C::BK, m0, &full[stage]);
+                    int ax = kb * C::BK;
+                    if constexpr (k3x) ax = ax < 2 * part3 ? ax % part3 : ax - part3;  // hi, hi, lo
+                    tzp::tma_load_2d(sa, &tmA, ax, m0, &full[stage]);
                     if (!b_done) {
                         if constexpr (kBmn) {
 #pragma unroll
@@ -739,7 +747,8 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     }
     CUtensorMap ta, tb, to;
     const uint64_t a_rows = g.a_rows_alloc > 0 ? static_cast<uint64_t>(g.a_rows_alloc) : static_cast<uint64_t>(g.M);
-    int rc = encode_tmap_2d(&ta, tmap_dtype(KIND), C::ELEM, g.a, static_cast<uint64_t>(g.K), a_rows,
+    const uint64_t a_inner = (FAST & F_3X) != 0 ? static_cast<uint64_t>(2 * (g.K / 3)) : static_cast<uint64_t>(g.K);
+    int rc = encode_tmap_2d(&ta, tmap_dtype(KIND), C::ELEM, g.a, a_inner, a_rows,
                             static_cast<uint64_t>(g.lda) * C::ELEM, C::BK, 128);
     if (rc) return rc;
     if constexpr ((FAST & F_BMN) != 0)  // B [K, N] row-major: 32-column x BK-row boxes
@@ -844,6 +853,11 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
         case KIND_F16: return g.N % 192 == 0 ? launch_impl<KIND_F16, 192, 4, 16>(ctx, g, s) : launch_impl<KIND_F16, 128, 4, 16>(ctx, g, s);
         case KIND_BF16: return launch_impl<KIND_BF16, 128, 4, 16>(ctx, g, s);
         case KIND_TF32:
+            if (g.a3x) {
+                TZ_CHECK(!g.b_mn && g.K % 96 == 0, TZ_EINVAL, "gemm: split tf32 needs K = 3 parts of a multiple of 32");
+                return g.N % 192 == 0 ? launch_impl<KIND_TF32, 192, 4, 16, F_3X>(ctx, g, s)
+                                      : launch_impl<KIND_TF32, 128, 4, 16, F_3X>(ctx, g, s);
+            }
             if (g.b_mn)
                 return g.N % 192 == 0 ? launch_impl<KIND_TF32, 192, 4, 16, F_BMN>(ctx, g, s)
                                       : launch_impl<KIND_TF32, 128, 4, 16, F_BMN>(ctx, g, s);

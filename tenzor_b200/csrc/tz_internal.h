@@ -113,6 +113,10 @@ struct GemmArgs {
     unsigned* row_absmax = nullptr;    // [M] atomicMax of |stored value| (float bits)
     int n_ops = -1;                    // >= 0: generic op chain instead of the fixed epilogue
     bool b_mn = false;                 // tf32 only: b is [K, N] row-major (ldb >= N), read N-major
+    // tf32 only, f32-accurate products from three tf32 ones (x = hi + lo, hi = tf32(x)):
+    // a rows hold [hi | lo] (K/3 each), b rows [hi | lo | hi], and the MMA walks K = 3 parts with A
+    // reading hi, hi, lo: sum hi_a hi_b + hi_a lo_b + lo_a hi_b.  K/3 a multiple of 32.
+    bool a3x = false;
     int ops[8] = {0};
     bool pdl = false;                  // programmatic dependent launch (inside the model forward)
 };

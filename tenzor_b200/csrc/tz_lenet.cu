@@ -8,19 +8,26 @@
 // (conv1 valid, 256 features, logits); TZ_LENET_PAD2 is the benchmark configuration (conv1 zero
 // padding 2, 400 features, softmax over the logits).
 //
-// Two kernels.  lenet_conv_kernel: a persistent CTA walks groups of G images; each group is staged
+// Three launches.  lenet_conv_kernel: a persistent CTA walks groups of G images; each group is staged
 // in shared memory (zero border for the padding), conv1+ReLU+pool writes the pooled map (NHWC) to
-// shared memory, conv2+ReLU+pool writes the flattened features to global memory.  A thread owns one
+// shared memory, conv2+ReLU+pool writes the flattened features to global memory, each split into a
+// tf32 head and its f32 remainder (x = hi + lo exactly), row [hi | lo] of 2 KP floats (KP = the
+// feature count rounded up to 32, zero padding).  A thread owns one
 // pooled output position (all 6 channels for conv1; 8 of the 16 channels for conv2) and its four
 // pre-pool conv outputs, so every input value read feeds 24 (conv1) or 32 (conv2) FMAs and the
 // weights are warp-uniform shared-memory broadcasts.  The inner products run on packed f32x2 FMAs
-// over output-channel pairs (each lane an IEEE fmaf).  lenet_fc_kernel: 64-image tiles; FC weights
-// staged through shared memory in K chunks (transposed so a thread's 8 outputs are contiguous),
-// 4 images x 8 outputs of register blocking per thread, ReLU fused, softmax per image at the end.
-// The work is FMA-bound (0.83 MFLOP per image for the padded variant), not HBM-bound (3 KB in).
+// over output-channel pairs (each lane an IEEE fmaf).  FC1 (400 -> 120, 58% of the FC work) runs on
+// the tensor cores as the split-tf32 GEMM of tz_gemm.cu (GemmArgs::a3x: hi*hi + hi*lo + lo*hi with
+// f32 accumulation, the dropped lo*lo term about 2^-22 of each product) with bias + ReLU in its
+// epilogue, writing h1 [n, 128] f32 (columns 120..127 zero).  lenet_fc_tail_kernel: 64-image tiles;
+// FC2 and FC3 with the weights staged through shared memory in K chunks (transposed so a thread's
+// 8 outputs are contiguous), 4 images x 8 outputs of register blocking per thread, ReLU fused,
+// softmax per image at the end.  The convolutions are FMA-bound (0.83 MFLOP per image for the padded
+// variant), not HBM-bound (3 KB in).
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstring>
 
@@ -36,8 +43,11 @@ struct tz_lenet_s {
     float* c1b = nullptr;     // [8]
     float* c2w = nullptr;     // [25][6][16]: conv2 weight by tap, input channel, output channel
     float* c2b = nullptr;     // [16]
-    float *f1w = nullptr, *f1b = nullptr, *f2w = nullptr, *f2b = nullptr, *f3w = nullptr, *f3b = nullptr;
-    float* d_feat = nullptr;  // [cap, features] scratch between the two kernels
+    float* f1x = nullptr;     // FC1 for the split-tf32 GEMM: [128][3 KP] rows [hi | lo | hi], rows >= 120 zero
+    float* f1b = nullptr;     // [128], zero past 120
+    float *f2w = nullptr, *f2b = nullptr, *f3w = nullptr, *f3b = nullptr;
+    float* d_feat = nullptr;  // [cap, 2 KP] split features between conv and FC1
+    float* d_h1 = nullptr;    // [cap, 128] FC1 output
     int64_t cap = 0;
     float* d_io = nullptr;    // host-API staging: images [cap_io, 784] then logits [cap_io, 10]
     int64_t cap_io = 0;
@@ -59,6 +69,7 @@ struct LenetShape {
     static constexpr int C2 = P1 - 4;            // conv2 output 8 / 10
     static constexpr int P2 = C2 / 2;            // pool2 4 / 5
     static constexpr int FEAT = P2 * P2 * 16;    // 256 / 400
+    static constexpr int KP = (FEAT + 31) / 32 * 32;  // 256 / 416: one part of the split-tf32 K
     static constexpr int G = PAD ? 5 : 8;        // images per group: G * P2 * P2 * 2 <= 256 conv2 items
     static constexpr int SMEM_FLOATS = 25 * 8 + 8 + 25 * 6 * 16 + 16 + G * PW * PW + G * P1 * P1 * 6;
 };
@@ -195,9 +206,17 @@ __global__ void __launch_bounds__(kThreads)
                 m[2 * c] = m0;
                 m[2 * c + 1] = m1;
             }
-            float* dst = feat + (img0 + g) * S::FEAT + (py * S::P2 + px) * 16 + half * 8;
-            *reinterpret_cast<float4*>(dst) = make_float4(m[0], m[1], m[2], m[3]);
-            *reinterpret_cast<float4*>(dst + 4) = make_float4(m[4], m[5], m[6], m[7]);
+            float hi[8], lo[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                hi[c] = tzp::tf32_rna(m[c]);
+                lo[c] = m[c] - hi[c];  // exact: hi and m share the exponent range, hi holds m's top bits
+            }
+            float* dst = feat + (img0 + g) * (2 * S::KP) + (py * S::P2 + px) * 16 + half * 8;
+            *reinterpret_cast<float4*>(dst) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<float4*>(dst + 4) = make_float4(hi[4], hi[5], hi[6], hi[7]);
+            *reinterpret_cast<float4*>(dst + S::KP) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<float4*>(dst + S::KP + 4) = make_float4(lo[4], lo[5], lo[6], lo[7]);
         }
         __syncthreads();
     }
@@ -261,29 +280,33 @@ __device__ __forceinline__ void fc_layer(const float* s_in, const float* __restr
     __syncthreads();
 }
 
-template <int FEAT, bool SOFTMAX>
+template <bool SOFTMAX>
 __global__ void __launch_bounds__(kThreads)
-    lenet_fc_kernel(const float* __restrict__ feat, int64_t n, const float* __restrict__ f1w,
-                    const float* __restrict__ f1b, const float* __restrict__ f2w, const float* __restrict__ f2b,
-                    const float* __restrict__ f3w, const float* __restrict__ f3b, float* __restrict__ out) {
-    constexpr int L0 = FEAT + 1, L1 = 121, L2 = 85, L3 = 11;
+    lenet_fc_tail_kernel(const float* __restrict__ h1, int64_t n, const float* __restrict__ f2w,
+                         const float* __restrict__ f2b, const float* __restrict__ f3w, const float* __restrict__ f3b,
+                         float* __restrict__ out) {
+    constexpr int L1 = 121, L2 = 85, L3 = 11;
     extern __shared__ __align__(16) float sm[];
-    float* s_x = sm;                  // [64][L0]
-    float* s_h1 = s_x + kTile * L0;   // [64][L1]
+    float* s_h1 = sm;                 // [64][L1]
     float* s_h2 = s_h1 + kTile * L1;  // [64][L2]
     float* s_wc = s_h2 + kTile * L2;  // [kKC][128 + 4]
-    float* s_o = s_x;                 // [64][L3], reuses s_x after FC1
+    float* s_o = s_h1;                // [64][L3], reuses s_h1 after FC2
     const int tid = threadIdx.x;
     const int64_t tiles = (n + kTile - 1) / kTile;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
         const int64_t base = t * kTile;
         const int cnt = static_cast<int>(n - base < kTile ? n - base : kTile);
         __syncthreads();
-        for (int i = tid; i < kTile * FEAT; i += kThreads) {
-            const int r = i / FEAT, k = i % FEAT;
-            s_x[r * L0 + k] = r < cnt ? feat[(base + r) * FEAT + k] : 0.0f;
+        for (int i = tid; i < kTile * 30; i += kThreads) {  // 120 columns as float4
+            const int r = i / 30, k = (i % 30) * 4;
+            const float4 v = r < cnt ? *reinterpret_cast<const float4*>(h1 + (base + r) * 128 + k)
+                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float* d = s_h1 + r * L1 + k;
+            d[0] = v.x;
+            d[1] = v.y;
+            d[2] = v.z;
+            d[3] = v.w;
         }
-        fc_layer<FEAT, 120, L0, L1, true>(s_x, f1w, f1b, s_h1, s_wc);
         fc_layer<120, 84, L1, L2, true>(s_h1, f2w, f2b, s_h2, s_wc);
         fc_layer<84, 10, L2, L3, false>(s_h2, f3w, f3b, s_o, s_wc);
         if (tid < cnt) {
@@ -310,17 +333,18 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// feat: [n, 2 KP] split features, h1: [n, 128] FC1 output; both slices of the model's scratch.
 template <int PAD>
-int launch_lenet(tz_lenet_s* m, const float* d_images, int64_t n, float* d_out, cudaStream_t s, float* feat) {
+int launch_lenet(tz_lenet_s* m, const float* d_images, int64_t n, float* d_out, cudaStream_t s, float* feat,
+                 float* h1) {
     using S = LenetShape<PAD>;
     const int conv_smem = S::SMEM_FLOATS * 4;
-    constexpr int FEAT = S::FEAT;
-    const int fc_smem = (kTile * (FEAT + 1) + kTile * 121 + kTile * 85 + kKC * 132) * 4;
+    const int fc_smem = (kTile * 121 + kTile * 85 + kKC * 132) * 4;
     static unsigned set = 0;
     const unsigned bit = 1u << (m->device & 31);
     if (!(set & bit)) {
         TZ_CUDA(cudaFuncSetAttribute(lenet_conv_kernel<PAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, conv_smem));
-        TZ_CUDA(cudaFuncSetAttribute(lenet_fc_kernel<FEAT, PAD != 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, fc_smem));
+        TZ_CUDA(cudaFuncSetAttribute(lenet_fc_tail_kernel<PAD != 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, fc_smem));
         set |= bit;
     }
     const int sms = m->ctx->sm_count;
@@ -328,12 +352,43 @@ int launch_lenet(tz_lenet_s* m, const float* d_images, int64_t n, float* d_out, 
     const int g1 = static_cast<int>(groups < 4LL * sms ? groups : 4LL * sms);
     lenet_conv_kernel<PAD><<<g1, kThreads, conv_smem, s>>>(d_images, n, m->c1w, m->c1b, m->c2w, m->c2b, feat);
     TZ_CUDA(cudaGetLastError());
+    for (int64_t r = 0; r < n; r += INT32_MAX / 2) {  // the GEMM takes int M
+        const int64_t rows = std::min<int64_t>(n - r, INT32_MAX / 2);
+        GemmArgs g;
+        g.kind = KIND_TF32;
+        g.a3x = true;
+        g.a = feat + 2 * S::KP * r;
+        g.lda = 2 * S::KP;
+        g.b = m->f1x;
+        g.ldb = 3 * S::KP;
+        g.M = static_cast<int>(rows);
+        g.N = 128;
+        g.K = 3 * S::KP;
+        g.bias = m->f1b;
+        g.gelu = 3;  // ReLU
+        g.out = h1 + 128 * r;
+        g.ldo = 128;
+        g.out_type = OUT_F32;
+        const int rc = launch_gemm(m->ctx, g, s);
+        if (rc) return rc;
+    }
     const int64_t tiles = (n + kTile - 1) / kTile;
-    const int g2 = static_cast<int>(tiles < sms ? tiles : sms);
-    lenet_fc_kernel<FEAT, PAD != 0><<<g2, kThreads, fc_smem, s>>>(feat, n, m->f1w, m->f1b, m->f2w, m->f2b, m->f3w,
-                                                                  m->f3b, d_out);
+    const int g2 = static_cast<int>(tiles < 2LL * sms ? tiles : 2LL * sms);
+    lenet_fc_tail_kernel<PAD != 0><<<g2, kThreads, fc_smem, s>>>(h1, n, m->f2w, m->f2b, m->f3w, m->f3b, d_out);
     TZ_CUDA(cudaGetLastError());
     return TZ_OK;
+}
+
+int lenet_kp(int variant) { return variant == TZ_LENET_PAD2 ? LenetShape<2>::KP : LenetShape<0>::KP; }
+
+// Nearest tf32 value of a finite f32, ties away from zero (the rounding of cvt.rna.tf32.f32).
+float tf32_rna_host(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
 }
 
 int lenet_reserve(tz_lenet_s* m, int64_t n) {
@@ -341,11 +396,15 @@ int lenet_reserve(tz_lenet_s* m, int64_t n) {
     TZ_CUDA(cudaSetDevice(m->device));
     TZ_CUDA(cudaDeviceSynchronize());
     if (m->d_feat) cudaFree(m->d_feat);
-    m->d_feat = nullptr;
+    if (m->d_h1) cudaFree(m->d_h1);
+    m->d_feat = m->d_h1 = nullptr;
     m->cap = 0;
-    const int feat = m->variant == TZ_LENET_PAD2 ? 400 : 256;
-    if (cudaMalloc(reinterpret_cast<void**>(&m->d_feat), sizeof(float) * feat * static_cast<size_t>(n)) != cudaSuccess)
+    const size_t row = 2 * static_cast<size_t>(lenet_kp(m->variant));
+    if (cudaMalloc(reinterpret_cast<void**>(&m->d_feat), sizeof(float) * row * static_cast<size_t>(n)) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&m->d_h1), sizeof(float) * 128 * static_cast<size_t>(n)) != cudaSuccess)
         return fail(TZ_ENOMEM, "tz_lenet: feature scratch for %lld images", static_cast<long long>(n));
+    // the padding columns of each [hi | lo] row are never written: zero them once
+    TZ_CUDA(cudaMemset(m->d_feat, 0, sizeof(float) * row * static_cast<size_t>(n)));
     m->cap = n;
     return TZ_OK;
 }
@@ -365,8 +424,11 @@ int tz_lenet_load(tz_ctx_t ctx, const tz_lenet_weights* w, int variant, tz_lenet
                           w->fc1_b,   w->fc2_w,   w->fc2_b,   w->fc3_w,   w->fc3_b};
     for (const float* p : req) TZ_CHECK(p, TZ_EMISSING, "tz_lenet_load: a weight pointer is NULL");
     const int feat = variant == TZ_LENET_PAD2 ? 400 : 256;
-    // device layout: conv1 [25][8] + [8], conv2 [25][6][16] + [16], FC weights as given
-    const size_t n_c1 = 25 * 8 + 8, n_c2 = 25 * 96 + 16, n_f1 = 120 * feat + 120, n_f2 = 84 * 120 + 84, n_f3 = 10 * 84 + 10;
+    const int kp = lenet_kp(variant);
+    // device layout: conv1 [25][8] + [8], conv2 [25][6][16] + [16], FC1 split [128][3 kp] + [128],
+    // FC2 and FC3 as given
+    const size_t n_c1 = 25 * 8 + 8, n_c2 = 25 * 96 + 16, n_f1 = 128 * 3 * static_cast<size_t>(kp) + 128,
+                 n_f2 = 84 * 120 + 84, n_f3 = 10 * 84 + 10;
     const size_t total = n_c1 + n_c2 + n_f1 + n_f2 + n_f3;
     float* h = new float[total];
     std::memset(h, 0, sizeof(float) * total);
@@ -379,8 +441,15 @@ int tz_lenet_load(tz_ctx_t ctx, const tz_lenet_weights* w, int variant, tz_lenet
             for (int ic = 0; ic < 6; ++ic) c2[tap * 96 + ic * 16 + oc] = w->conv2_w[(oc * 25 + tap) * 6 + ic];
     for (int oc = 0; oc < 16; ++oc) c2[2400 + oc] = w->conv2_b[oc];
     float* f = c2 + n_c2;
-    std::memcpy(f, w->fc1_w, sizeof(float) * 120 * feat);
-    std::memcpy(f + 120 * feat, w->fc1_b, sizeof(float) * 120);
+    for (int o = 0; o < 120; ++o)  // row o: [hi | lo | hi] of W1[o, :], each part kp wide
+        for (int k = 0; k < feat; ++k) {
+            const float x = w->fc1_w[o * feat + k], hi = tf32_rna_host(x);
+            float* r = f + static_cast<size_t>(o) * 3 * kp;
+            r[k] = hi;
+            r[kp + k] = x - hi;
+            r[2 * kp + k] = hi;
+        }
+    std::memcpy(f + 128 * 3 * static_cast<size_t>(kp), w->fc1_b, sizeof(float) * 120);
     f += n_f1;
     std::memcpy(f, w->fc2_w, sizeof(float) * 84 * 120);
     std::memcpy(f + 84 * 120, w->fc2_b, sizeof(float) * 84);
@@ -405,9 +474,9 @@ int tz_lenet_load(tz_ctx_t ctx, const tz_lenet_weights* w, int variant, tz_lenet
     m->c1b = m->c1w + 200;
     m->c2w = m->d_w + n_c1;
     m->c2b = m->c2w + 2400;
-    m->f1w = m->c2w + n_c2;
-    m->f1b = m->f1w + 120 * feat;
-    m->f2w = m->f1w + n_f1;
+    m->f1x = m->c2w + n_c2;
+    m->f1b = m->f1x + 128 * 3 * static_cast<size_t>(kp);
+    m->f2w = m->f1x + n_f1;
     m->f2b = m->f2w + 84 * 120;
     m->f3w = m->f2w + n_f2;
     m->f3b = m->f3w + 840;
@@ -421,6 +490,7 @@ int tz_lenet_free(tz_lenet_t m) {
     cudaDeviceSynchronize();
     if (m->d_w) cudaFree(m->d_w);
     if (m->d_feat) cudaFree(m->d_feat);
+    if (m->d_h1) cudaFree(m->d_h1);
     if (m->d_io) cudaFree(m->d_io);
     if (m->h_out) cudaFreeHost(m->h_out);
     if (m->s2) cudaStreamDestroy(m->s2);
@@ -442,8 +512,8 @@ int tz_lenet_forward_device(tz_lenet_t m, const float* images, int64_t n, float*
     int rc = lenet_reserve(m, n);
     if (rc) return rc;
     cudaStream_t s = pick_stream(m->ctx, stream);
-    return m->variant == TZ_LENET_PAD2 ? launch_lenet<2>(m, images, n, out, s, m->d_feat)
-                                       : launch_lenet<0>(m, images, n, out, s, m->d_feat);
+    return m->variant == TZ_LENET_PAD2 ? launch_lenet<2>(m, images, n, out, s, m->d_feat, m->d_h1)
+                                       : launch_lenet<0>(m, images, n, out, s, m->d_feat, m->d_h1);
 }
 
 int tz_lenet_forward(tz_lenet_t m, const float* images, int64_t n, float* out) {
@@ -473,7 +543,7 @@ int tz_lenet_forward(tz_lenet_t m, const float* images, int64_t n, float* out) {
     // staging and of the feature scratch: no chunk waits for another's buffers.  Probabilities come
     // back through pinned staging (a copy into pageable memory would block the host between chunks).
     cudaStream_t st[2] = {m->ctx->stream, m->s2};
-    const int feat = m->variant == TZ_LENET_PAD2 ? 400 : 256;
+    const int64_t row = 2 * lenet_kp(m->variant);
     const int64_t chunk = n <= 8192 ? n : std::max<int64_t>(4096, ((n + 7) / 8 + kTile - 1) / kTile * kTile);
     TZ_CUDA(cudaEventRecord(m->ev, st[0]));  // s2 starts after the work already queued on the context's stream
     TZ_CUDA(cudaStreamWaitEvent(st[1], m->ev, 0));
@@ -483,8 +553,10 @@ int tz_lenet_forward(tz_lenet_t m, const float* images, int64_t n, float* out) {
         float* d_img = m->d_io + 784 * a;
         float* d_out = m->d_io + 784 * n + 10 * a;
         TZ_CUDA(cudaMemcpyAsync(d_img, images + 784 * a, sizeof(float) * 784 * c, cudaMemcpyHostToDevice, st[k]));
-        rc = m->variant == TZ_LENET_PAD2 ? launch_lenet<2>(m, d_img, c, d_out, st[k], m->d_feat + feat * a)
-                                         : launch_lenet<0>(m, d_img, c, d_out, st[k], m->d_feat + feat * a);
+        float* feat = m->d_feat + row * a;
+        float* h1 = m->d_h1 + 128 * a;
+        rc = m->variant == TZ_LENET_PAD2 ? launch_lenet<2>(m, d_img, c, d_out, st[k], feat, h1)
+                                         : launch_lenet<0>(m, d_img, c, d_out, st[k], feat, h1);
         if (rc) return rc;
         TZ_CUDA(cudaMemcpyAsync(m->h_out + 10 * a, d_out, sizeof(float) * 10 * c, cudaMemcpyDeviceToHost, st[k]));
     }

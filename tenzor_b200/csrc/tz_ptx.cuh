@@ -150,6 +150,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 // Hardware tanh (PTX tanh.approx.f32, max relative error about 2^-11).
 // ---- packed f32x2 arithmetic (sm_100): two independent IEEE round-to-nearest operations per
 // instruction, bit-identical to the scalar __fmaf_rn / __fmul_rn / __fadd_rn / __fsub_rn. ----------
+// Nearest tf32 value (10-bit mantissa, low 13 bits zero), ties away from zero.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
     uint64_t r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
