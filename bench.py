@@ -13,9 +13,10 @@ U{1000..30521}; the W8A8 tensor-core path.  Weak scaling: every rank runs its ow
             each step's forward + gather, L2 flushed before every step), max over ranks.
 `e2e`     : the same metric through the public host API (tz_arctic_forward: host ids in, host
             embeddings out; H2D + D2H inside the timed call), wall time of the synchronous call.
-`roofline`: the dominant kernel class, its algorithmic FLOPs (or bytes) per launch over its
+`roofline`: the dominant kernel class, its algorithmic FLOPs and bytes per launch over its
             average launch duration, measured with CUDA events recorded between launches on the
-            launching stream during the timed steps.
+            launching stream during the timed steps; `bound` is the binding limit (the larger of
+            FLOPs / tensor peak and bytes / HBM peak), `limits` carries both fractions.
 `--impl reference`: the reference's CPU algorithm (C restatement; the Zig reference cannot be
             built here) on the host cores, rank 0 only.
 `--model lenet`: BASELINE configs[4], LeNet-5 (padded variant, softmax) over 65536 seeded U[0,1]
@@ -59,6 +60,26 @@ def peaks():
         d = json.load(open(p))
         return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
     return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def class_bytes(cls, T, B, int8):
+    """Algorithmic HBM bytes of one launch of a forward kernel class: the operands it must read and
+    the results it must write, each once (weights once per launch), for T packed tokens.  Per token:
+    the GEMM operand XA is int8 + an f32 scale (W8A8) or f16; QKV, the attention output OA and the
+    FFN hidden H are f16 (W8A8 adds a u32 row |max| to OA and H); the residual stream X is f32, read
+    and rewritten by each GEMM+LayerNorm kernel, which also writes the next XA."""
+    a_in = 384 + 4 if int8 else 768
+    amax = 4 if int8 else 0
+    wb = 1 if int8 else 2
+    return {0: T * 384 * (4 + 1 + 4) + T * 384 * 2,
+            1: T * (a_in + 1152 * 2) + 1152 * 384 * wb,
+            2: T * (1152 * 2 + 384 * 2),
+            3: T * (384 * 2 + amax + 384 * 4 * 2 + a_in) + 384 * 384 * wb,
+            4: T * 384 * (4 + 4 + 1) + T * 4,
+            5: T * (a_in + 1536 * 2 + amax) + 1536 * 384 * wb,
+            6: T * 1536 * 3 + T * 8,
+            7: T * (1536 * 2 + amax + 384 * 4 * 2 + a_in) + 384 * 1536 * wb,
+            8: B * 384 * 8}[cls]
 
 
 def measured_int8_peak():
@@ -421,24 +442,29 @@ def run_ours(a):
         dom_ms, dom = max(per)
         avg_ms = dom_ms / cls_n[dom]
         Tl = T
+        int8 = a.mode == "w8a8"
         flops = {1: 2 * Tl * 384 * 1152, 3: 2 * Tl * 384 * 384, 5: 2 * Tl * 384 * 1536, 7: 2 * Tl * 1536 * 384,
                  2: 4 * 384 * float((l_lens.astype(np.float64) ** 2).sum())}
-        int8 = a.mode == "w8a8"
+        byts = class_bytes(dom, Tl, B, int8)
+        t_hbm = byts / (hbm * 1e9)
+        hbm_side = {"achieved": byts / (avg_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                    "peak_source": f"{src} HBM copy", "bytes_per_launch": byts}
+        hbm_side["frac"] = hbm_side["achieved"] / hbm
+        sides = {"hbm": hbm_side}
         if dom in flops:
-            bound, unit = "tensor", "TFLOP/s"
-            achieved = flops[dom] / (avg_ms / 1e3) / 1e12
             if dom == 2:
-                peak, peak_note = bf16_sus, f"dense f16 = {src} bf16 sustained"
+                tpeak, tnote = bf16_sus, f"dense f16 = {src} bf16 sustained"
             elif int8:
-                peak, peak_note = measured_int8_peak(), "int8 dense, cuBLAS torch._int_mm 8192^3 measured in this run"
+                tpeak, tnote = measured_int8_peak(), "int8 dense, cuBLAS torch._int_mm 8192^3 measured in this run"
             else:
-                peak, peak_note = bf16_sus, f"f16 = {src} bf16 sustained"
-        else:
-            bound, unit = "hbm", "GB/s"
-            byts = {0: Tl * 384 * (4 + 1 + 4) + Tl * 384 * 2, 4: Tl * 384 * (4 + 4 + 1) + Tl * 4,
-                    6: Tl * 1536 * 3 + Tl * 8, 8: B * 384 * 8}[dom]
-            achieved = byts / (avg_ms / 1e3) / 1e9
-            peak, peak_note = hbm, f"{src} HBM copy"
+                tpeak, tnote = bf16_sus, f"f16 = {src} bf16 sustained"
+            ach = flops[dom] / (avg_ms / 1e3) / 1e12
+            sides["tensor"] = {"achieved": ach, "peak": tpeak, "unit": "TFLOP/s", "peak_source": tnote,
+                               "flops_per_launch": flops[dom], "frac": ach / tpeak}
+        # the binding limit: the larger of (FLOPs / tensor peak) and (algorithmic bytes / HBM peak)
+        bound = "tensor" if "tensor" in sides and flops[dom] / (sides["tensor"]["peak"] * 1e12) > t_hbm else "hbm"
+        b_side = sides[bound]
+        achieved, peak, unit, peak_note = b_side["achieved"], b_side["peak"], b_side["unit"], b_side["peak_source"]
         tr = traffic_table().get(f"{CLASS_NAMES[dom]}_{a.mode}_{a.config}")
         dom_flops_or_bytes = flops.get(dom)
         cfg = CONFIGS[a.config]
@@ -455,7 +481,8 @@ def run_ours(a):
                        "useful_gflop_per_step": flop_useful(lens) / 1e9},
             "roofline": {"kernel": CLASS_NAMES[dom], "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "peak_source": peak_note, "traffic": tr,
-                         "per_launch_work": dom_flops_or_bytes, "avg_launch_ms": avg_ms,
+                         "per_launch_work": byts if bound == "hbm" else dom_flops_or_bytes, "avg_launch_ms": avg_ms,
+                         "limits": sides,
                          "class_ms_per_forward": {CLASS_NAMES[c]: round(cls_ms[c] / nfwd, 4) for c in range(9) if cls_n[c]},
                          "profiled_ms_per_step": ms_prof / a.steps},
             "e2e": {"value": e2e_value, "unit": "seq/s", "h2d_bytes_per_step": int(T * 4 + (B + 1) * 4),
