@@ -299,6 +299,41 @@ int tz_lenet_forward(tz_lenet_t model, const float* images, int64_t n, float* ou
 int tz_lenet_forward_device(tz_lenet_t model, const float* images, int64_t n, float* out,
                             tz_stream_t stream);
 
+/* ---- .tenzor checkpoint files --------------------------------------------------------------
+ * The reference's own format (src/io/tenzor_format.zig): 64-byte header, metadata JSON, 48-byte
+ * index entries keyed by the FNV-1a hash of the tensor name, 4 KiB-aligned data.  The file is
+ * memory-mapped read-only and tensor data is used in place (TenzorFile.open, 140-199). */
+typedef struct tz_tenzor_s* tz_tenzor_t;
+enum { /* DType, tenzor_format.zig:26-38 */
+    TZ_DT_F32 = 0, TZ_DT_F16 = 1, TZ_DT_BF16 = 2, TZ_DT_F64 = 3, TZ_DT_I8 = 4, TZ_DT_I16 = 5,
+    TZ_DT_I32 = 6, TZ_DT_I64 = 7, TZ_DT_U8 = 8, TZ_DT_U16 = 9, TZ_DT_U32 = 10, TZ_DT_U64 = 11
+};
+typedef struct { /* TensorEntry (tenzor_format.zig:84-104), data resolved into the mapping */
+    uint64_t name_hash;
+    int dtype, ndim;
+    uint32_t shape[5];
+    const void* data; /* valid until tz_tenzor_close */
+    uint64_t bytes;
+} tz_tenzor_entry;
+/* hashName (tenzor_format.zig:107-114): FNV-1a 64 of the name's bytes. */
+uint64_t tz_tenzor_hash_name(const char* name, size_t len);
+/* TenzorFile.open / close.  TZ_EINVAL for a bad magic, version, or offsets outside the file. */
+int tz_tenzor_open(const char* path, tz_tenzor_t* out);
+int tz_tenzor_close(tz_tenzor_t file);
+int64_t tz_tenzor_count(tz_tenzor_t file);
+int tz_tenzor_entry_at(tz_tenzor_t file, int64_t index, tz_tenzor_entry* out);
+/* getTensor (tenzor_format.zig:224-226); TZ_EMISSING when no entry has the name's hash. */
+int tz_tenzor_find(tz_tenzor_t file, const char* name, tz_tenzor_entry* out);
+/* The metadata JSON bytes (not NUL-terminated), valid until tz_tenzor_close. */
+int tz_tenzor_metadata(tz_tenzor_t file, const char** json, uint64_t* len);
+/* A LeNet training checkpoint (names conv1_weight .. fc3_bias, f32; main.zig:502-511, read back by
+ * runEval 638-667) -> tz_lenet_load.  Every tensor is required (TZ_EMISSING otherwise). */
+int tz_lenet_load_tenzor(tz_ctx_t ctx, const char* path, int variant, tz_lenet_t* out);
+/* An Arctic checkpoint converted from safetensors (convertFromSafetensors, tenzor_format.zig:
+ * 441-485: safetensors names and dtypes kept) -> tz_arctic_load, names resolved as in
+ * tz_arctic_load_safetensors. */
+int tz_arctic_load_tenzor(tz_ctx_t ctx, const char* path, int mode, tz_model_t* out);
+
 /* ---- text -> device ids -> embeddings ------------------------------------------------------
  * The WordPiece tokenizer of src/io/tokenizer.zig (host code: string work) and the embed CLI's two
  * text paths of main.zig on the device.  Special ids are [UNK] 100, [CLS] 101, [SEP] 102

@@ -32,7 +32,9 @@ EXPORTS = [
     "tz_lenet_forward_device", "tz_tokenizer_create", "tz_tokenizer_free", "tz_tokenizer_set_special",
     "tz_tokenizer_load_vocab", "tz_tokenizer_load_vocab_bytes", "tz_tokenizer_put", "tz_tokenizer_vocab_size",
     "tz_tokenizer_encode", "tz_tokenizer_encode_raw", "tz_tokenizer_encode_batch", "tz_arctic_embed_texts",
-    "tz_doc_chunk_count", "tz_arctic_embed_documents",
+    "tz_doc_chunk_count", "tz_arctic_embed_documents", "tz_tenzor_hash_name", "tz_tenzor_open",
+    "tz_tenzor_close", "tz_tenzor_count", "tz_tenzor_entry_at", "tz_tenzor_find", "tz_tenzor_metadata",
+    "tz_lenet_load_tenzor", "tz_arctic_load_tenzor",
 ]
 
 
@@ -54,6 +56,11 @@ class ArcticLayer(C.Structure):
     _fields_ += [(n, P) for n in ("query_bias", "key_bias", "value_bias", "attn_output_bias",
                                   "intermediate_bias", "output_bias", "attn_ln_gamma", "attn_ln_beta",
                                   "output_ln_gamma", "output_ln_beta")]
+
+
+class TenzorEntry(C.Structure):
+    _fields_ = [("name_hash", C.c_uint64), ("dtype", C.c_int), ("ndim", C.c_int), ("shape", C.c_uint32 * 5),
+                ("data", P), ("bytes", C.c_uint64)]
 
 
 class EwInstr(C.Structure):
@@ -131,6 +138,12 @@ def _declare(L):
         "tz_tokenizer_encode_batch": [P, P, P, i, i, P, P, i64],
         "tz_arctic_embed_texts": [P, P, P, P, i, P],
         "tz_arctic_embed_documents": [P, P, P, P, i, P],
+        "tz_tenzor_open": [C.c_char_p, C.POINTER(P)], "tz_tenzor_close": [P],
+        "tz_tenzor_entry_at": [P, i64, C.POINTER(TenzorEntry)],
+        "tz_tenzor_find": [P, C.c_char_p, C.POINTER(TenzorEntry)],
+        "tz_tenzor_metadata": [P, C.POINTER(C.c_char_p), C.POINTER(C.c_uint64)],
+        "tz_lenet_load_tenzor": [P, C.c_char_p, i, C.POINTER(P)],
+        "tz_arctic_load_tenzor": [P, C.c_char_p, i, C.POINTER(P)],
     }
     for name, args in sig.items():
         f = getattr(L, name)
@@ -138,6 +151,10 @@ def _declare(L):
         f.restype = C.c_int
     L.tz_doc_chunk_count.argtypes = [i64]
     L.tz_doc_chunk_count.restype = i64
+    L.tz_tenzor_hash_name.argtypes = [C.c_char_p, u]
+    L.tz_tenzor_hash_name.restype = C.c_uint64
+    L.tz_tenzor_count.argtypes = [P]
+    L.tz_tenzor_count.restype = i64
 
 
 def check(rc: int):

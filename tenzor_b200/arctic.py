@@ -4,6 +4,7 @@ the sm_100a kernels of libtenzor_cuda.so.
 Reference -> here:
   Config (arctic.zig:29-45)                        -> Config
   ModelWeights.fromSafeTensors (arctic.zig:113)    -> ArcticModel.from_safetensors / from_checkpoint
+  TenzorFile (tenzor_format.zig:140)               -> ArcticModel.from_tenzor
   forward(output, token_ids, weights, ctx) (874)   -> ArcticModel.forward(token_ids)
   forwardBatch / forwardBatchParallel (902, 959)   -> ArcticModel.forward_batch(list_of_ids)
   (packed device batch, no counterpart)            -> ArcticModel.forward_packed / forward_padded
@@ -131,6 +132,13 @@ class ArcticModel:
     def from_safetensors(cls, ctx: Context, path: str, mode: str = "f32") -> "ArcticModel":
         h = C.c_void_p()
         L.check(L.lib().tz_arctic_load_safetensors(ctx.handle, path.encode(), MODES[mode], C.byref(h)))
+        return cls(ctx, h, mode)
+
+    @classmethod
+    def from_tenzor(cls, ctx: Context, path: str, mode: str = "f32") -> "ArcticModel":
+        """A .tenzor file converted from safetensors (tenzor_format.zig:441-485), memory-mapped."""
+        h = C.c_void_p()
+        L.check(L.lib().tz_arctic_load_tenzor(ctx.handle, path.encode(), MODES[mode], C.byref(h)))
         return cls(ctx, h, mode)
 
     def close(self):

@@ -49,6 +49,16 @@ class LeNet:
         self.ctx, self.handle, self.variant = ctx, h, variant
         ctx._adopt(self)
 
+    @classmethod
+    def from_tenzor(cls, ctx: Context, path: str, variant: int = LENET_PAD2) -> "LeNet":
+        """A LeNet training checkpoint in .tenzor form (main.zig:502-511, runEval 638-667)."""
+        h = C.c_void_p()
+        L.check(L.lib().tz_lenet_load_tenzor(ctx.handle, path.encode(), variant, C.byref(h)))
+        self = cls.__new__(cls)
+        self.ctx, self.handle, self.variant = ctx, h, variant
+        ctx._adopt(self)
+        return self
+
     def close(self):
         if self.handle:
             L.lib().tz_lenet_free(self.handle)
