@@ -98,8 +98,10 @@ typedef struct {
 } tz_arctic_weights;
 
 /* Copies the host weights to the device in the layout the kernels want (QKV concatenated,
- * f16 or int8 operands, f32 scales).  `mode` must agree with the weights: TZ_QUANT_F32 needs
- * f32 Linear weights; the int8 modes need q8 Linear weights (embedding tables may be either).
+ * f16 or int8 operands, f32 scales).  TZ_QUANT_F32 needs f32 Linear weights.  The int8 modes take
+ * q8 Linear weights (embedding tables may be either), or an all-f32 checkpoint, which is then
+ * quantised on the device during the load exactly as quantize_arctic_xs.zig:22-115 would (every
+ * Linear weight and the word / position tables; the 768-element type table stays f32).
  * Replaces ModelWeights.fromSafeTensors, arctic.zig:113-166 / getMatWeightAlloc 258-287. */
 int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_t* out);
 /* Same, reading a safetensors checkpoint (f32, or I8 + '<name>.scale' F16 as written by

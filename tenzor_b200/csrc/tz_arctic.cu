@@ -343,6 +343,9 @@ struct tz_model_s {
     tz_ctx_t ctx = nullptr;
     int device = 0;
     int mode = TZ_QUANT_F32;
+    // int8 mode from an f32 checkpoint: the weights quantize_arctic_xs.zig would quantise are
+    // quantised on the device during the load (GPU row quantiser, same rounding)
+    bool quantize_on_load = false;
     std::vector<void*> allocs;  // every device allocation owned by the model
     EmbTables emb{};
     float *emb_g = nullptr, *emb_b = nullptr;
@@ -418,6 +421,18 @@ int upload_f32(tz_model_s* m, const float* src, size_t n, float** dst, const cha
     return upload_raw(m, src, n * sizeof(float), reinterpret_cast<void**>(dst));
 }
 
+// f32 host rows -> int8 rows + f16 scale bits on the device (quantize_arctic_xs.zig:94-115 rules,
+// through the row quantiser of tz_quantize_weight_rows).
+int quantize_upload(tz_model_s* m, const float* src, int64_t rows, int cols, int8_t* dq, uint16_t* ds) {
+    void* tmp = nullptr;
+    TZ_CUDA(cudaMalloc(&tmp, sizeof(float) * rows * cols));
+    int rc = h2d(m, tmp, src, sizeof(float) * rows * cols);
+    if (!rc) rc = tz_quantize_weight_rows(m->ctx, static_cast<const float*>(tmp), dq, ds, rows, cols, m->ctx->stream);
+    cudaStreamSynchronize(m->ctx->stream);
+    cudaFree(tmp);
+    return rc;
+}
+
 // A Linear weight [rows, cols] into the device operand format of the mode, at row offset `row0` of
 // a (possibly concatenated) destination with `total_rows` rows.
 int upload_linear(tz_model_s* m, const tz_mat_weight& w, int rows, int cols, void* dst, int row0, float* scale_dst,
@@ -435,13 +450,15 @@ int upload_linear(tz_model_s* m, const tz_mat_weight& w, int rows, int cols, voi
         cudaFree(tmp);
         return rc;
     }
-    TZ_CHECK(w.q8 && w.scale_f16, TZ_EINVAL, "%s: int8 modes need int8 weights with a half scale", what);
+    const bool qload = m->quantize_on_load && !w.q8 && w.f32;
+    TZ_CHECK(qload || (w.q8 && w.scale_f16), TZ_EINVAL, "%s: int8 modes need int8 weights with a half scale", what);
     void* tq = nullptr;
     void* ts = nullptr;
     TZ_CUDA(cudaMalloc(&tq, static_cast<size_t>(rows) * cols));
     TZ_CUDA(cudaMalloc(&ts, sizeof(uint16_t) * rows));
-    int rc = h2d(m, tq, w.q8, static_cast<size_t>(rows) * cols);
-    if (!rc) rc = h2d(m, ts, w.scale_f16, sizeof(uint16_t) * rows);
+    int rc = qload ? quantize_upload(m, w.f32, rows, cols, static_cast<int8_t*>(tq), static_cast<uint16_t*>(ts))
+                   : h2d(m, tq, w.q8, static_cast<size_t>(rows) * cols);
+    if (!rc && !qload) rc = h2d(m, ts, w.scale_f16, sizeof(uint16_t) * rows);
     if (!rc)
         rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), scale_dst + row0, rows, s);
     if (!rc) {
@@ -463,22 +480,26 @@ int upload_table(tz_model_s* m, const tz_mat_weight& w, int rows, const float** 
     *f = nullptr;
     *q = nullptr;
     *s = nullptr;
-    if (w.f32) {
+    // shouldQuantize (quantize_arctic_xs.zig:22-40): 2-D, >= 4096 elements (word and position tables)
+    const bool qload = m->quantize_on_load && w.f32 && !w.q8 && static_cast<int64_t>(rows) * kH >= 4096;
+    if (w.f32 && !qload) {
         float* d = nullptr;
         int rc = upload_f32(m, w.f32, static_cast<size_t>(rows) * kH, &d, what);
         *f = d;
         return rc;
     }
-    TZ_CHECK(w.q8 && w.scale_f16, TZ_EMISSING, "missing weight: %s", what);
+    TZ_CHECK(qload || (w.q8 && w.scale_f16), TZ_EMISSING, "missing weight: %s", what);
     void* dq = nullptr;
-    int rc = upload_raw(m, w.q8, static_cast<size_t>(rows) * kH, &dq);
+    int rc = dalloc(m, m->allocs, static_cast<size_t>(rows) * kH, &dq);
     if (rc) return rc;
     void* ts = nullptr;
     float* ds = nullptr;
     rc = dalloc(m, m->allocs, sizeof(float) * rows, reinterpret_cast<void**>(&ds));
     if (rc) return rc;
     TZ_CUDA(cudaMalloc(&ts, sizeof(uint16_t) * rows));
-    rc = h2d(m, ts, w.scale_f16, sizeof(uint16_t) * rows);
+    rc = qload ? quantize_upload(m, w.f32, rows, kH, static_cast<int8_t*>(dq), static_cast<uint16_t*>(ts))
+               : h2d(m, dq, w.q8, static_cast<size_t>(rows) * kH);
+    if (!rc && !qload) rc = h2d(m, ts, w.scale_f16, sizeof(uint16_t) * rows);
     if (!rc) rc = launch_f16bits_to_f32(m->ctx, static_cast<uint16_t*>(ts), ds, rows, m->ctx->stream);
     cudaStreamSynchronize(m->ctx->stream);
     cudaFree(ts);
@@ -827,6 +848,7 @@ int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_
     m->ctx = ctx;
     m->device = ctx->device;
     m->mode = mode;
+    m->quantize_on_load = mode != TZ_QUANT_F32 && w->layers[0].query.f32 && !w->layers[0].query.q8;
     int rc = TZ_OK;
     auto fail_cleanup = [&](int code) {
         for (void* p : m->allocs) cudaFree(p);

@@ -220,6 +220,19 @@ def test_safetensors_loader(ctx, weights, qweights, models, c1):
             m8.close()
 
 
+@pytest.mark.parametrize("mode", ["w8a8", "w8a32"])
+def test_quantize_on_load_matches_quantized_checkpoint(ctx, weights, models, c1, mode):
+    """An f32 checkpoint loaded in an int8 mode is quantised on the device with the reference
+    quantiser's rules: the model is the one the offline-quantised checkpoint gives, bit for bit."""
+    from tenzor_b200.arctic import ArcticModel
+    ids, lens, packed, cu = c1
+    m = ArcticModel.from_checkpoint(ctx, weights, mode)
+    try:
+        assert np.array_equal(m.forward_packed(packed, cu), models[mode].forward_packed(packed, cu))
+    finally:
+        m.close()
+
+
 def test_gpu_quantizer_matches_oracle_checkpoint(ctx, weights, qweights):
     from tenzor_b200.quantize import quantize_checkpoint
     g = quantize_checkpoint(ctx, weights)
