@@ -346,6 +346,9 @@ struct tz_model_s {
     // int8 mode from an f32 checkpoint: the weights quantize_arctic_xs.zig would quantise are
     // quantised on the device during the load (GPU row quantiser, same rounding)
     bool quantize_on_load = false;
+    // load-time pinned staging: two chunks, so the host fills one while the other's DMA runs
+    void* stage[2] = {nullptr, nullptr};
+    cudaEvent_t stage_ev[2] = {nullptr, nullptr};
     std::vector<void*> allocs;  // every device allocation owned by the model
     EmbTables emb{};
     float *emb_g = nullptr, *emb_b = nullptr;
@@ -404,10 +407,42 @@ int dalloc(tz_model_s* m, std::vector<void*>& list, size_t bytes, void** p) {
 // Host -> device copy ordered on the context stream and complete on return.  (A plain cudaMemcpy
 // from pageable memory may return before its DMA lands, and the conversion kernels that consume
 // the copies run on the context's non-blocking stream, so the copy must be stream-ordered.)
+// Copies of 4 MiB and more go through the model's two pinned staging chunks (memcpy into chunk k
+// while chunk 1 - k is on the wire): the source may be pageable or a file mapping.
+constexpr size_t kStageBytes = 8u << 20;
 int h2d(tz_model_s* m, void* dst, const void* src, size_t bytes) {
-    TZ_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, m->ctx->stream));
-    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    cudaStream_t s = m->ctx->stream;
+    if (bytes < (4u << 20)) {
+        TZ_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s));
+        TZ_CUDA(cudaStreamSynchronize(s));
+        return TZ_OK;
+    }
+    for (int k = 0; k < 2; ++k)
+        if (!m->stage[k]) {
+            TZ_CUDA(cudaMallocHost(&m->stage[k], kStageBytes));
+            TZ_CUDA(cudaEventCreateWithFlags(&m->stage_ev[k], cudaEventDisableTiming));
+        }
+    const char* p = static_cast<const char*>(src);
+    char* d = static_cast<char*>(dst);
+    int k = 0;
+    for (size_t off = 0; off < bytes; off += kStageBytes, k ^= 1) {
+        const size_t n = bytes - off < kStageBytes ? bytes - off : kStageBytes;
+        TZ_CUDA(cudaEventSynchronize(m->stage_ev[k]));  // chunk k's previous copy has left the buffer
+        std::memcpy(m->stage[k], p + off, n);
+        TZ_CUDA(cudaMemcpyAsync(d + off, m->stage[k], n, cudaMemcpyHostToDevice, s));
+        TZ_CUDA(cudaEventRecord(m->stage_ev[k], s));
+    }
+    TZ_CUDA(cudaStreamSynchronize(s));
     return TZ_OK;
+}
+
+void release_staging(tz_model_s* m) {
+    for (int k = 0; k < 2; ++k) {
+        if (m->stage[k]) cudaFreeHost(m->stage[k]);
+        if (m->stage_ev[k]) cudaEventDestroy(m->stage_ev[k]);
+        m->stage[k] = nullptr;
+        m->stage_ev[k] = nullptr;
+    }
 }
 
 int upload_raw(tz_model_s* m, const void* src, size_t bytes, void** dst) {
@@ -851,6 +886,7 @@ int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_
     m->quantize_on_load = mode != TZ_QUANT_F32 && w->layers[0].query.f32 && !w->layers[0].query.q8;
     int rc = TZ_OK;
     auto fail_cleanup = [&](int code) {
+        release_staging(m.get());
         for (void* p : m->allocs) cudaFree(p);
         m->allocs.clear();
         return code;
@@ -911,6 +947,7 @@ int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_
     }
 #undef TRY
     TZ_CUDA(cudaDeviceSynchronize());
+    release_staging(m.get());
     *out = m.release();
     return TZ_OK;
 }
