@@ -389,6 +389,7 @@ struct tz_model_s {
     cudaGraphExec_t graph = nullptr;
     int g_batch = -1, g_maxlen = -1;
     int64_t g_tokens = -1;
+    const void* g_io[3] = {nullptr, nullptr, nullptr};  // pinned ids / cu / out the graph copies (or none)
     bool use_graph = true;
     // graph cache for the device-pointer forward (keyed by buffers, shape and stream)
     cudaGraphExec_t dgraph = nullptr;
@@ -548,6 +549,7 @@ void drop_graphs(tz_model_s* m) {
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
     }
+    m->g_io[0] = m->g_io[1] = m->g_io[2] = nullptr;
     if (m->dgraph) {
         cudaGraphExecDestroy(m->dgraph);
         m->dgraph = nullptr;
@@ -831,14 +833,32 @@ int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, f
     }
     if (!cu_pin) memcpy(m->h_cu, cu, sizeof(int) * (B + 1));
     const bool graph_ok = m->use_graph && !m->keep_stages;
-    if (graph_ok && !(m->graph && m->g_batch == B && m->g_tokens == T && m->g_maxlen == maxL)) {
+    // With every host buffer pinned, the copies are captured with the forward: one graph launch per
+    // call (the graph is keyed by the buffers as well as the shape).
+    const bool io_graph = graph_ok && ids_pin && cu_pin && out_pin;
+    const void* io[3] = {io_graph ? static_cast<const void*>(ids) : nullptr, io_graph ? static_cast<const void*>(cu) : nullptr,
+                         io_graph ? static_cast<const void*>(out) : nullptr};
+    auto h2d_inputs = [&]() -> int {
+        TZ_CUDA(cudaMemcpyAsync(m->d_ids, ids_pin ? ids : m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
+        TZ_CUDA(cudaMemcpyAsync(m->d_cu, cu_pin ? cu : m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s));
+        return TZ_OK;
+    };
+    auto d2h_outputs = [&]() -> int {
+        TZ_CUDA(cudaMemcpyAsync(out_pin ? out : m->h_out, m->out, sizeof(float) * B * kH, cudaMemcpyDeviceToHost, s));
+        TZ_CUDA(cudaMemcpyAsync(m->h_status, m->ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, s));
+        return TZ_OK;
+    };
+    if (graph_ok && !(m->graph && m->g_batch == B && m->g_tokens == T && m->g_maxlen == maxL && m->g_io[0] == io[0] &&
+                      m->g_io[1] == io[1] && m->g_io[2] == io[2])) {
         if (m->graph) {
             cudaGraphExecDestroy(m->graph);
             m->graph = nullptr;
         }
         cudaGraph_t gr = nullptr;
         TZ_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-        const int crc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
+        int crc = io_graph ? h2d_inputs() : TZ_OK;
+        if (!crc) crc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
+        if (!crc && io_graph) crc = d2h_outputs();
         const cudaError_t ee = cudaStreamEndCapture(s, &gr);
         if (crc) {
             if (gr) cudaGraphDestroy(gr);
@@ -851,16 +871,15 @@ int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, f
         m->g_batch = B;
         m->g_tokens = T;
         m->g_maxlen = maxL;
+        for (int i = 0; i < 3; ++i) m->g_io[i] = io[i];
     }
-    TZ_CUDA(cudaMemcpyAsync(m->d_ids, ids_pin ? ids : m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
-    TZ_CUDA(cudaMemcpyAsync(m->d_cu, cu_pin ? cu : m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s));
+    if (!io_graph && (rc = h2d_inputs())) return rc;
     if (graph_ok) {
         TZ_CUDA(cudaGraphLaunch(m->graph, s));
     } else if ((rc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s))) {
         return rc;
     }
-    TZ_CUDA(cudaMemcpyAsync(out_pin ? out : m->h_out, m->out, sizeof(float) * B * kH, cudaMemcpyDeviceToHost, s));
-    TZ_CUDA(cudaMemcpyAsync(m->h_status, m->ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (!io_graph && (rc = d2h_outputs())) return rc;
     TZ_CUDA(cudaStreamSynchronize(s));
     if (*m->h_status) {
         if ((rc = read_status(m->ctx, s))) return rc;

@@ -220,6 +220,39 @@ def test_safetensors_loader(ctx, weights, qweights, models, c1):
             m8.close()
 
 
+def test_pinned_host_buffers_graph_with_copies(models, c1):
+    """With pinned ids / cu / out the host call captures the copies into its graph, keyed by the
+    buffers: new contents in the same buffers, other buffers, and pageable buffers all agree."""
+    import torch
+    ids, lens, packed, cu = c1
+    m = models["w8a8"]
+
+    def pinned(a):
+        t = torch.empty(a.shape, dtype={np.uint32: torch.int32, np.int32: torch.int32, np.float32: torch.float32}[a.dtype.type],
+                        pin_memory=True)
+        v = t.numpy().view(a.dtype)
+        v[:] = a
+        return t, v
+    ref = m.forward_packed(packed, cu)
+    ti, hi = pinned(packed.astype(np.uint32))
+    tc, hc = pinned(cu.astype(np.int32))
+    to, ho = pinned(np.zeros((len(lens), 384), np.float32))
+    for _ in range(2):
+        m.forward_packed(hi, hc, out=ho)
+        assert np.array_equal(ho, ref)
+    rng = np.random.default_rng(5)
+    other = rng.integers(0, 30522, packed.shape).astype(np.uint32)
+    hi[:] = other  # same buffers, new contents: the graph's copies read them
+    m.forward_packed(hi, hc, out=ho)
+    assert np.array_equal(ho, m.forward_packed(other, cu))
+    ti2, hi2 = pinned(packed.astype(np.uint32))  # another pinned buffer: a new graph
+    m.forward_packed(hi2, hc, out=ho)
+    assert np.array_equal(ho, ref)
+    hi[0] = 40000  # an id past the vocabulary is still refused
+    with pytest.raises(Exception):
+        m.forward_packed(hi, hc, out=ho)
+
+
 @pytest.mark.parametrize("mode", ["w8a8", "w8a32"])
 def test_quantize_on_load_matches_quantized_checkpoint(ctx, weights, models, c1, mode):
     """An f32 checkpoint loaded in an int8 mode is quantised on the device with the reference
