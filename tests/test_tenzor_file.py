@@ -101,6 +101,17 @@ def test_corrupt_files_are_rejected():
             TF.TenzorFile(_tmp(d, "absent.tenzor"))
 
 
+def test_empty_file_and_empty_tensor():
+    with tempfile.TemporaryDirectory() as d:
+        p = _tmp(d)
+        TF.write(p, {}, "")
+        with TF.TenzorFile(p) as f:
+            assert len(f) == 0 and f.metadata() == {}
+        TF.write(p, {"z": np.zeros((0, 4), np.float32), "a": np.ones(2, np.float32)})
+        with TF.TenzorFile(p) as f:
+            assert f.get("z").shape == (0, 4) and np.array_equal(f.get("a"), np.ones(2, np.float32))
+
+
 def test_repeated_hash_first_entry_wins():
     # getTensorByHash's linear scan returns the first matching entry
     with tempfile.TemporaryDirectory() as d:
