@@ -170,6 +170,24 @@ def test_full_size_c2_properties(models):
     assert np.abs(y2 - y[perm]).max() < 1e-5
 
 
+def test_full_size_c4_properties(oracle, weights, models):
+    """configs[3] at full size (B=8192, S=512, lengths 32..512, ~2.2M packed tokens): unit norms and
+    permutation equivariance on the W8A8 model, and three sequences of the f32 model's full batch
+    against the oracle run on those sequences alone."""
+    ids, lens = S.token_batch(8192, 512, 32, 512, seed=31)
+    packed, cu = S.pack(ids, lens)
+    m = models["w8a8"]
+    y = m.forward_packed(packed, cu)
+    assert np.isfinite(y).all() and np.abs(np.linalg.norm(y, axis=1) - 1).max() < 1e-5
+    perm = np.random.default_rng(1).permutation(len(lens))
+    p2, c2 = S.pack(ids[perm], lens[perm])
+    assert np.abs(m.forward_packed(p2, c2) - y[perm]).max() < 1e-5
+    yf = models["f32"].forward_packed(packed, cu)
+    pick = [int(np.argmax(lens)), int(np.argmin(lens)), 4097]
+    sp, sc = S.pack(ids[pick], lens[pick])
+    _close(yf[pick], oracle.OracleModel(weights).forward(sp, sc, oracle.MODE_F32))
+
+
 def test_errors(ctx, weights, qweights, models):
     from tenzor_b200 import TenzorError
     from tenzor_b200.arctic import ArcticModel
