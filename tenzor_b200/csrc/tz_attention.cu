@@ -6,7 +6,10 @@
 // packed back to back (cu_seqlens) and each CTA only visits the keys of its own sequence, which is
 // the masked-batch form with key mask = (position < length).
 //
-// CTA = (64-query block, head, sequence); 4 warps x 16 query rows.  K_h and V_h for every key of
+// CTA = (64-query block, head, sequence); 4 warps x 16 query rows.  The grid is (head, sequence,
+// query block) with the last query block first: the block scheduler hands out the CTAs of long
+// sequences' later queries (the ones that see every key, or exit at once for short sequences) before
+// the first blocks of every sequence, so the lighter CTAs fill the tail of the wave.  K_h and V_h for every key of
 // the sequence and the CTA's Q rows arrive in shared memory as 64- and 16-row TMA boxes (32 f16 columns,
 // 64-byte swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3), so ldmatrix is conflict-free),
 // issued by one thread and completed on one mbarrier; V rows past the sequence's end are zeroed.  S = Q K^T and
@@ -127,15 +130,16 @@ __global__ void __launch_bounds__(128)
     }
     // cu_seqlens is a forward input, written before the forward's first kernel: read it while the
     // previous kernel (QKV) may still run; Q/K/V are read only after griddepcontrol.wait.
-    const int b = blockIdx.z;
-    const int h = blockIdx.y;
+    const int b = blockIdx.y;
+    const int h = blockIdx.x;
+    const int qb = static_cast<int>(gridDim.z - 1 - blockIdx.z);  // the last query block is dispatched first
     const int seq0 = cu_seqlens[b];
     const int L = cu_seqlens[b + 1] - seq0;
     __syncthreads();
     tzp::pdl_wait();
-    const int q0 = blockIdx.x * kQTile;
+    const int q0 = qb * kQTile;
     if (L > lpad || L < 0) {  // the caller's max_len was too small: refuse rather than overrun shared memory
-        if (tid == 0 && blockIdx.x == 0) atomicOr(status, TZ_DEV_BOUNDS);
+        if (tid == 0 && qb == 0) atomicOr(status, TZ_DEV_BOUNDS);
         return;
     }
     if (q0 >= L) return;  // uniform over the CTA
@@ -262,7 +266,7 @@ int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const 
     rc = encode_tmap_2d_swz(&tm64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens),
                             kQKV * 2, kHd, 64, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
-    dim3 grid((max_len + kQTile - 1) / kQTile, kHeads, batch);
+    dim3 grid(kHeads, batch, (max_len + kQTile - 1) / kQTile);
     return launch_kernel(attention_kernel, grid, dim3(128), smem, s, pdl, tm, tm64, cu_seqlens, lpad, static_cast<__half*>(out),
                          row_absmax, ctx->d_status);
 }
