@@ -349,7 +349,9 @@ int launch_lenet(tz_lenet_s* m, const float* d_images, int64_t n, float* d_out, 
     }
     const int sms = m->ctx->sm_count;
     const int64_t groups = (n + S::G - 1) / S::G;
-    const int g1 = static_cast<int>(groups < 4LL * sms ? groups : 4LL * sms);
+    // 24 CTAs per SM (3 resident): short per-CTA runs of groups balance the end of the grid, and
+    // most CTAs stage the conv weights once for several groups (measured best of 3 .. 12k per SM)
+    const int g1 = static_cast<int>(groups < 24LL * sms ? groups : 24LL * sms);
     lenet_conv_kernel<PAD><<<g1, kThreads, conv_smem, s>>>(d_images, n, m->c1w, m->c1b, m->c2w, m->c2b, feat);
     TZ_CUDA(cudaGetLastError());
     for (int64_t r = 0; r < n; r += INT32_MAX / 2) {  // the GEMM takes int M
