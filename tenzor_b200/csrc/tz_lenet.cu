@@ -375,7 +375,8 @@ int launch_lenet(tz_lenet_s* m, const float* d_images, int64_t n, float* d_out, 
         if (rc) return rc;
     }
     const int64_t tiles = (n + kTile - 1) / kTile;
-    const int g2 = static_cast<int>(tiles < 2LL * sms ? tiles : 2LL * sms);
+    // 6 CTAs per SM (3 resident): fills every slot, shorter per-CTA runs of tiles (swept 2x .. all)
+    const int g2 = static_cast<int>(tiles < 6LL * sms ? tiles : 6LL * sms);
     lenet_fc_tail_kernel<PAD != 0><<<g2, kThreads, fc_smem, s>>>(h1, n, m->f2w, m->f2b, m->f3w, m->f3b, d_out);
     TZ_CUDA(cudaGetLastError());
     return TZ_OK;
