@@ -3,7 +3,7 @@
  * encoder hot path of tenzor.
  *
  * The reference (mattneel/tenzor) is Zig; its host code binds this header with `extern fn`
- * (see INTEGRATION.md).  Every entry point names the reference function it replaces
+ * declarations of the same names and types.  Every entry point names the reference function it replaces
  * (path:line inside the reference project).  Conventions, mirroring the reference kernels:
  *   - caller-owned, contiguous, row-major buffers plus explicit dimensions;
  *   - Linear weights in PyTorch layout [out, in];
@@ -132,15 +132,28 @@ int tz_arctic_forward_device(tz_model_t model, const uint32_t* d_ids_packed,
                              const int32_t* d_cu_seqlens, int batch, int64_t total_tokens,
                              int max_len, float* d_out, tz_stream_t stream);
 /* Debug/parity hook: copies the device hidden state [T, 384] after stage `stage` (0 = after the
- * embeddings, l+1 = after layer l) of the LAST forward into host `out`.  Capture is switched on
- * by a first call (which returns TZ_EINVAL) and applies from the next forward. */
+ * embeddings, l+1 = after layer l, 7 = layer 0's state after its attention block, i.e. the FFN1
+ * input) of the LAST forward into host `out`.  Capture is switched on by a first call (which returns
+ * TZ_EINVAL) and applies from the next forward. */
 int tz_arctic_debug_hidden(tz_model_t model, int stage, float* out, int64_t total_tokens);
-/* Debug/parity hook (W8A8): copies an int8 GEMM operand of layer 0 captured in the LAST forward
- * (which: 0 = QKV input, 1 = attention-output-projection input, 2 = FFN1 input, 3 = FFN2 input;
- * int8 [T, K] with K = 384, or 1536 for which = 3, plus its per-row f32 scale [T]).  Capture is
- * switched on by a first call (which returns TZ_EINVAL) and applies from the next forward. */
+/* Switches the capture of the debug hooks on (from the next forward) or off (frees the capture
+ * buffers; the forward returns to its captured CUDA graph). */
+int tz_arctic_debug_capture(tz_model_t model, int on);
+/* Debug/parity hooks (W8A8), written by the forward's own GEMM kernels for layer 0 during the LAST
+ * forward (which: 0 = QKV, 1 = attention-output projection, 2 = FFN1, 3 = FFN2).  Capture is
+ * switched on by a first call to any of them (which returns TZ_EINVAL) and applies from the next
+ * forward; it adds stores to the same kernels and is meant for parity tests only.
+ *   tz_arctic_debug_operand:    the int8 A operand [T, K] as the GEMM consumed it (K = 384, or 1536
+ *                               for which = 3) and its per-token f32 scale [T]; for which = 1 and 3
+ *                               these are the rows the gemm_ln kernel quantised into its MMA stages;
+ *   tz_arctic_debug_accum:      the raw int32 accumulators [T, N] the epilogue read from TMEM
+ *                               (N = 1152, 384, 1536, 384);
+ *   tz_arctic_debug_gemm_input: (which = 1, 3) the f16 activation [T, K] (IEEE half bits) that the
+ *                               kernel quantised per token. */
 int tz_arctic_debug_operand(tz_model_t model, int which, int8_t* q_out, float* scale_out,
                             int64_t total_tokens);
+int tz_arctic_debug_accum(tz_model_t model, int which, int32_t* acc_out, int64_t total_tokens);
+int tz_arctic_debug_gemm_input(tz_model_t model, int which, uint16_t* x_out, int64_t total_tokens);
 
 /* Kernel timing of the forward: when enabled (enable = number of forwards to keep, 0 = off), CUDA
  * events are recorded on the launching stream between consecutive launches (inside a captured
@@ -216,6 +229,9 @@ int tz_linear_w8a8(tz_ctx_t ctx, const float* x, const int8_t* wq, const uint16_
  * m*k + 4*m + 4*n bytes (each part rounded up to 256) <= 8 MiB and returns TZ_EINVAL otherwise.
  * The first call on a device looks the array's address up (cudaGetSymbolAddress); make that first
  * call before any stream capture.  All calls share the array: calls that overlap on the GPU race.
+ * The context's device must be the calling thread's current device (TZ_EINVAL otherwise); the
+ * array's address is kept per device for the life of the process, which assumes the device's
+ * primary context is not reset (cudaDeviceReset) while the library is loaded.
  * Same arguments, result and stream semantics as tz_linear_w8a8. */
 int tz_linear_w8a8_noalloc(tz_ctx_t ctx, const float* x, const int8_t* wq, const uint16_t* scale_f16,
                            const float* bias, float* y, int m, int k, int n, tz_stream_t stream);

@@ -109,12 +109,13 @@ static void* dlopen_with_siblings_global(const char* path, int depth) {
     if (n == 0 || n >= sizeof dep) return NULL;
     memcpy(dep, err, n);
     dep[n] = 0;
-    char dir[512];
-    snprintf(dir, sizeof dir, "%s", path);
+    char dir[800];
+    if (strlen(path) >= sizeof dir) return NULL;
+    memcpy(dir, path, strlen(path) + 1);
     char* slash = strrchr(dir, '/');
     if (!slash) return NULL;
     *slash = 0;
-    char full[800];
+    char full[1200];
     snprintf(full, sizeof full, "%s/%s", dir, dep);
     if (!dlopen_with_siblings_global(full, depth + 1)) return NULL;
     return dlopen_with_siblings_global(path, depth + 1);
@@ -141,12 +142,13 @@ static void* dlopen_with_siblings(const char* path, int depth) {
     if (n == 0 || n >= sizeof dep) return NULL;
     memcpy(dep, err, n);
     dep[n] = 0;
-    char dir[512];
-    snprintf(dir, sizeof dir, "%s", path);
+    char dir[800];
+    if (strlen(path) >= sizeof dir) return NULL;
+    memcpy(dir, path, strlen(path) + 1);
     char* slash = strrchr(dir, '/');
     if (!slash) return NULL;
     *slash = 0;
-    char full[800];
+    char full[1200];
     snprintf(full, sizeof full, "%s/%s", dir, dep);
     if (!dlopen_with_siblings_global(full, depth + 1)) return NULL;
     return dlopen_with_siblings(path, depth + 1);
@@ -157,19 +159,31 @@ static void blas_init(void) {
 #pragma omp critical(tzo_blas)
     {
         if (!g_blas_tried) {
-            const char* path = getenv("TENZOR_BLAS_LIB");
-            if (path && *path) {
+            /* TENZOR_BLAS_LIB first (blas.zig:199-204), else the library names of the reference's
+             * Linux candidate list (blas.zig:206-220) through the dynamic loader's search path. */
+            static const char* const kCandidates[] = {
+                "libopenblas.so.0", "libopenblas.so", "libopenblas64_.so.0", "libopenblas64_.so",
+                "libopenblas64.so.0", "libopenblas64.so", "libopenblasp.so.0", "libopenblasp.so",
+                "libcblas.so.3", "libcblas.so", "libblas.so.3", "libblas.so", "libmkl_rt.so"};
+            const char* env = getenv("TENZOR_BLAS_LIB");
+            const int n_cand = (int)(sizeof kCandidates / sizeof kCandidates[0]);
+            int tried_env = 0;
+            for (int i = (env && *env) ? -1 : 0; i < n_cand && !g_sgemm; i++) {
+                const char* path = i < 0 ? env : kCandidates[i];
                 void* h = dlopen_with_siblings(path, 0);
-                if (h) {
-                    g_sgemm = (cblas_sgemm_fn)dlsym(h, "cblas_sgemm");
-                    void (*set_threads)(int) = (void (*)(int))dlsym(h, "openblas_set_num_threads");
-                    if (set_threads) set_threads(1); /* parallelism is per sequence */
-                    snprintf(g_blas_status, sizeof g_blas_status, "%s%s", path,
-                             g_sgemm ? "" : " (no cblas_sgemm)");
-                } else {
-                    snprintf(g_blas_status, sizeof g_blas_status, "dlopen failed: %s", path);
+                if (i < 0) tried_env = 1;
+                if (!h) {
+                    if (i < 0) snprintf(g_blas_status, sizeof g_blas_status, "dlopen failed: %s", path);
+                    continue;
                 }
+                g_sgemm = (cblas_sgemm_fn)dlsym(h, "cblas_sgemm");
+                if (!g_sgemm) continue;
+                void (*set_threads)(int) = (void (*)(int))dlsym(h, "openblas_set_num_threads");
+                if (set_threads) set_threads(1); /* parallelism is per sequence */
+                snprintf(g_blas_status, sizeof g_blas_status, "%s", path);
             }
+            if (!g_sgemm && !tried_env)
+                snprintf(g_blas_status, sizeof g_blas_status, "no CBLAS found (restated loops)");
             __atomic_store_n(&g_blas_tried, 1, __ATOMIC_RELEASE);
         }
     }

@@ -222,14 +222,30 @@ class ArcticModel:
         L.check(L.lib().tz_arctic_debug_hidden(self.handle, stage, out.ctypes.data, total_tokens))
         return out
 
-    def enable_capture(self):
-        """Switches on stage / operand capture from the next forward."""
-        dummy = np.empty(1, np.float32)
-        L.lib().tz_arctic_debug_hidden(self.handle, 0, dummy.ctypes.data, -1)
+    def enable_capture(self, on: bool = True):
+        """Switches stage / operand capture on from the next forward (or off, freeing its buffers)."""
+        L.check(L.lib().tz_arctic_debug_capture(self.handle, int(bool(on))))
+
+    # K and N of layer 0's GEMMs: 0 QKV, 1 attention output, 2 FFN1, 3 FFN2
+    GEMM_K = (384, 384, 384, 1536)
+    GEMM_N = (1152, 384, 1536, 384)
 
     def debug_operand(self, which: int, total_tokens: int):
-        K = 1536 if which == 3 else 384
-        q = np.empty((total_tokens, K), np.int8)
+        """W8A8: layer 0's int8 A operand [T, K] and per-token scales [T] of GEMM `which`, as the
+        forward's own kernel consumed them (for 1 and 3: quantised inside the gemm_ln mainloop)."""
+        q = np.empty((total_tokens, self.GEMM_K[which]), np.int8)
         s = np.empty(total_tokens, np.float32)
         L.check(L.lib().tz_arctic_debug_operand(self.handle, which, q.ctypes.data, s.ctypes.data, total_tokens))
         return q, s
+
+    def debug_accum(self, which: int, total_tokens: int) -> np.ndarray:
+        """W8A8: the raw int32 accumulators [T, N] of layer 0's GEMM `which`, read by its epilogue."""
+        acc = np.empty((total_tokens, self.GEMM_N[which]), np.int32)
+        L.check(L.lib().tz_arctic_debug_accum(self.handle, which, acc.ctypes.data, total_tokens))
+        return acc
+
+    def debug_gemm_input(self, which: int, total_tokens: int) -> np.ndarray:
+        """W8A8, which = 1 or 3: the f16 activation [T, K] that gemm_ln quantised per token (as f32)."""
+        x = np.empty((total_tokens, self.GEMM_K[which]), np.uint16)
+        L.check(L.lib().tz_arctic_debug_gemm_input(self.handle, which, x.ctypes.data, total_tokens))
+        return x.view(np.float16).astype(np.float32)

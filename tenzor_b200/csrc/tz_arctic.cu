@@ -1,6 +1,5 @@
-// tz_arctic.cu -- Arctic-embed-xs forward on sm_100a: model kernels (embedding + LayerNorm, per-token
-// requantisation of f16 activations for the W8A8 path, CLS pooling + L2 norm) and the host
-// orchestration behind tz_arctic_*.  Per layer: QKV GEMM (tz_gemm.cu) -> attention
+// tz_arctic.cu -- Arctic-embed-xs forward on sm_100a: model kernels (embedding + LayerNorm, CLS
+// pooling + L2 norm, long-document pooling) and the host orchestration behind tz_arctic_*.  Per layer: QKV GEMM (tz_gemm.cu) -> attention
 // (tz_attention.cu) -> output projection + residual + LayerNorm (tz_gemm_ln.cu) -> FFN1 + GELU
 // (tz_gemm.cu) -> FFN2 + residual + LayerNorm (tz_gemm_ln.cu).  In W8A8 the f16 attention and GELU
 // outputs carry their row |max| and are quantised per token inside the consuming gemm_ln kernel.
@@ -223,38 +222,6 @@ __global__ void __launch_bounds__(256, 4)
         *reinterpret_cast<float4*>(dst + q * 128 + lane * 4) = *reinterpret_cast<const float4*>(tile + lane * kH + ((q ^ (lane & 7)) << 2));
 }
 
-// W8A8 per-token requantisation of an f16 activation X [rows, cols] whose row |max| (float bits) was
-// accumulated by its producer (GEMM epilogue or attention): s = max/127 (1 if 0),
-// q = clamp(round(x * (1/s))); the row max is reset to 0 for the next producer.  Warp per row.
-__global__ void requant_rows_kernel(const __half* __restrict__ x, int cols, unsigned* __restrict__ xmax,
-                                    int8_t* __restrict__ q, float* __restrict__ qs, long long rows, int reset) {
-    tzp::pdl_wait();
-    tzp::pdl_trigger();
-    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float m = __uint_as_float(xmax[row]);
-    const float sc = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
-    const float inv = __fdiv_rn(1.0f, sc);
-    const __half* xr = x + row * cols;
-    int8_t* qr = q + row * cols;
-    for (int col = lane * 8; col < cols; col += 256) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(xr + col);
-        const __half* hv = reinterpret_cast<const __half*>(&raw);
-        const uint64_t inv2 = tzp::f2_pack(inv, inv);  // the row's own |max|: the fused gemm_ln arithmetic
-        const uint32_t w0 = __byte_perm(quant2_own_max(__half2float(hv[0]), __half2float(hv[1]), inv2),
-                                        quant2_own_max(__half2float(hv[2]), __half2float(hv[3]), inv2), 0x5410);
-        const uint32_t w1 = __byte_perm(quant2_own_max(__half2float(hv[4]), __half2float(hv[5]), inv2),
-                                        quant2_own_max(__half2float(hv[6]), __half2float(hv[7]), inv2), 0x5410);
-        *reinterpret_cast<uint2*>(qr + col) = make_uint2(w0, w1);
-    }
-    __syncwarp();
-    if (lane == 0) {
-        qs[row] = sc;
-        if (reset) xmax[row] = 0u;
-    }
-}
-
 // CLS pooling + l2Normalize (arctic.zig:851-863, forward 894-897): warp per sequence.
 __global__ void pool_l2_kernel(const float* __restrict__ x, const int* __restrict__ cu, float* __restrict__ out,
                                int batch) {
@@ -319,8 +286,6 @@ __global__ void doc_mean_l2_kernel(const float* __restrict__ emb, const int* __r
     }
 }
 
-inline int rows_grid(long long rows) { return static_cast<int>((rows * 32 + 255) / 256); }
-
 }  // namespace
 }  // namespace tz
 
@@ -359,8 +324,8 @@ struct tz_model_s {
     std::vector<void*> ws;
     uint32_t* d_ids = nullptr;
     int* d_cu = nullptr;
-    float *X = nullptr, *xs = nullptr, *os = nullptr, *hs = nullptr, *out = nullptr;
-    void *XA = nullptr, *QKV = nullptr, *OA = nullptr, *Hh = nullptr, *HQ = nullptr;
+    float *X = nullptr, *xs = nullptr, *out = nullptr;
+    void *XA = nullptr, *QKV = nullptr, *OA = nullptr, *Hh = nullptr;
     unsigned* hmax = nullptr;
     unsigned* omax = nullptr;
     uint32_t* h_ids = nullptr;  // pinned staging (used when the caller's buffers are pageable)
@@ -373,9 +338,16 @@ struct tz_model_s {
     int64_t cap_pad = 0;
     // debug
     bool keep_stages = false;
-    float* d_stages = nullptr;  // [7, cap_tokens, 384] when keep_stages
-    int8_t* d_opq[4] = {nullptr, nullptr, nullptr, nullptr};  // W8A8 layer-0 GEMM operands
+    // [8, cap_tokens, 384] when keep_stages: 0 after the embeddings, l + 1 after layer l, 7 layer 0's
+    // hidden state after its attention block (the FFN1 input)
+    float* d_stages = nullptr;
+    // W8A8 layer-0 GEMM captures, written by the forward's own kernels (which = 0 QKV, 1 O-proj,
+    // 2 FFN1, 3 FFN2): the int8 A operand and its per-token scales as the GEMM consumed them, the
+    // raw int32 accumulators, and (1, 3) the f16 activation the gemm_ln kernel quantised
+    int8_t* d_opq[4] = {nullptr, nullptr, nullptr, nullptr};
     float* d_ops[4] = {nullptr, nullptr, nullptr, nullptr};
+    int32_t* d_acc[4] = {nullptr, nullptr, nullptr, nullptr};
+    __half* d_in16[4] = {nullptr, nullptr, nullptr, nullptr};
     int64_t last_T = 0;
     // kernel-class timing: events around every launch of the forward (recorded in graphs too)
     bool profile = false;
@@ -398,6 +370,10 @@ struct tz_model_s {
 };
 
 namespace {
+
+// K and N of the layer's four GEMMs (0 QKV, 1 attention output, 2 FFN1, 3 FFN2).
+constexpr int gemm_k(int which) { return which == 3 ? kF : kH; }
+constexpr int gemm_n(int which) { return which == 0 ? 3 * kH : (which == 2 ? kF : kH); }
 
 int dalloc(tz_model_s* m, std::vector<void*>& list, size_t bytes, void** p) {
     TZ_CUDA(cudaMalloc(p, bytes ? bytes : 16));
@@ -575,6 +551,8 @@ void free_workspace(tz_model_s* m) {
     for (int i = 0; i < 4; ++i) {
         m->d_opq[i] = nullptr;
         m->d_ops[i] = nullptr;
+        m->d_acc[i] = nullptr;
+        m->d_in16[i] = nullptr;
     }
 }
 
@@ -601,23 +579,19 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
         A(sizeof(unsigned) * T, reinterpret_cast<void**>(&m->hmax));
         A(sizeof(unsigned) * T, reinterpret_cast<void**>(&m->omax));
         A(sizeof(__half) * T * kF, &m->Hh);
-        if (m->keep_stages) {  // int8 copies of the in-kernel-quantised operands, for the parity hook
-            A(T * kH, &m->OA);
-            A(sizeof(float) * T, reinterpret_cast<void**>(&m->os));
-            A(sizeof(float) * T, reinterpret_cast<void**>(&m->hs));
-            A(T * kF, &m->HQ);
-        }
     } else {
         A(sizeof(__half) * T * kH, &m->XA);
         A(sizeof(__half) * T * kH, &m->OA);
         A(sizeof(__half) * T * kF, &m->Hh);
     }
     if (m->keep_stages) {
-        A(sizeof(float) * 7 * xblk_rows(static_cast<long long>(T)) * kH, reinterpret_cast<void**>(&m->d_stages));
+        A(sizeof(float) * 8 * xblk_rows(static_cast<long long>(T)) * kH, reinterpret_cast<void**>(&m->d_stages));
         if (m->mode == TZ_QUANT_W8A8)
             for (int i = 0; i < 4; ++i) {
-                A(T * (i == 3 ? kF : kH), reinterpret_cast<void**>(&m->d_opq[i]));
+                A(T * gemm_k(i), reinterpret_cast<void**>(&m->d_opq[i]));
                 A(sizeof(float) * T, reinterpret_cast<void**>(&m->d_ops[i]));
+                A(sizeof(int32_t) * T * gemm_n(i), reinterpret_cast<void**>(&m->d_acc[i]));
+                if (i & 1) A(sizeof(__half) * T * gemm_k(i), reinterpret_cast<void**>(&m->d_in16[i]));
             }
     }
     if (rc) {
@@ -693,6 +667,8 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         g.a = m->XA; g.lda = kH; g.b = L.wqkv; g.ldb = kH; g.M = M; g.N = 3 * kH; g.K = kH;
         g.bias = L.bqkv; g.col_scale = wscale ? L.sqkv : nullptr; g.row_scale = q8 ? m->xs : nullptr;
         g.out = m->QKV; g.ldo = 3 * kH; g.out_type = OUT_F16;
+        const bool cap = q8 && l == 0 && m->keep_stages && m->d_acc[0];  // W8A8 layer-0 parity capture
+        if (cap) g.dbg_acc = m->d_acc[0];
         if (l == 0 && (rc = keep_operand(m, 0, m->XA, m->xs, T, kH, s))) return rc;
         if ((rc = prof_mark(m, P_QKV, s))) return rc;
         if ((rc = launch_gemm(ctx, g, s))) return rc;
@@ -702,12 +678,8 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         // buffer; the output projection quantises it per token inside its own kernel.
         if ((rc = launch_attention(ctx, m->QKV, T, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s, pdl)))
             return rc;
-        if (q8 && l == 0 && m->keep_stages) {  // parity hook only: the same quantisation, kept aside
-            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, false,
-                                    static_cast<const __half*>(m->Hh), kH, m->omax, static_cast<int8_t*>(m->OA), m->os, T, 0)))
-                return rc;
-            if ((rc = keep_operand(m, 1, m->OA, m->os, T, kH, s))) return rc;
-        }
+        if (cap)  // the f16 attention output the next kernel quantises in its mainloop
+            TZ_CUDA(cudaMemcpyAsync(m->d_in16[1], m->Hh, sizeof(__half) * T * kH, cudaMemcpyDeviceToDevice, s));
         // output projection + bias + residual + LayerNorm in one kernel (arctic.zig:716-746)
         GemmLnArgs o;
         o.pdl = pdl;
@@ -716,8 +688,16 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         o.bias = L.bo; o.col_scale = wscale ? L.so : nullptr; o.a_absmax = q8 ? m->omax : nullptr;
         o.residual = m->X; o.gamma = L.ln1g; o.beta = L.ln1b; o.eps = kEps;
         o.x_out = m->X; o.aux = m->XA; o.aux_scale = q8 ? m->xs : nullptr; o.aux_int8 = q8;
+        if (cap) {
+            o.dbg_acc = m->d_acc[1];
+            o.dbg_aq = m->d_opq[1];
+            o.dbg_as = m->d_ops[1];
+        }
         if ((rc = prof_mark(m, P_OPROJ, s))) return rc;
         if ((rc = launch_gemm_ln(ctx, o, s))) return rc;
+        if (l == 0 && m->keep_stages)  // layer 0's hidden state after the attention block
+            TZ_CUDA(cudaMemcpyAsync(m->d_stages + static_cast<size_t>(7) * xblk_rows(m->cap_tokens) * kH, m->X,
+                                    sizeof(float) * xblk_rows(T) * kH, cudaMemcpyDeviceToDevice, s));
         // FFN1 + bias + GELU
         GemmArgs f1;
         f1.pdl = pdl;
@@ -725,15 +705,12 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         f1.a = m->XA; f1.lda = kH; f1.b = L.w1; f1.ldb = kH; f1.M = M; f1.N = kF; f1.K = kH;
         f1.bias = L.b1; f1.col_scale = wscale ? L.s1 : nullptr; f1.row_scale = q8 ? m->xs : nullptr;
         f1.gelu = 1; f1.out = m->Hh; f1.ldo = kF; f1.out_type = OUT_F16; f1.row_absmax = q8 ? m->hmax : nullptr;
+        if (cap) f1.dbg_acc = m->d_acc[2];
         if (l == 0 && (rc = keep_operand(m, 2, m->XA, m->xs, T, kH, s))) return rc;
         if ((rc = prof_mark(m, P_FFN1, s))) return rc;
         if ((rc = launch_gemm(ctx, f1, s))) return rc;
-        if (q8 && l == 0 && m->keep_stages) {  // parity hook only
-            if ((rc = launch_kernel(requant_rows_kernel, dim3(rows_grid(T)), dim3(256), 0, s, false,
-                                    static_cast<const __half*>(m->Hh), kF, m->hmax, static_cast<int8_t*>(m->HQ), m->hs, T, 0)))
-                return rc;
-            if ((rc = keep_operand(m, 3, m->HQ, m->hs, T, kF, s))) return rc;
-        }
+        if (cap)  // the f16 GELU output the next kernel quantises in its mainloop
+            TZ_CUDA(cudaMemcpyAsync(m->d_in16[3], m->Hh, sizeof(__half) * T * kF, cudaMemcpyDeviceToDevice, s));
         // FFN2 + bias + residual + LayerNorm in one kernel (arctic.zig:779-807); W8A8 quantises the
         // f16 GELU output per token inside the kernel.
         GemmLnArgs f2;
@@ -743,6 +720,11 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.a_absmax = q8 ? m->hmax : nullptr;
         f2.residual = m->X; f2.gamma = L.ln2g; f2.beta = L.ln2b; f2.eps = kEps;
         f2.x_out = m->X; f2.aux = m->XA; f2.aux_scale = q8 ? m->xs : nullptr; f2.aux_int8 = q8;
+        if (cap) {
+            f2.dbg_acc = m->d_acc[3];
+            f2.dbg_aq = m->d_opq[3];
+            f2.dbg_as = m->d_ops[3];
+        }
         if ((rc = prof_mark(m, P_FFN2, s))) return rc;
         if ((rc = launch_gemm_ln(ctx, f2, s))) return rc;
         if (m->keep_stages)
@@ -1055,7 +1037,7 @@ int tz_arctic_forward_device(tz_model_t m, const uint32_t* d_ids, const int32_t*
 }
 
 int tz_arctic_debug_hidden(tz_model_t m, int stage, float* out, int64_t T) {
-    TZ_CHECK(m && out && stage >= 0 && stage <= kLayers, TZ_EINVAL, "tz_arctic_debug_hidden: bad arguments");
+    TZ_CHECK(m && out && stage >= 0 && stage <= kLayers + 1, TZ_EINVAL, "tz_arctic_debug_hidden: bad arguments");
     if (!m->keep_stages) {
         m->keep_stages = true;  // takes effect from the next forward
         return fail(TZ_EINVAL, "stage capture was off; it is on from the next forward");
@@ -1068,6 +1050,16 @@ int tz_arctic_debug_hidden(tz_model_t m, int stage, float* out, int64_t T) {
     TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
     for (int64_t r = 0; r < T; ++r)
         for (int c = 0; c < kH; ++c) out[static_cast<size_t>(r) * kH + c] = blk[static_cast<size_t>(xblk(r, c))];
+    return TZ_OK;
+}
+
+int tz_arctic_debug_capture(tz_model_t m, int on) {
+    TZ_CHECK(m, TZ_EINVAL, "tz_arctic_debug_capture: null model");
+    if (static_cast<bool>(on) == m->keep_stages) return TZ_OK;
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    m->keep_stages = on != 0;
+    if (!on) free_workspace(m);  // the next forward re-reserves without the capture buffers
     return TZ_OK;
 }
 
@@ -1119,9 +1111,37 @@ int tz_arctic_debug_operand(tz_model_t m, int which, int8_t* q_out, float* scale
         return fail(TZ_EINVAL, "operand capture was off; it is on from the next forward");
     }
     TZ_CHECK(m->d_opq[which] && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
-    const int K = which == 3 ? kF : kH;
+    const int K = gemm_k(which);
     TZ_CUDA(cudaMemcpyAsync(q_out, m->d_opq[which], static_cast<size_t>(T) * K, cudaMemcpyDeviceToHost, m->ctx->stream));
     TZ_CUDA(cudaMemcpyAsync(scale_out, m->d_ops[which], sizeof(float) * T, cudaMemcpyDeviceToHost, m->ctx->stream));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    return TZ_OK;
+}
+
+int tz_arctic_debug_accum(tz_model_t m, int which, int32_t* acc_out, int64_t T) {
+    TZ_CHECK(m && acc_out && which >= 0 && which < 4, TZ_EINVAL, "tz_arctic_debug_accum: bad arguments");
+    TZ_CHECK(m->mode == TZ_QUANT_W8A8, TZ_EINVAL, "tz_arctic_debug_accum: W8A8 models only");
+    if (!m->keep_stages) {
+        m->keep_stages = true;
+        return fail(TZ_EINVAL, "accumulator capture was off; it is on from the next forward");
+    }
+    TZ_CHECK(m->d_acc[which] && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
+    TZ_CUDA(cudaMemcpyAsync(acc_out, m->d_acc[which], sizeof(int32_t) * static_cast<size_t>(T) * gemm_n(which),
+                            cudaMemcpyDeviceToHost, m->ctx->stream));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    return TZ_OK;
+}
+
+int tz_arctic_debug_gemm_input(tz_model_t m, int which, uint16_t* x_out, int64_t T) {
+    TZ_CHECK(m && x_out && (which == 1 || which == 3), TZ_EINVAL, "tz_arctic_debug_gemm_input: which must be 1 or 3");
+    TZ_CHECK(m->mode == TZ_QUANT_W8A8, TZ_EINVAL, "tz_arctic_debug_gemm_input: W8A8 models only");
+    if (!m->keep_stages) {
+        m->keep_stages = true;
+        return fail(TZ_EINVAL, "input capture was off; it is on from the next forward");
+    }
+    TZ_CHECK(m->d_in16[which] && T == m->last_T, TZ_EINVAL, "no captured forward with %lld tokens", static_cast<long long>(T));
+    TZ_CUDA(cudaMemcpyAsync(x_out, m->d_in16[which], sizeof(uint16_t) * static_cast<size_t>(T) * gemm_k(which),
+                            cudaMemcpyDeviceToHost, m->ctx->stream));
     TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
     return TZ_OK;
 }

@@ -42,6 +42,7 @@ struct EpiParams {
     int n_ops;
     uint64_t ops;  // op o in bits [5o, 5o+5) (packed: no dynamic indexing of kernel parameters)
     int vec_ok;  // 16-byte aligned rows for vector stores / residual loads
+    int32_t* dbg_acc;  // parity capture: raw accumulators [M, N] (specialised epilogue), or null
 };
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
@@ -577,6 +578,13 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                     __syncwarp();
                     if (lane == 0) tzp::mbar_arrive(&tempty[acc]);
                 }
+                if (ep.dbg_acc != nullptr && row_ok) {  // parity capture: the raw accumulators of this chunk
+                    int4* d = reinterpret_cast<int4*>(ep.dbg_acc + static_cast<long long>(row) * N + cbase + 16 * c);
+#pragma unroll
+                    for (int j = 0; j < CW / 4; ++j)
+                        d[j] = make_int4(static_cast<int>(cur[4 * j]), static_cast<int>(cur[4 * j + 1]),
+                                         static_cast<int>(cur[4 * j + 2]), static_cast<int>(cur[4 * j + 3]));
+                }
                 // dequantise (+ bias, GELU) two columns per packed f32x2 instruction; the f16 pairs
                 // feed both the staging and the row |max| (max |f16| is exact on the packed halves)
                 uint32_t h[CW / 2];
@@ -772,6 +780,7 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     ep.row_absmax = g.row_absmax;
     ep.n_ops = g.n_ops;
     ep.ops = 0;
+    ep.dbg_acc = g.dbg_acc;
     for (int i = 0; i < 8; ++i) ep.ops |= (static_cast<uint64_t>(g.ops[i]) & 31u) << (5 * i);
     const int out_elem = g.out_type == OUT_F16 ? 2 : 4;
     const bool out_al = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldo * out_elem) % 16 == 0);
@@ -793,6 +802,8 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
         to = tb;  // unused
     }
     if ((FAST & F_ON) != 0 && !use_tma) return fail(TZ_EINVAL, "gemm: specialised epilogue without TMA store");
+    if (g.dbg_acc && ((FAST & F_ON) == 0 || reinterpret_cast<uintptr_t>(g.dbg_acc) % 16 != 0))
+        return fail(TZ_EINVAL, "gemm: accumulator capture needs the specialised epilogue and a 16-byte aligned buffer");
     const int n_tiles = (g.N + BN - 1) / BN;
     const int tiles = ((g.M + 127) / 128) * n_tiles;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;

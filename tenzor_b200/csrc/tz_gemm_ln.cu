@@ -48,6 +48,9 @@ struct LnParams {
     const __half* a16;    // AQ: f16 A [M, K]
     long long lda16;
     unsigned* a_absmax;   // AQ: per-row |max| bits of A
+    int32_t* dbg_acc;     // parity capture (or null): raw accumulators [M, 384]
+    int8_t* dbg_aq;       // AQ parity capture (or null): the int8 A rows as quantised [M, K]
+    float* dbg_as;        // AQ parity capture (or null): their per-token scales [M]
 };
 
 template <int KIND>
@@ -314,6 +317,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             w[2 * i + j] = __byte_perm(quant2_own_max(f0.x, f0.y, inv2), quant2_own_max(f1.x, f1.y, inv2), 0x5410);
                         }
                     }
+                    if (p.dbg_aq != nullptr && cok) {  // parity capture: this thread's 32 quantised columns
+                        uint4* d = reinterpret_cast<uint4*>(p.dbg_aq + static_cast<long long>(grow) * K + kb * 128 + qq * 32);
+                        d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                        d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    }
                     const uint32_t rowa = tzp::smem_u32(smem + cstage * C::STAGE_BYTES) + static_cast<uint32_t>(crow * 128);
                     tzp::st_shared_v4(rowa + (static_cast<uint32_t>((2 * qq) ^ (crow & 7)) << 4), w[0], w[1], w[2], w[3]);
                     tzp::st_shared_v4(rowa + (static_cast<uint32_t>((2 * qq + 1) ^ (crow & 7)) << 4), w[4], w[5], w[6], w[7]);
@@ -340,10 +348,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ok) {
                     const float mx = __uint_as_float(p.a_absmax[row]);
                     rs = (mx == 0.0f) ? 1.0f : __fdiv_rn(mx, 127.0f);
+                    if (p.dbg_as != nullptr && slice == 0) p.dbg_as[row] = rs;
                 }
             }
 
             // ---- pass A: x = dequant(acc) + bias + residual -> TMEM; row sum ----
+            if (p.dbg_acc != nullptr) {  // parity capture: the raw accumulators, before pass A rewrites TMEM
+#pragma unroll 1
+                for (int c = 0; c < kSlice / 16; ++c) {
+                    uint32_t r[16];
+                    tzp::tmem_ld16(tbase + 16 * c, r);
+                    tzp::tmem_ld_wait();
+                    if (ok) {
+                        int4* d = reinterpret_cast<int4*>(p.dbg_acc + static_cast<long long>(row) * kN + c0 + 16 * c);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            d[j] = make_int4(static_cast<int>(r[4 * j]), static_cast<int>(r[4 * j + 1]),
+                                             static_cast<int>(r[4 * j + 2]), static_cast<int>(r[4 * j + 3]));
+                    }
+                }
+            }
             const uint64_t rs2 = tzp::f2_pack(rs, rs);
             uint64_t sum2 = 0;  // (even columns, odd columns)
             bool bad = false;
@@ -553,7 +577,7 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     }
     if (AQ) ta = tb;  // unused: A arrives through the epilogue warps
     LnParams p{g.bias, g.col_scale, g.row_scale, g.residual, g.gamma, g.beta, g.eps, g.x_out, g.aux, g.aux_scale,
-               AQ ? static_cast<const __half*>(g.a) : nullptr, g.lda, g.a_absmax};
+               AQ ? static_cast<const __half*>(g.a) : nullptr, g.lda, g.a_absmax, g.dbg_acc, g.dbg_aq, g.dbg_as};
     const int tiles = (g.M + 127) / 128;
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
     if (grid <= 0) return TZ_OK;
@@ -570,6 +594,9 @@ int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     TZ_CHECK(g.aux_int8 == (g.aux_scale != nullptr), TZ_EINVAL, "gemm_ln: int8 aux needs its scale vector");
     TZ_CHECK(reinterpret_cast<uintptr_t>(g.residual) % 16 == 0 && reinterpret_cast<uintptr_t>(g.x_out) % 16 == 0, TZ_EINVAL,
              "gemm_ln: the blocked residual stream must be 16-byte aligned");
+    TZ_CHECK(reinterpret_cast<uintptr_t>(g.dbg_acc) % 16 == 0 && reinterpret_cast<uintptr_t>(g.dbg_aq) % 16 == 0 &&
+                 (!g.dbg_aq || g.a_absmax),
+             TZ_EINVAL, "gemm_ln: capture buffers must be 16-byte aligned; A capture needs in-kernel quantisation");
     if (g.a_absmax) {
         TZ_CHECK(g.kind == KIND_I8 && g.aux_int8 && !g.row_scale && g.col_scale, TZ_EINVAL,
                  "gemm_ln: in-kernel A quantisation needs the int8 kind, int8 aux, column scales and no row scales");

@@ -119,6 +119,10 @@ struct GemmArgs {
     bool a3x = false;
     int ops[8] = {0};
     bool pdl = false;                  // programmatic dependent launch (inside the model forward)
+    // Parity capture (int8 kind, specialised epilogue): when non-null the epilogue also stores the
+    // raw int32 accumulators it reads from TMEM to dbg_acc [M, N] row-major.  A runtime pointer of
+    // the same kernel instantiation: the forward's own code path writes the capture.
+    int32_t* dbg_acc = nullptr;
 };
 int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s);
 
@@ -155,6 +159,13 @@ struct GemmLnArgs {
     // and resets a_absmax[row] to 0 once the row is done.  kind must be KIND_I8, row_scale null.
     unsigned* a_absmax = nullptr;
     bool pdl = false;
+    // Parity capture (same kernel instantiation, runtime pointers): dbg_acc [M, 384] receives the
+    // raw accumulators (int32 for the int8 kind) read in the LayerNorm epilogue; with in-kernel A
+    // quantisation dbg_aq [M, K] receives the int8 A rows as quantised into the MMA stages and
+    // dbg_as [M] their per-token scales.
+    int32_t* dbg_acc = nullptr;
+    int8_t* dbg_aq = nullptr;
+    float* dbg_as = nullptr;
 };
 int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s);
 

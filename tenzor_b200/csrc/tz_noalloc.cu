@@ -15,6 +15,11 @@
 // the GPU (different streams, or different host threads on one device) race on it.  Its contents
 // are whatever the last call left; nothing here needs it to start at zero, because every byte read
 // is written first by the same call.
+//
+// The kernels run on the calling thread's current device, so that device must be the context's
+// (the call is refused otherwise).  The array's device address is looked up once per device and
+// kept for the life of the process: it assumes the device's primary context lives until exit (a
+// cudaDeviceReset invalidates it).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -74,6 +79,11 @@ extern "C" int tz_linear_w8a8_noalloc(tz_ctx_t ctx, const float* x, const int8_t
              "tz_linear_w8a8_noalloc: m=%d, k=%d, n=%d needs %zu bytes of scratch; the fixed scratch holds %zu "
              "(m*k + 4*m + 4*n, each rounded up to 256 bytes); split the rows or use tz_linear_w8a8",
              m, k, n, bq + bxs + bs, kNoallocBytes);
+    int cur = -1;
+    TZ_CUDA(cudaGetDevice(&cur));
+    TZ_CHECK(cur == ctx->device, TZ_EINVAL,
+             "tz_linear_w8a8_noalloc: the current device (%d) is not the context's (%d); make it current first", cur,
+             ctx->device);
     void* base = nullptr;
     int rc = scratch_address(ctx->device, &base);
     if (rc) return rc;

@@ -18,7 +18,7 @@ def _call(fn, ctx, x, wq, s16, bias, y, m, k, n):
                C.c_void_p(0x1)))  # cudaStreamLegacy: torch's default stream
 
 
-def test_noalloc_matches_allocating_entry_point(ctx):
+def test_noalloc_matches_allocating_entry_point(ctx, oracle):
     from tenzor_b200 import _lib as L
     lib = L.lib()
     rng = np.random.default_rng(2024)
@@ -29,12 +29,16 @@ def test_noalloc_matches_allocating_entry_point(ctx):
         bias = torch.from_numpy(rng.normal(0, 0.02, n).astype(np.float32)).cuda()
         ref = torch.empty((m, n), device="cuda")
         _call(lib.tz_linear_w8a8, ctx, x, wq, s16, bias, ref, m, k, n)
+        # the CPU oracle's W8A8 linear (per-token quantiser, exact integer GEMM, one-rounding epilogue)
+        want = oracle.linear_w8a8(x.cpu().numpy(), wq.cpu().numpy(), s16.cpu().numpy().view(np.uint16),
+                                  bias.cpu().numpy())
         for _ in range(2):  # two calls in a row share the fixed scratch
             out = torch.full((m, n), float("nan"), device="cuda")
             _call(lib.tz_linear_w8a8_noalloc, ctx, x, wq, s16, bias, out, m, k, n)
             torch.cuda.synchronize()
             # same kernels on the same operands: equal within 0 (the tests' int8 tolerance is exact)
             assert torch.equal(out, ref), float((out - ref).abs().max())
+            assert np.array_equal(out.cpu().numpy(), want), float(np.abs(out.cpu().numpy() - want).max())
     ctx.check_status()
 
 
@@ -50,3 +54,22 @@ def test_noalloc_rejects_oversized_problem(ctx):
     rc = lib.tz_linear_w8a8_noalloc(ctx.handle, x.data_ptr(), wq.data_ptr(), s16.data_ptr(), bias.data_ptr(),
                                     y.data_ptr(), m, k, n, C.c_void_p(0x1))
     assert rc == L.TZ_EINVAL and b"fixed scratch" in lib.tz_get_last_error()
+
+
+def test_noalloc_rejects_other_current_device(ctx):
+    """The kernels run on the current device: a context of another device is refused."""
+    from tenzor_b200 import _lib as L
+    from tenzor_b200.runtime import Context
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    lib = L.lib()
+    other = Context(1)
+    try:
+        torch.cuda.set_device(0)
+        t = torch.zeros(16, device="cuda:0")
+        rc = lib.tz_linear_w8a8_noalloc(other.handle, t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(),
+                                        t.data_ptr(), 1, 16, 1, C.c_void_p(0x1))
+        assert rc == L.TZ_EINVAL and b"current device" in lib.tz_get_last_error()
+    finally:
+        other.close()
+        torch.cuda.set_device(0)
