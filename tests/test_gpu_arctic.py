@@ -11,7 +11,7 @@ from tenzor_b200 import synthetic as S
 pytestmark = pytest.mark.gpu
 
 MAX_ABS, MIN_COS = 2e-3, 0.9999
-STAGE_MAX_ABS = 2e-2  # per-stage hidden states (LayerNorm outputs of magnitude up to ~5)
+STAGE_MAX_ABS = 2e-3  # per-stage hidden states (LayerNorm outputs of magnitude up to ~5); measured <= 1.2e-3
 
 
 def _cos(a, b):
@@ -90,8 +90,8 @@ def test_f32_per_stage_parity(oracle, weights, models, c1):
     for stage, h in enumerate(hs):
         d = np.abs(h - dump[stage]).max()
         print(f"f32 stage {stage}: max-abs {d:.3e}, min cos {_cos(h, dump[stage]).min():.8f}")
-        # hidden states are LayerNorm outputs (unit variance, |x| up to ~5): f16 GEMM operands give a
-        # few 1e-3 here
+        # hidden states are LayerNorm outputs (unit variance, |x| up to ~5): f16 GEMM operands give
+        # about 1e-3 here by the last layer
         assert d < STAGE_MAX_ABS, f"stage {stage}: max-abs {d}"
         assert _cos(h, dump[stage]).min() > 0.99999, f"stage {stage}"
 
