@@ -183,16 +183,27 @@ typedef enum {
     TZ_OP_RSQRT = 12,
     TZ_OP_SIN = 13,
     TZ_OP_COS = 14,
-    TZ_OP_ERF = 15,      /* ONNX Erf */
-    TZ_OP_GELU_ERF = 16, /* ONNX Gelu (default): 0.5 x (1 + erf(x / sqrt 2)) */
+    TZ_OP_ERF = 15,       /* erf (the device erff)                                               */
+    TZ_OP_GELU_ERF = 16,  /* the ONNX specification's Gelu: 0.5 x (1 + erf(x / sqrt 2))          */
+    TZ_OP_ERF_AS = 17,    /* the reference ONNX executor's Erf (onnx/executor.zig:125-137): the
+                             Abramowitz-Stegun 7.1.26 polynomial, |error| <= 1.5e-7               */
+    TZ_OP_GELU_TANH = 18, /* the reference ONNX executor's Gelu (onnx/executor.zig:122):
+                             0.5 x (1 + tanh(0.7978845608 (x + 0.044715 x^3))) with tanhf         */
     /* binary ops of an elementwise program (BinaryExpr, expr.zig:352-513) */
     TZ_EW_ADD = 20,
     TZ_EW_SUB = 21,
     TZ_EW_MUL = 22,
     TZ_EW_DIV = 23,
     TZ_EW_MAX = 24,
-    TZ_EW_MIN = 25
+    TZ_EW_MIN = 25,
+    TZ_EW_POW = 26,   /* powf(a, b) (onnx/executor.zig:3558 execPow)                             */
+    TZ_EW_EQ = 27,    /* a == b ? 1 : 0 (execEqual 2656)                                         */
+    TZ_EW_LT = 28,    /* a < b ? 1 : 0 (execCompare .less)                                       */
+    TZ_EW_GT = 29,    /* a > b ? 1 : 0 (execCompare .greater)                                    */
+    /* ternary op: reg[dst] = reg[a] != 0 ? reg[b] : reg[c] (execWhere 2733)                     */
+    TZ_EW_WHERE = 30
 } tz_op;
+#define TZ_OP_LAST_UNARY TZ_OP_GELU_TANH
 
 typedef enum { TZ_RED_SUM = 0, TZ_RED_MEAN = 1, TZ_RED_PROD = 2, TZ_RED_MAX = 3, TZ_RED_MIN = 4 } tz_reduce_op;
 
@@ -260,11 +271,11 @@ int tz_ew_add_mul_exp(tz_ctx_t ctx, const float* a, const float* b_row, const fl
  * in[k][r * row_stride[k] + c * col_stride[k]] for output element (r, c) of [rows, cols] (stride 0 =
  * broadcast, executor.zig:152-197).  Instruction i computes reg[dst] = op(reg[a], reg[b]); registers
  * 0..3 hold the inputs, 4..11 temporaries, 12..15 the constants consts[0..3]; unary ops
- * (TZ_OP_RELU..TZ_OP_GELU_ERF) ignore b.  The output is reg[result]. */
+ * (TZ_OP_RELU..TZ_OP_LAST_UNARY) ignore b.  The output is reg[result]. */
 #define TZ_EW_MAX_INPUTS 4
 #define TZ_EW_MAX_INSTR 16
 typedef struct {
-    int op, dst, a, b;
+    int op, dst, a, b, c; /* c: third operand of TZ_EW_WHERE, ignored otherwise */
 } tz_ew_instr;
 typedef struct {
     int n_inputs;
@@ -278,12 +289,67 @@ typedef struct {
 } tz_ew_program;
 int tz_ew_program_run(tz_ctx_t ctx, const tz_ew_program* prog, float* out, int64_t rows, int cols,
                       tz_stream_t stream);
+/* The same program over N-D broadcast operands (evalBinaryBroadcast, executor.zig:152-197, any rank
+ * up to TZ_MAX_DIMS): out is row-major [shape]; input k of output element idx is read at
+ * in[k][sum_d idx[d] * stride[k][d]] (element strides, 0 along a broadcast dimension).  The
+ * program's row_stride / col_stride are not used. */
+#define TZ_MAX_DIMS 6
+typedef struct {
+    int ndim;
+    int64_t shape[TZ_MAX_DIMS];
+    int64_t stride[TZ_EW_MAX_INPUTS][TZ_MAX_DIMS];
+} tz_nd_layout;
+int tz_ew_program_run_nd(tz_ctx_t ctx, const tz_ew_program* prog, const tz_nd_layout* layout, float* out,
+                         tz_stream_t stream);
 /* General fused elementwise chain (FusedElementwiseKernel, codegen.zig:15-74): out = ops(x). */
 int tz_ew_unary_chain(tz_ctx_t ctx, const float* x, float* out, int64_t n, const int* ops,
                       int n_ops, tz_stream_t stream);
 /* FusedReduceKernel, codegen.zig:151-205: *out (device) = reduce(pre_ops(x)). */
 int tz_reduce(tz_ctx_t ctx, int reduce_op, const int* pre_ops, int n_pre, const float* x,
               int64_t n, float* out, tz_stream_t stream);
+/* ---- N-D tensor ops of the `.eval()` executor and the ONNX op map ---------------------------
+ * Device pointers, asynchronous on `stream`, f32 unless noted. */
+/* Batched matmul with broadcast batch dimensions (evalBatchedMatmul, executor.zig:199-325, and
+ * execMatMul, onnx/executor.zig:1490): for every batch index b (up to 4 dimensions, row-major
+ * batch_shape), c[b][i, j] = sum_k a[b][i, k] * b[b][k, j], where operand element (i, k) of batch b
+ * is at a + sum_d b[d] * a_bstride[d] + i * a_rs + k * a_cs (element strides; a zero batch stride
+ * broadcasts; the matrix strides express transposed or head-interleaved views without a copy), and
+ * the same for b and c.  Contiguous batches of large products go to the tcgen05 GEMM (tf32);
+ * small or strided ones to an f32 CUDA-core kernel with f32 accumulation. */
+typedef struct {
+    int batch_ndim;
+    int64_t batch_shape[4];
+    int64_t a_bstride[4], b_bstride[4], c_bstride[4];
+    int64_t a_rs, a_cs, b_rs, b_cs, c_rs, c_cs;
+    int m, k, n;
+} tz_bmm_layout;
+int tz_batched_matmul(tz_ctx_t ctx, const float* a, const float* b, float* c, const tz_bmm_layout* layout,
+                      tz_stream_t stream);
+/* tz_matmul_epilogue with f32-accurate products: both operands are split into a tf32 head and its
+ * f32 remainder in context scratch and the tcgen05 GEMM sums hi*hi + hi*lo + lo*hi with f32
+ * accumulation (the dropped lo*lo term is about 2^-22 of each product).  Same arguments. */
+int tz_matmul_f32x3(tz_ctx_t ctx, const float* a, const float* b, int trans_b, const float* bias,
+                    const int* ops, int n_ops, float* c, int m, int k, int n, tz_stream_t stream);
+/* reduceAxis (reduce.zig:52-95, executor.zig:327-361): x viewed as [outer, len, inner];
+ * out[outer, inner] = reduce over len (sum / mean accumulate in f64; mean divides by len). */
+int tz_reduce_axis(tz_ctx_t ctx, int reduce_op, const float* x, int64_t outer, int64_t len, int64_t inner,
+                   float* out, tz_stream_t stream);
+/* softmaxAxis (softmax.zig:157-220): x and y viewed as [outer, len, inner], softmax over len
+ * (max-subtracted exp, then multiplied by 1 / sum).  x and y may alias. */
+int tz_softmax_axis(tz_ctx_t ctx, const float* x, float* y, int64_t outer, int64_t len, int64_t inner,
+                    tz_stream_t stream);
+/* Transpose (onnx/executor.zig:2296-2390): y = x permuted, x row-major [shape[0..ndim)], y row-major
+ * with y's dimension d = x's dimension perm[d]; elements of elem_bytes = 1, 2, 4 or 8. */
+int tz_permute(tz_ctx_t ctx, const void* x, void* y, int elem_bytes, int ndim, const int64_t* shape,
+               const int* perm, tz_stream_t stream);
+/* Cast (onnx/executor.zig:2852): element conversion between the TZ_DT_* types f32, f16, i8, i32,
+ * i64 and u8 (bool); float to integer truncates toward zero. */
+int tz_cast(tz_ctx_t ctx, const void* x, int src_dtype, void* y, int dst_dtype, int64_t n, tz_stream_t stream);
+/* Concat (onnx/executor.zig:2112-2225): inputs viewed as [outer, axis_len[i] * inner] row-major, out
+ * [outer, sum(axis_len) * inner]; elements of elem_bytes. */
+int tz_concat(tz_ctx_t ctx, const void* const* inputs, const int64_t* axis_len, int n_inputs, int64_t outer,
+              int64_t inner, int elem_bytes, void* out, tz_stream_t stream);
+
 /* gather, gather.zig:15-57: out[i,:] = table[ids[i],:]; ids out of range -> TZ_EINVAL via the
  * device status word (the row is zero-filled). */
 int tz_gather_rows(tz_ctx_t ctx, const float* table, int64_t table_rows, const uint32_t* ids,

@@ -14,8 +14,10 @@ LIB_PATH = os.path.join(PKG, "libtenzor_cuda.so")
 TZ_OK, TZ_EINVAL, TZ_ENOMEM, TZ_ECUDA, TZ_ETIMEOUT, TZ_EUNSUPPORTED, TZ_EMISSING = range(7)
 QUANT_F32, QUANT_W8A32, QUANT_W8A8 = 0, 1, 2
 OP = {"add": 1, "relu": 2, "gelu": 3, "sigmoid": 4, "tanh": 5, "exp": 6, "neg": 7, "abs": 8,
-      "silu": 9, "log": 10, "sqrt": 11, "rsqrt": 12, "sin": 13, "cos": 14, "erf": 15, "gelu_erf": 16}
-EW_BINARY = {"add": 20, "sub": 21, "mul": 22, "div": 23, "max": 24, "min": 25}
+      "silu": 9, "log": 10, "sqrt": 11, "rsqrt": 12, "sin": 13, "cos": 14, "erf": 15, "gelu_erf": 16,
+      "erf_as": 17, "gelu_tanh": 18}
+EW_BINARY = {"add": 20, "sub": 21, "mul": 22, "div": 23, "max": 24, "min": 25, "pow": 26, "eq": 27, "lt": 28, "gt": 29}
+EW_WHERE = 30
 RED = {"sum": 0, "mean": 1, "prod": 2, "max": 3, "min": 4}
 
 # Every symbol include/tenzor_cuda.h declares (checked by tests/test_abi.py).
@@ -36,7 +38,8 @@ EXPORTS = [
     "tz_tokenizer_encode", "tz_tokenizer_encode_raw", "tz_tokenizer_encode_batch", "tz_arctic_embed_texts",
     "tz_doc_chunk_count", "tz_arctic_embed_documents", "tz_tenzor_hash_name", "tz_tenzor_open",
     "tz_tenzor_close", "tz_tenzor_count", "tz_tenzor_entry_at", "tz_tenzor_find", "tz_tenzor_metadata",
-    "tz_lenet_load_tenzor", "tz_arctic_load_tenzor",
+    "tz_lenet_load_tenzor", "tz_arctic_load_tenzor", "tz_ew_program_run_nd", "tz_batched_matmul",
+    "tz_matmul_f32x3", "tz_reduce_axis", "tz_softmax_axis", "tz_permute", "tz_cast", "tz_concat",
 ]
 
 
@@ -66,12 +69,27 @@ class TenzorEntry(C.Structure):
 
 
 class EwInstr(C.Structure):
-    _fields_ = [("op", C.c_int), ("dst", C.c_int), ("a", C.c_int), ("b", C.c_int)]
+    _fields_ = [("op", C.c_int), ("dst", C.c_int), ("a", C.c_int), ("b", C.c_int), ("c", C.c_int)]
 
 
 class EwProgram(C.Structure):
     _fields_ = [("n_inputs", C.c_int), ("in_", P * 4), ("row_stride", C.c_int64 * 4), ("col_stride", C.c_int64 * 4),
                 ("n_instr", C.c_int), ("instr", EwInstr * 16), ("result", C.c_int), ("consts", C.c_float * 4)]
+
+
+MAX_DIMS = 6
+DT = {"f32": 0, "f16": 1, "bf16": 2, "f64": 3, "i8": 4, "i16": 5, "i32": 6, "i64": 7, "u8": 8}
+
+
+class NdLayout(C.Structure):
+    _fields_ = [("ndim", C.c_int), ("shape", C.c_int64 * MAX_DIMS), ("stride", (C.c_int64 * MAX_DIMS) * 4)]
+
+
+class BmmLayout(C.Structure):
+    _fields_ = [("batch_ndim", C.c_int), ("batch_shape", C.c_int64 * 4), ("a_bstride", C.c_int64 * 4),
+                ("b_bstride", C.c_int64 * 4), ("c_bstride", C.c_int64 * 4)]
+    _fields_ += [(n, C.c_int64) for n in ("a_rs", "a_cs", "b_rs", "b_cs", "c_rs", "c_cs")]
+    _fields_ += [("m", C.c_int), ("k", C.c_int), ("n", C.c_int)]
 
 
 class ArcticWeights(C.Structure):
@@ -147,6 +165,14 @@ def _declare(L):
         "tz_tenzor_metadata": [P, C.POINTER(C.c_char_p), C.POINTER(C.c_uint64)],
         "tz_lenet_load_tenzor": [P, C.c_char_p, i, C.POINTER(P)],
         "tz_arctic_load_tenzor": [P, C.c_char_p, i, C.POINTER(P)],
+        "tz_ew_program_run_nd": [P, C.POINTER(EwProgram), C.POINTER(NdLayout), P, P],
+        "tz_batched_matmul": [P, P, P, P, C.POINTER(BmmLayout), P],
+        "tz_matmul_f32x3": [P, P, P, i, P, P, i, P, i, i, i, P],
+        "tz_reduce_axis": [P, i, P, i64, i64, i64, P, P],
+        "tz_softmax_axis": [P, P, P, i64, i64, i64, P],
+        "tz_permute": [P, P, P, i, i, P, P, P],
+        "tz_cast": [P, P, i, P, i, i64, P],
+        "tz_concat": [P, P, P, i, i64, i64, i, P, P],
     }
     for name, args in sig.items():
         f = getattr(L, name)

@@ -24,6 +24,7 @@
 
 #include "tz_internal.h"
 #include "tz_ptx.cuh"
+#include "tz_rowops.cuh"
 
 namespace tz {
 namespace {
@@ -45,8 +46,6 @@ struct EpiParams {
     int32_t* dbg_acc;  // parity capture: raw accumulators [M, N] (specialised epilogue), or null
 };
 
-__device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
-
 // The fusion GELU (simd.zig:168-178: tanh(z) = 2 sigmoid(2z) - 1) for the fixed epilogue of the f32 /
 // tf32 GEMMs: tanh(z) = 1 - 2 / (1 + exp(2z)) with the fast exponential (ex2.approx on a pre-scaled
 // argument) and the approximate reciprocal (no slow path: an infinite or huge denominator gives 0,
@@ -59,32 +58,9 @@ __device__ __forceinline__ float gelu_sigmoid_fast(float x) {
     return fmaf(hx, t, hx);
 }
 
-// Unary op table of codegen.zig:228-244 (simd.zig scalar ops); TZ_OP_* codes.
-__device__ __forceinline__ float apply_op(int op, float x) {
-    switch (op) {
-        case TZ_OP_RELU: return x > 0.0f ? x : 0.0f;
-        case TZ_OP_GELU: {
-            const float x3 = x * x * x;
-            const float inner = 0.7978845608028654f * (x + 0.044715f * x3);
-            const float t = 2.0f * sigmoid_ref(2.0f * inner) - 1.0f;
-            return 0.5f * x * (1.0f + t);
-        }
-        case TZ_OP_SIGMOID: return sigmoid_ref(x);
-        case TZ_OP_TANH: return 2.0f * sigmoid_ref(2.0f * x) - 1.0f;
-        case TZ_OP_EXP: return expf(x);
-        case TZ_OP_NEG: return -x;
-        case TZ_OP_ABS: return fabsf(x);
-        case TZ_OP_SILU: return x * sigmoid_ref(x);
-        case TZ_OP_LOG: return logf(x);
-        case TZ_OP_SQRT: return sqrtf(x);
-        case TZ_OP_RSQRT: return 1.0f / sqrtf(x);
-        case TZ_OP_SIN: return sinf(x);
-        case TZ_OP_COS: return cosf(x);
-        case TZ_OP_ERF: return erff(x);
-        case TZ_OP_GELU_ERF: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-        default: return x;
-    }
-}
+// Unary op table of codegen.zig:228-244 (simd.zig scalar ops) for the generic epilogue chain: the
+// shared table of the row kernels (tz_rowops.cuh).
+__device__ __forceinline__ float apply_op(int op, float x) { return unary_op(op, x); }
 
 template <int KIND>
 struct KindTraits;

@@ -97,7 +97,7 @@ int tz_matmul_epilogue(tz_ctx_t ctx, const float* a, const float* b, int trans_b
     TZ_CHECK(ctx && a && b && c && m >= 0 && k > 0 && n > 0 && n_ops >= 0 && n_ops <= 8 && (n_ops == 0 || ops),
              TZ_EINVAL, "tz_matmul_epilogue: bad arguments");
     for (int i = 0; i < n_ops; ++i)
-        TZ_CHECK(ops[i] >= TZ_OP_ADD && ops[i] <= TZ_OP_GELU_ERF, TZ_EINVAL, "tz_matmul_epilogue: bad op %d", ops[i]);
+        TZ_CHECK(ops[i] >= TZ_OP_ADD && ops[i] <= TZ_OP_LAST_UNARY, TZ_EINVAL, "tz_matmul_epilogue: bad op %d", ops[i]);
     cudaStream_t s = pick_stream(ctx, stream);
     GemmArgs g;
     g.kind = KIND_TF32;

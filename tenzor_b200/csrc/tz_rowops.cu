@@ -263,10 +263,34 @@ struct EwProgram {
     const float* in[4];
     long long rs[4], cs[4];
     int n_instr;
-    int op[16], dst[16], a[16], b[16];
+    int op[16], dst[16], a[16], b[16], c[16];
     int result;
     float consts[4];
 };
+
+// The program's instructions over one element whose inputs are in reg[0..3]; returns reg[result].
+__device__ __forceinline__ float run_program(const EwProgram& p, float (&reg)[16]) {
+#pragma unroll
+    for (int k = 4; k < 12; ++k) reg[k] = 0.0f;
+#pragma unroll
+    for (int k = 12; k < 16; ++k) reg[k] = p.consts[k - 12];
+    for (int t = 0; t < p.n_instr; ++t) {
+        float va = 0.f, vb = 0.f, vc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {  // register reads by unrolled select: no local memory
+            va = (k == p.a[t]) ? reg[k] : va;
+            vb = (k == p.b[t]) ? reg[k] : vb;
+            vc = (k == p.c[t]) ? reg[k] : vc;
+        }
+        const float res = p.op[t] == TZ_EW_WHERE ? (va != 0.0f ? vb : vc) : binary_op(p.op[t], va, vb);
+#pragma unroll
+        for (int k = 4; k < 12; ++k) reg[k] = (k == p.dst[t]) ? res : reg[k];
+    }
+    float o = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) o = (k == p.result) ? reg[k] : o;
+    return o;
+}
 
 __global__ void ew_program_kernel(EwProgram p, float* __restrict__ out, long long rows, int cols) {
     const long long n = rows * cols;
@@ -276,25 +300,35 @@ __global__ void ew_program_kernel(EwProgram p, float* __restrict__ out, long lon
         float reg[16];
 #pragma unroll
         for (int k = 0; k < 4; ++k) reg[k] = k < p.n_in ? __ldg(p.in[k] + r * p.rs[k] + c * p.cs[k]) : 0.0f;
+        out[i] = run_program(p, reg);
+    }
+}
+
+// N-D broadcast form (executor.zig:152-197 evalBinaryBroadcast, any rank up to TZ_MAX_DIMS): the
+// output is row-major [shape]; input k of output element idx is at sum_d idx[d] * stride[k][d]
+// (stride 0 along a broadcast dimension).
+struct NdLayout {
+    int ndim;
+    long long shape[TZ_MAX_DIMS];
+    long long stride[4][TZ_MAX_DIMS];
+};
+
+__global__ void ew_program_nd_kernel(EwProgram p, NdLayout l, float* __restrict__ out, long long n) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        long long off[4] = {0, 0, 0, 0};
+        long long rem = i;
+        for (int d = l.ndim - 1; d >= 0; --d) {
+            const long long q = rem / l.shape[d];
+            const long long x = rem - q * l.shape[d];
+            rem = q;
 #pragma unroll
-        for (int k = 4; k < 12; ++k) reg[k] = 0.0f;
-#pragma unroll
-        for (int k = 12; k < 16; ++k) reg[k] = p.consts[k - 12];
-        for (int t = 0; t < p.n_instr; ++t) {
-            float va = 0.f, vb = 0.f;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {  // register reads by unrolled select: no local memory
-                va = (k == p.a[t]) ? reg[k] : va;
-                vb = (k == p.b[t]) ? reg[k] : vb;
-            }
-            const float res = binary_op(p.op[t], va, vb);
-#pragma unroll
-            for (int k = 4; k < 12; ++k) reg[k] = (k == p.dst[t]) ? res : reg[k];
+            for (int k = 0; k < 4; ++k) off[k] += x * l.stride[k][d];
         }
-        float o = 0.f;
+        float reg[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) o = (k == p.result) ? reg[k] : o;
-        out[i] = o;
+        for (int k = 0; k < 4; ++k) reg[k] = k < p.n_in ? __ldg(p.in[k] + off[k]) : 0.0f;
+        out[i] = run_program(p, reg);
     }
 }
 
@@ -471,16 +505,19 @@ int tz_ew_add_mul_exp(tz_ctx_t ctx, const float* a, const float* b_row, const fl
     return TZ_OK;
 }
 
-int tz_ew_program_run(tz_ctx_t ctx, const tz_ew_program* prog, float* out, int64_t rows, int cols,
-                      tz_stream_t stream) {
-    TZ_CHECK(ctx && prog && out && rows >= 0 && cols > 0, TZ_EINVAL, "tz_ew_program_run: bad arguments");
+}  // extern "C"
+
+namespace {
+// Checks a tz_ew_program and converts it to the kernel's form.
+int load_program(const tz_ew_program* prog, EwProgram* out, const char* who) {
     TZ_CHECK(prog->n_inputs >= 1 && prog->n_inputs <= TZ_EW_MAX_INPUTS && prog->n_instr >= 0 &&
                  prog->n_instr <= TZ_EW_MAX_INSTR && prog->result >= 0 && prog->result < 16,
-             TZ_EINVAL, "tz_ew_program_run: bad program shape");
-    EwProgram p{};
+             TZ_EINVAL, "%s: bad program shape", who);
+    EwProgram& p = *out;
+    p = EwProgram{};
     p.n_in = prog->n_inputs;
     for (int k = 0; k < p.n_in; ++k) {
-        TZ_CHECK(prog->in[k], TZ_EINVAL, "tz_ew_program_run: input %d is null", k);
+        TZ_CHECK(prog->in[k], TZ_EINVAL, "%s: input %d is null", who, k);
         p.in[k] = prog->in[k];
         p.rs[k] = prog->row_stride[k];
         p.cs[k] = prog->col_stride[k];
@@ -488,21 +525,59 @@ int tz_ew_program_run(tz_ctx_t ctx, const tz_ew_program* prog, float* out, int64
     p.n_instr = prog->n_instr;
     for (int t = 0; t < p.n_instr; ++t) {
         const tz_ew_instr& in = prog->instr[t];
-        const bool unary = in.op >= TZ_OP_RELU && in.op <= TZ_OP_GELU_ERF;
-        const bool binary = in.op >= TZ_EW_ADD && in.op <= TZ_EW_MIN;
-        TZ_CHECK((unary || binary) && in.dst >= 4 && in.dst < 12 && in.a >= 0 && in.a < 16 && (unary || (in.b >= 0 && in.b < 16)),
-                 TZ_EINVAL, "tz_ew_program_run: bad instruction %d", t);
+        const bool unary = in.op >= TZ_OP_RELU && in.op <= TZ_OP_LAST_UNARY;
+        const bool binary = in.op >= TZ_EW_ADD && in.op <= TZ_EW_GT;
+        const bool ternary = in.op == TZ_EW_WHERE;
+        TZ_CHECK((unary || binary || ternary) && in.dst >= 4 && in.dst < 12 && in.a >= 0 && in.a < 16 &&
+                     (unary || (in.b >= 0 && in.b < 16)) && (!ternary || (in.c >= 0 && in.c < 16)),
+                 TZ_EINVAL, "%s: bad instruction %d", who, t);
         p.op[t] = in.op;
         p.dst[t] = in.dst;
         p.a[t] = in.a;
         p.b[t] = unary ? 0 : in.b;
+        p.c[t] = ternary ? in.c : 0;
     }
     p.result = prog->result;
     for (int k = 0; k < 4; ++k) p.consts[k] = prog->consts[k];
+    return TZ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int tz_ew_program_run(tz_ctx_t ctx, const tz_ew_program* prog, float* out, int64_t rows, int cols,
+                      tz_stream_t stream) {
+    TZ_CHECK(ctx && prog && out && rows >= 0 && cols > 0, TZ_EINVAL, "tz_ew_program_run: bad arguments");
+    EwProgram p;
+    int rc = load_program(prog, &p, "tz_ew_program_run");
+    if (rc) return rc;
     const long long n = rows * static_cast<long long>(cols);
     if (n == 0) return TZ_OK;
     cudaStream_t s = pick_stream(ctx, stream);
     ew_program_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(p, out, rows, cols);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+
+int tz_ew_program_run_nd(tz_ctx_t ctx, const tz_ew_program* prog, const tz_nd_layout* layout, float* out,
+                         tz_stream_t stream) {
+    TZ_CHECK(ctx && prog && layout && out, TZ_EINVAL, "tz_ew_program_run_nd: null argument");
+    TZ_CHECK(layout->ndim >= 0 && layout->ndim <= TZ_MAX_DIMS, TZ_EINVAL, "tz_ew_program_run_nd: rank %d", layout->ndim);
+    EwProgram p;
+    int rc = load_program(prog, &p, "tz_ew_program_run_nd");
+    if (rc) return rc;
+    NdLayout l{};
+    l.ndim = layout->ndim;
+    long long n = 1;
+    for (int d = 0; d < l.ndim; ++d) {
+        TZ_CHECK(layout->shape[d] >= 0, TZ_EINVAL, "tz_ew_program_run_nd: negative extent");
+        l.shape[d] = layout->shape[d];
+        n *= l.shape[d];
+        for (int k = 0; k < 4; ++k) l.stride[k][d] = layout->stride[k][d];
+    }
+    if (n == 0) return TZ_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    ew_program_nd_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(p, l, out, n);
     TZ_CUDA(cudaGetLastError());
     return TZ_OK;
 }
@@ -515,7 +590,7 @@ int tz_ew_unary_chain(tz_ctx_t ctx, const float* x, float* out, int64_t n, const
     OpList l{};
     l.n = n_ops;
     for (int i = 0; i < n_ops; ++i) {
-        TZ_CHECK(ops[i] >= TZ_OP_RELU && ops[i] <= TZ_OP_GELU_ERF, TZ_EINVAL, "tz_ew_unary_chain: op %d is not unary", ops[i]);
+        TZ_CHECK(ops[i] >= TZ_OP_RELU && ops[i] <= TZ_OP_LAST_UNARY, TZ_EINVAL, "tz_ew_unary_chain: op %d is not unary", ops[i]);
         l.op[i] = ops[i];
     }
     cudaStream_t s = pick_stream(ctx, stream);
@@ -532,7 +607,7 @@ int tz_reduce(tz_ctx_t ctx, int reduce_op, const int* pre_ops, int n_pre, const 
     OpList l{};
     l.n = n_pre;
     for (int i = 0; i < n_pre; ++i) {
-        TZ_CHECK(pre_ops[i] >= TZ_OP_RELU && pre_ops[i] <= TZ_OP_GELU_ERF, TZ_EINVAL, "tz_reduce: op %d is not unary", pre_ops[i]);
+        TZ_CHECK(pre_ops[i] >= TZ_OP_RELU && pre_ops[i] <= TZ_OP_LAST_UNARY, TZ_EINVAL, "tz_reduce: op %d is not unary", pre_ops[i]);
         l.op[i] = pre_ops[i];
     }
     cudaStream_t s = pick_stream(ctx, stream);

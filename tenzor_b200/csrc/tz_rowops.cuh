@@ -86,6 +86,14 @@ __device__ __forceinline__ float unary_op(int op, float x) {
         case TZ_OP_COS: return cosf(x);
         case TZ_OP_ERF: return erff(x);
         case TZ_OP_GELU_ERF: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+        case TZ_OP_ERF_AS: {  // Abramowitz-Stegun 7.1.26, in the reference executor's operation order
+            const float ax = fabsf(x);
+            const float t = 1.0f / (1.0f + 0.3275911f * ax);
+            const float y = 1.0f - (((((1.061405429f * t + -1.453152027f) * t) + 1.421413741f) * t + -0.284496736f) * t +
+                                    0.254829592f) * t * expf(-ax * ax);
+            return x < 0.0f ? -y : y;
+        }
+        case TZ_OP_GELU_TANH: return x * 0.5f * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
         default: return x;
     }
 }
@@ -98,6 +106,10 @@ __device__ __forceinline__ float binary_op(int op, float a, float b) {
         case TZ_EW_DIV: return a / b;
         case TZ_EW_MAX: return fmaxf(a, b);
         case TZ_EW_MIN: return fminf(a, b);
+        case TZ_EW_POW: return powf(a, b);
+        case TZ_EW_EQ: return a == b ? 1.0f : 0.0f;
+        case TZ_EW_LT: return a < b ? 1.0f : 0.0f;
+        case TZ_EW_GT: return a > b ? 1.0f : 0.0f;
         default: return unary_op(op, a);
     }
 }

@@ -2,9 +2,12 @@
 (src/ops/expr.zig node types, src/backend/cpu/executor.zig evalInto) with the fusion planner of
 src/fusion/analyzer.zig deciding how each graph becomes launches of libtenzor_cuda.so.
 
-Nodes: Tensor (leaf, a device tensor), Constant, Unary, Binary (2-D numpy-style broadcasting, as
-executor.zig:152-197), Matmul (A @ B), Reduce (full reduction), Softmax (last axis), LayerNorm
-(last axis, eps 1e-5 as executor.zig:420 hard-codes), Gather (rows of a table).
+Nodes: Tensor (leaf, a device tensor), Constant, Unary, Binary (numpy-style broadcasting of any rank
+up to 6, as executor.zig:152-197), Matmul (evalMatmul, executor.zig:199-325: dot, vector-matrix,
+matrix-vector, 2-D and batched with broadcast batch dimensions), Reduce (full, or over one axis with
+keep_dims: executor.zig:327-361), Softmax (any axis: softmax.zig:157-220), LayerNorm (last axis, eps
+1e-5 as executor.zig:420 hard-codes), Gather (rows of a table), Transpose and Reshape (expr.zig
+TransposeExpr / ReshapeExpr).
 
 `analyze(expr)` restates analyzePattern (analyzer.zig:106-153): single / elementwise_chain /
 matmul_epilogue / reduce_epilogue (the reference's fused_reduce pattern is never produced by
@@ -31,8 +34,8 @@ from . import ops
 from .runtime import Context
 
 UNARY = ("relu", "gelu", "sigmoid", "tanh", "exp", "neg", "abs", "silu", "log", "sqrt", "rsqrt", "sin", "cos",
-         "erf", "gelu_erf")
-BINARY = ("add", "sub", "mul", "div", "max", "min")
+         "erf", "gelu_erf", "erf_as", "gelu_tanh")
+BINARY = ("add", "sub", "mul", "div", "max", "min", "pow", "eq", "lt", "gt")
 REDUCE = ("sum", "mean", "prod", "max", "min")
 
 
@@ -60,14 +63,17 @@ class Expr:
     def div(self, o): return Binary("div", self, _wrap(o))
     def maximum(self, o): return Binary("max", self, _wrap(o))
     def minimum(self, o): return Binary("min", self, _wrap(o))
+    def pow(self, o): return Binary("pow", self, _wrap(o))
     def matmul(self, o): return Matmul(self, _wrap(o))
-    def sum(self): return Reduce("sum", self)
-    def mean(self): return Reduce("mean", self)
-    def max(self): return Reduce("max", self)
-    def min(self): return Reduce("min", self)
-    def prod(self): return Reduce("prod", self)
-    def softmax(self): return Softmax(self)
+    def sum(self, axis=None, keep_dims=False): return Reduce("sum", self, axis, keep_dims)
+    def mean(self, axis=None, keep_dims=False): return Reduce("mean", self, axis, keep_dims)
+    def max(self, axis=None, keep_dims=False): return Reduce("max", self, axis, keep_dims)
+    def min(self, axis=None, keep_dims=False): return Reduce("min", self, axis, keep_dims)
+    def prod(self, axis=None, keep_dims=False): return Reduce("prod", self, axis, keep_dims)
+    def softmax(self, axis=-1): return Softmax(self, axis)
     def layer_norm(self, gamma, beta): return LayerNorm(self, _wrap(gamma), _wrap(beta))
+    def transpose(self, perm): return Transpose(self, tuple(perm))
+    def reshape(self, shape): return Reshape(self, tuple(shape))
 
     def eval(self, ctx: Context):
         return evaluate(ctx, self)
@@ -124,38 +130,107 @@ class Binary(Expr):
 
 @dataclass(eq=False)
 class Matmul(Expr):
+    """evalMatmul (executor.zig:199-325) shapes: [K]@[K] -> (), [K]@[K,N] -> [N], [M,K]@[K] -> [M],
+    [M,K]@[K,N] -> [M,N], and batched [..., M, K] @ [..., K, N] with numpy-broadcast batch dims.
+    `trans_b` (2-D only) reads b as [N, K]; `precision` is the 2-D tensor-core form: "tf32" or
+    "f32x3" (split tf32, f32-accurate products)."""
     a: Expr
     b: Expr
     trans_b: bool = False
+    precision: str = "tf32"
     kind = "matmul"
 
     def __post_init__(self):
-        m, k = self.a.shape
-        n = self.b.shape[0] if self.trans_b else self.b.shape[1]
-        kb = self.b.shape[1] if self.trans_b else self.b.shape[0]
-        if k != kb:
-            raise ValueError(f"matmul inner dims {k} != {kb}")
-        self.shape = (m, n)
+        sa, sb = tuple(self.a.shape), tuple(self.b.shape)
+        if self.trans_b:
+            if len(sa) != 2 or len(sb) != 2:
+                raise ValueError("trans_b needs 2-D operands")
+            sb = (sb[1], sb[0])
+        if not sa or not sb:
+            raise ValueError("matmul of a scalar")
+        ka = sa[-1]
+        kb = sb[0] if len(sb) == 1 else sb[-2]
+        if ka != kb:
+            raise ValueError(f"matmul inner dims {ka} != {kb}")
+        if len(sa) == 1 and len(sb) == 1:
+            self.shape = ()
+        elif len(sa) == 1:
+            self.shape = sb[:-2] + (sb[-1],)
+        elif len(sb) == 1:
+            self.shape = sa[:-1]
+        else:
+            self.shape = _bshape(sa[:-2], sb[:-2]) + (sa[-2], sb[-1])
 
 
 @dataclass(eq=False)
 class Reduce(Expr):
+    """ReduceExpr: over every element (axis None) or one axis (reduceAxis), keep_dims as given."""
     op: str
     input: Expr
+    axis: object = None
+    keep_dims: bool = False
     kind = "reduce"
 
     def __post_init__(self):
         assert self.op in REDUCE
-        self.shape = ()
+        ish = tuple(self.input.shape)
+        if self.axis is None:
+            self.shape = (1,) * len(ish) if self.keep_dims else ()
+        else:
+            ax = self.axis % len(ish)
+            self.axis = ax
+            self.shape = ish[:ax] + ((1,) if self.keep_dims else ()) + ish[ax + 1:]
 
 
 @dataclass(eq=False)
 class Softmax(Expr):
     input: Expr
+    axis: int = -1
     kind = "softmax"
 
     def __post_init__(self):
         self.shape = self.input.shape
+
+
+@dataclass(eq=False)
+class Transpose(Expr):
+    """TransposeExpr (expr.zig:927): output dimension d is input dimension perm[d]."""
+    input: Expr
+    perm: tuple
+    kind = "transpose"
+
+    def __post_init__(self):
+        if sorted(self.perm) != list(range(len(self.input.shape))):
+            raise ValueError(f"bad permutation {self.perm} for rank {len(self.input.shape)}")
+        self.shape = tuple(self.input.shape[p] for p in self.perm)
+
+
+@dataclass(eq=False)
+class Reshape(Expr):
+    """ReshapeExpr (expr.zig:856): the same elements in row-major order, a new shape (one -1 allowed)."""
+    input: Expr
+    target: tuple
+    kind = "reshape"
+
+    def __post_init__(self):
+        n = 1
+        for d in self.input.shape:
+            n *= d
+        t = list(self.target)
+        if t.count(-1) > 1:
+            raise ValueError("at most one -1 in a reshape")
+        if -1 in t:
+            known = 1
+            for d in t:
+                if d != -1:
+                    known *= d
+            t[t.index(-1)] = n // known if known else 0
+        m = 1
+        for d in t:
+            m *= d
+        if m != n:
+            raise ValueError(f"cannot reshape {self.input.shape} to {self.target}")
+        self.shape = tuple(t)
 
 
 @dataclass(eq=False)
@@ -192,8 +267,8 @@ def tensor(t: torch.Tensor) -> Tensor:
     return Tensor(t)
 
 
-def matmul(a, b, trans_b=False) -> Matmul:
-    return Matmul(_wrap(a), _wrap(b), trans_b)
+def matmul(a, b, trans_b=False, precision="tf32") -> Matmul:
+    return Matmul(_wrap(a), _wrap(b), trans_b, precision)
 
 
 def gather(table, ids) -> Gather:
@@ -246,6 +321,10 @@ def analyze(e: Expr) -> str:
             return "reduce_epilogue"
         return "single"
     return "single"
+
+
+def _is_2d_matmul(m: "Matmul") -> bool:
+    return len(m.a.shape) == 2 and len(m.b.shape) == 2
 
 
 def find_matmul_base(e: Expr):
@@ -318,7 +397,8 @@ def _as2d(shape):
 
 
 def _strides2d(src_shape, out_shape):
-    """(row_stride, col_stride) that read a broadcast source as the 2-D view of out_shape."""
+    """(row_stride, col_stride) that read a broadcast source as the 2-D view of out_shape, or None
+    when the broadcast is not a row / column broadcast of that view (then the N-D form is used)."""
     orow, ocol = _as2d(out_shape)
     if len(src_shape) == 0:
         return 0, 0
@@ -330,7 +410,18 @@ def _strides2d(src_shape, out_shape):
         return 0, 1  # row vector broadcast along rows
     if s[-1] == 1 and tuple(lead) == tuple(out_shape[:-1]):
         return 1, 0  # column vector broadcast along columns
-    raise NotImplementedError(f"broadcast of {src_shape} to {out_shape} is not a 2-D row/column broadcast")
+    return None
+
+
+def _bstrides(src_shape, out_shape):
+    """broadcastStrides (core/strides.zig): element strides of a contiguous source read at every
+    index of out_shape (0 along broadcast dimensions)."""
+    s = (1,) * (len(out_shape) - len(src_shape)) + tuple(src_shape)
+    st, acc = [0] * len(s), 1
+    for d in range(len(s) - 1, -1, -1):
+        st[d] = 0 if s[d] == 1 and out_shape[d] != 1 else acc
+        acc *= s[d]
+    return st
 
 
 def _eval_leaf(ctx, e: Expr) -> torch.Tensor:
@@ -389,21 +480,44 @@ def _program(ctx, e: Expr) -> torch.Tensor:
         return d
 
     res = emit(e)
-    out = _dev(e.shape)
+    return _launch_program(ctx, prog, leaves, instr, consts, res, e.shape)
+
+
+def _launch_program(ctx, prog, leaves, instr, consts, res, out_shape):
+    """One tz_ew_program_run launch (2-D row / column broadcasts) or tz_ew_program_run_nd (any
+    other broadcast, rank <= 6).  instr: (op, dst, a, b[, c]) tuples."""
+    out = _dev(out_shape)
     prog.n_inputs = len(leaves)
+    s2d = [_strides2d(shape, out_shape) for _, shape in leaves]
     for i, (t, shape) in enumerate(leaves):
         prog.in_[i] = t.data_ptr()
-        rs, cs = _strides2d(shape, e.shape)
+        rs, cs = s2d[i] if s2d[i] is not None else (0, 0)
         prog.row_stride[i] = rs
         prog.col_stride[i] = cs
     prog.n_instr = len(instr)
-    for i, (op, d, a, b) in enumerate(instr):
+    for i, ins in enumerate(instr):
+        op, d, a, b = ins[:4]
         prog.instr[i].op, prog.instr[i].dst, prog.instr[i].a, prog.instr[i].b = op, d, a, b
+        prog.instr[i].c = ins[4] if len(ins) > 4 else 0
     prog.result = res
     for i, v in enumerate(consts):
         prog.consts[i] = v
-    rows, cols = _as2d(e.shape)
-    L.check(L.lib().tz_ew_program_run(ctx.handle, C.byref(prog), out.data_ptr(), rows, cols, ops._stream()))
+    if out.numel() == 0:
+        return out
+    if all(x is not None for x in s2d) and len(out_shape) >= 1:
+        rows, cols = _as2d(out_shape)
+        L.check(L.lib().tz_ew_program_run(ctx.handle, C.byref(prog), out.data_ptr(), rows, cols, ops._stream()))
+        return out
+    if len(out_shape) > L.MAX_DIMS:
+        raise ValueError(f"rank {len(out_shape)} is above {L.MAX_DIMS}")
+    lay = L.NdLayout()
+    lay.ndim = len(out_shape)
+    for d, n in enumerate(out_shape):
+        lay.shape[d] = n
+    for i, (t, shape) in enumerate(leaves):
+        for d, st in enumerate(_bstrides(shape, out_shape)):
+            lay.stride[i][d] = st
+    L.check(L.lib().tz_ew_program_run_nd(ctx.handle, C.byref(prog), C.byref(lay), out.data_ptr(), ops._stream()))
     return out
 
 
@@ -422,6 +536,10 @@ def _match_add_mul_exp(e: Expr):
 def evaluate(ctx: Context, e: Expr) -> torch.Tensor:
     """executor.evalInto (executor.zig:49-93) with FusionPlan-driven CUDA launches."""
     p = plan(e)
+    if p.pattern == "matmul_epilogue" and not _is_2d_matmul(find_matmul_base(e)):
+        base = find_matmul_base(e)  # batched / vector products: the product, then the rest as a program
+        mm = evaluate(ctx, base)
+        return _program(ctx, _replace(e, base, Tensor(mm)))
     if p.pattern == "matmul_epilogue":
         base = find_matmul_base(e)
         chain = []
@@ -441,7 +559,8 @@ def evaluate(ctx: Context, e: Expr) -> torch.Tensor:
         if ok and len(chain) <= 8:
             a = _eval_leaf(ctx, base.a)
             b = _eval_leaf(ctx, base.b)
-            return ops.matmul_epilogue(ctx, a, b, bias, chain, trans_b=base.trans_b)
+            mm = ops.matmul_f32x3 if base.precision == "f32x3" else ops.matmul_epilogue
+            return mm(ctx, a, b, bias, chain, trans_b=base.trans_b)
         # epilogue not expressible as bias + activations: matmul, then the rest as a program
         mm = evaluate(ctx, base)
         return _program(ctx, _replace(e, base, Tensor(mm)))
@@ -455,6 +574,8 @@ def evaluate(ctx: Context, e: Expr) -> torch.Tensor:
         if chain is not None and len(chain) <= 8:
             return ops.ew_unary_chain(ctx, _eval_leaf(ctx, leaf), chain)
         return _program(ctx, e)
+    if p.pattern == "reduce_epilogue" and e.axis is not None:
+        return _reduce_axis(ctx, e, _program(ctx, e.input))
     if p.pattern == "reduce_epilogue":
         chain, leaf = collect_unary_chain(e.input)
         if chain is not None and len(chain) <= 8:
@@ -471,17 +592,61 @@ def evaluate(ctx: Context, e: Expr) -> torch.Tensor:
         return _program(ctx, Binary(e.op, Tensor(_eval_leaf(ctx, e.lhs)) if e.lhs.kind not in ("tensor", "constant") else e.lhs,
                                     Tensor(_eval_leaf(ctx, e.rhs)) if e.rhs.kind not in ("tensor", "constant") else e.rhs))
     if k == "matmul":
-        return ops.matmul_epilogue(ctx, _eval_leaf(ctx, e.a), _eval_leaf(ctx, e.b), None, [], trans_b=e.trans_b)
+        return _matmul(ctx, e)
     if k == "reduce":
-        return ops.reduce(ctx, e.op, [], _eval_leaf(ctx, e.input).contiguous())
+        x = _eval_leaf(ctx, e.input).contiguous()
+        if e.axis is not None:
+            return _reduce_axis(ctx, e, x)
+        r = ops.reduce(ctx, e.op, [], x)
+        return r.reshape(e.shape)
     if k == "softmax":
-        return ops.softmax_last_axis(ctx, _eval_leaf(ctx, e.input).contiguous())
+        x = _eval_leaf(ctx, e.input).contiguous()
+        if len(e.shape) <= 1 or e.axis % len(e.shape) == len(e.shape) - 1:
+            return ops.softmax_last_axis(ctx, x.reshape(-1, x.shape[-1] if x.dim() else 1)).reshape(e.shape)
+        return ops.softmax_axis(ctx, x, e.axis)
+    if k == "transpose":
+        return ops.permute(ctx, _eval_leaf(ctx, e.input).contiguous(), list(e.perm))
+    if k == "reshape":
+        return _eval_leaf(ctx, e.input).contiguous().reshape(e.shape)  # a view: no data moves
     if k == "layernorm":
         return ops.layer_norm_last_dim(ctx, _eval_leaf(ctx, e.input).contiguous(), _eval_leaf(ctx, e.gamma),
                                        _eval_leaf(ctx, e.beta), e.eps)
     if k == "gather":
         return ops.gather_rows(ctx, _eval_leaf(ctx, e.table), e.ids)
     raise NotImplementedError(k)
+
+
+def _reduce_axis(ctx, e: Reduce, x):
+    return ops.reduce_axis(ctx, e.op, x.contiguous(), e.axis, e.keep_dims)
+
+
+def _matmul(ctx, e: Matmul):
+    """evalMatmul (executor.zig:199-325): 2-D products and [B, M, K] @ [K, N] (flattened to one
+    2-D GEMM, the batchedMatmulBroadcastB case) on the tcgen05 GEMM; vector and batched products
+    with distinct or broadcast batch matrices on tz_batched_matmul."""
+    a = _eval_leaf(ctx, e.a).contiguous()
+    b = _eval_leaf(ctx, e.b).contiguous()
+    mm = ops.matmul_f32x3 if e.precision == "f32x3" else ops.matmul_epilogue
+    if a.dim() == 2 and b.dim() == 2:
+        return mm(ctx, a, b, None, [], trans_b=e.trans_b)
+    if a.dim() >= 3 and b.dim() == 2 and a.shape[-1] % 4 == 0 and b.shape[1] % 4 == 0:
+        return mm(ctx, a.reshape(-1, a.shape[-1]), b, None, []).reshape(e.shape)
+    sa = tuple(a.shape) if a.dim() >= 2 else (1,) + tuple(a.shape)   # [K] -> [1, K]
+    sb = tuple(b.shape) if b.dim() >= 2 else tuple(b.shape) + (1,)   # [K] -> [K, 1]
+    m, k, n = sa[-2], sa[-1], sb[-1]
+    batch = _bshape(sa[:-2], sb[:-2])
+    if len(batch) > 4:
+        raise ValueError("more than 4 batch dimensions")
+
+    def bstr(shape):
+        full = (1,) * (len(batch) - len(shape[:-2])) + tuple(shape[:-2])
+        mat, st, acc = shape[-2] * shape[-1], [0] * len(batch), shape[-2] * shape[-1]
+        for d in range(len(batch) - 1, -1, -1):
+            st[d] = 0 if full[d] == 1 else acc
+            acc *= full[d]
+        return st
+    out = ops.batched_matmul(ctx, a, b, tuple(batch) + (m, n), batch, bstr(sa), bstr(sb), m, k, n, k, 1, n, 1)
+    return out.reshape(e.shape)
 
 
 def _replace(e: Expr, old: Expr, new: Expr) -> Expr:

@@ -187,7 +187,7 @@ def _node(data: bytes) -> Node:
             attrs[k] = v
         else:
             r.skip(w)
-    return Node(op, [i for i in ins if i], outs, attrs)
+    return Node(op, ins, outs, attrs)  # an empty name stands for an omitted optional input
 
 
 def _value_info_name(data: bytes) -> str:
@@ -259,18 +259,22 @@ def load(path: str) -> OnnxModel:
         return parse_model(fh.read())
 
 
-def run(ctx, model: OnnxModel, feeds: dict, ref_ln_eps: bool = False):
-    """Executes the model on the device: initializers and feeds become CUDA tensors (floating point as
-    f32, integer index tensors as int64), then run_graph walks the nodes.  Returns the outputs."""
+def run(ctx, model: OnnxModel, feeds: dict, spec: bool = False, precision: str = "f32x3"):
+    """Executes the model on the device: floating-point initializers and feeds become f32 CUDA
+    tensors, integer feeds int64 CUDA tensors, integer initializers stay host arrays (the value model
+    of tenzor_b200.onnx_ops), then run_graph walks the nodes.  Returns the outputs."""
     import torch
 
-    def dev(a):
+    def value(a, feed):
         a = np.asarray(a)
         if np.issubdtype(a.dtype, np.floating):
             return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
-        return torch.from_numpy(np.ascontiguousarray(a, np.int64)).cuda()
-    inits = {k: dev(v) for k, v in model.initializers.items()}
+        if feed:  # integer data (ids, masks) go to the device
+            return torch.from_numpy(np.ascontiguousarray(a.astype(np.int64))).cuda()
+        return np.ascontiguousarray(a)  # integer constants (axes, shapes, position ids) stay host metadata
+    inits = {k: value(v, False) for k, v in model.initializers.items()}
     missing = [i for i in model.inputs if i not in feeds]
     if missing:
         raise KeyError(f"missing graph inputs {missing}")
-    return run_graph(ctx, model.nodes, inits, {k: dev(v) for k, v in feeds.items()}, model.outputs, ref_ln_eps)
+    return run_graph(ctx, model.nodes, inits, {k: value(v, True) for k, v in feeds.items()}, model.outputs, spec=spec,
+                     precision=precision)

@@ -8,6 +8,8 @@ every computation runs in libtenzor_cuda.so).  Names follow the reference kernel
   matmul_epilogue       codegen.zig:78-147            ew_add_mul_exp      executor.zig:114-197
   ew_unary_chain        codegen.zig:15-74             reduce              codegen.zig:151-205
   gather_rows           gather.zig:15-57
+N-D forms (executor.zig / onnx/executor.zig): batched_matmul, matmul_f32x3, reduce_axis, softmax_axis,
+permute, cast, concat.
 """
 from __future__ import annotations
 
@@ -150,4 +152,115 @@ def gather_rows(ctx: Context, table, ids, out=None):
     rows, cols = table.shape
     out = torch.empty((ids.numel(), cols), device=table.device, dtype=torch.float32) if out is None else out
     L.check(L.lib().tz_gather_rows(ctx.handle, _p(table), rows, _p(ids), ids.numel(), cols, _p(out), _stream()))
+    return out
+
+
+# ---- N-D ops -------------------------------------------------------------------------------------
+_TORCH_DT = {torch.float32: "f32", torch.float16: "f16", torch.int8: "i8", torch.int32: "i32",
+             torch.int64: "i64", torch.uint8: "u8", torch.bool: "u8"}
+
+
+def matmul_f32x3(ctx: Context, a, b, bias, ops, trans_b=False, out=None):
+    """matmul_epilogue with f32-accurate products (split tf32 on the tensor cores)."""
+    m, k = a.shape
+    n = b.shape[0] if trans_b else b.shape[1]
+    out = torch.empty((m, n), device=a.device, dtype=torch.float32) if out is None else out
+    codes = (C.c_int * max(1, len(ops)))(*[L.OP[o] if isinstance(o, str) else int(o) for o in ops])
+    L.check(L.lib().tz_matmul_f32x3(ctx.handle, _p(a), _p(b), int(trans_b), _p(bias), C.addressof(codes),
+                                    len(ops), _p(out), m, k, n, _stream()))
+    return out
+
+
+def batched_matmul(ctx: Context, a, b, out_shape, batch_shape, a_bstride, b_bstride, m, k, n,
+                   a_rs, a_cs, b_rs, b_cs, out=None, c_view=None):
+    """Batched matmul on element strides (tz_batched_matmul).  The output is a new contiguous
+    tensor of out_shape unless `out` is given with `c_view` = (c_bstride, c_rs, c_cs)."""
+    if out is None:
+        out = torch.empty(out_shape, device=a.device, dtype=torch.float32)
+    lay = L.BmmLayout()
+    lay.batch_ndim = len(batch_shape)
+    if c_view is None:
+        cb, acc = [], m * n
+        for d in reversed(batch_shape):
+            cb.append(acc)
+            acc *= d
+        c_view = (list(reversed(cb)), n, 1)
+    for d, e in enumerate(batch_shape):
+        lay.batch_shape[d] = e
+        lay.a_bstride[d] = a_bstride[d]
+        lay.b_bstride[d] = b_bstride[d]
+        lay.c_bstride[d] = c_view[0][d]
+    lay.a_rs, lay.a_cs, lay.b_rs, lay.b_cs = a_rs, a_cs, b_rs, b_cs
+    lay.c_rs, lay.c_cs = c_view[1], c_view[2]
+    lay.m, lay.k, lay.n = m, k, n
+    L.check(L.lib().tz_batched_matmul(ctx.handle, _p(a), _p(b), _p(out), C.byref(lay), _stream()))
+    return out
+
+
+def _split_axis(shape, axis):
+    axis = axis % len(shape) if shape else 0
+    outer = 1
+    for d in shape[:axis]:
+        outer *= d
+    inner = 1
+    for d in shape[axis + 1:]:
+        inner *= d
+    return axis, outer, shape[axis], inner
+
+
+def reduce_axis(ctx: Context, op: str, x, axis: int, keepdims=False):
+    """reduceAxis (reduce.zig:52-95): one axis of a contiguous f32 tensor."""
+    shape = list(x.shape)
+    axis, outer, ln, inner = _split_axis(shape, axis)
+    oshape = shape[:axis] + ([1] if keepdims else []) + shape[axis + 1:]
+    out = torch.empty(oshape, device=x.device, dtype=torch.float32)
+    L.check(L.lib().tz_reduce_axis(ctx.handle, L.RED[op], _p(x), outer, ln, inner, _p(out), _stream()))
+    return out
+
+
+def softmax_axis(ctx: Context, x, axis: int = -1, out=None):
+    """softmaxAxis (softmax.zig:157-220)."""
+    shape = list(x.shape)
+    axis, outer, ln, inner = _split_axis(shape, axis)
+    out = torch.empty_like(x) if out is None else out
+    L.check(L.lib().tz_softmax_axis(ctx.handle, _p(x), _p(out), outer, ln, inner, _stream()))
+    return out
+
+
+def permute(ctx: Context, x, perm):
+    """Transpose (onnx/executor.zig:2296): a contiguous copy of x.permute(perm)."""
+    shape = list(x.shape)
+    out = torch.empty([shape[p] for p in perm], device=x.device, dtype=x.dtype)
+    sh = (C.c_int64 * max(1, len(shape)))(*shape)
+    pm = (C.c_int * max(1, len(perm)))(*perm)
+    L.check(L.lib().tz_permute(ctx.handle, _p(x), _p(out), x.element_size(), len(shape), C.addressof(sh),
+                               C.addressof(pm), _stream()))
+    return out
+
+
+def cast(ctx: Context, x, dtype):
+    """Cast (onnx/executor.zig:2852) on the device."""
+    out = torch.empty(x.shape, device=x.device, dtype=dtype)
+    L.check(L.lib().tz_cast(ctx.handle, _p(x), L.DT[_TORCH_DT[x.dtype]], _p(out), L.DT[_TORCH_DT[dtype]], x.numel(),
+                            _stream()))
+    return out
+
+
+def concat(ctx: Context, xs, axis: int):
+    """Concat (onnx/executor.zig:2112) of contiguous tensors of one dtype along `axis`."""
+    shape = list(xs[0].shape)
+    axis = axis % len(shape)
+    outer = 1
+    for d in shape[:axis]:
+        outer *= d
+    inner = 1
+    for d in shape[axis + 1:]:
+        inner *= d
+    lens = [int(t.shape[axis]) for t in xs]
+    oshape = shape[:axis] + [sum(lens)] + shape[axis + 1:]
+    out = torch.empty(oshape, device=xs[0].device, dtype=xs[0].dtype)
+    ptrs = (C.c_void_p * len(xs))(*[t.data_ptr() for t in xs])
+    ln = (C.c_int64 * len(xs))(*lens)
+    L.check(L.lib().tz_concat(ctx.handle, C.addressof(ptrs), C.addressof(ln), len(xs), outer, inner,
+                              xs[0].element_size(), _p(out), _stream()))
     return out

@@ -119,3 +119,10 @@ TOKENIZER_HF = [
     ("don't", [101, 2123, 1005, 1056, 102]),
     ("   spaces   ", [101, 7258, 102]),
 ]
+
+# onnx/executor.zig:6197-6244 ("Executor basic elementwise") and 6246-6293 ("Executor MatMul"):
+# (op, A, B, shape A, shape B, expected C)
+ONNX_EXECUTOR = [
+    ("Add", [1, 2, 3, 4], [10, 20, 30, 40], (4,), (4,), [11, 22, 33, 44]),
+    ("MatMul", [1, 2, 3, 4, 5, 6], [1, 2, 3, 4, 5, 6], (2, 3), (3, 2), [22, 28, 49, 64]),
+]
