@@ -559,7 +559,7 @@ def evaluate(ctx: Context, e: Expr) -> torch.Tensor:
         if ok and len(chain) <= 8:
             a = _eval_leaf(ctx, base.a)
             b = _eval_leaf(ctx, base.b)
-            mm = ops.matmul_f32x3 if base.precision == "f32x3" else ops.matmul_epilogue
+            mm = _mm2d_fn(base.precision, a.shape[1])
             return mm(ctx, a, b, bias, chain, trans_b=base.trans_b)
         # epilogue not expressible as bias + activations: matmul, then the rest as a program
         mm = evaluate(ctx, base)
@@ -616,6 +616,12 @@ def evaluate(ctx: Context, e: Expr) -> torch.Tensor:
     raise NotImplementedError(k)
 
 
+def _mm2d_fn(precision, k):
+    """The 2-D tensor-core product: one tf32 pass, or split tf32 when asked for or when K is not a
+    whole number of 16-byte TMA units (the split operands are padded to 32 columns)."""
+    return ops.matmul_f32x3 if precision == "f32x3" or k % 4 else ops.matmul_epilogue
+
+
 def _reduce_axis(ctx, e: Reduce, x):
     return ops.reduce_axis(ctx, e.op, x.contiguous(), e.axis, e.keep_dims)
 
@@ -626,7 +632,7 @@ def _matmul(ctx, e: Matmul):
     with distinct or broadcast batch matrices on tz_batched_matmul."""
     a = _eval_leaf(ctx, e.a).contiguous()
     b = _eval_leaf(ctx, e.b).contiguous()
-    mm = ops.matmul_f32x3 if e.precision == "f32x3" else ops.matmul_epilogue
+    mm = _mm2d_fn(e.precision, a.shape[-1])
     if a.dim() == 2 and b.dim() == 2:
         return mm(ctx, a, b, None, [], trans_b=e.trans_b)
     if a.dim() >= 3 and b.dim() == 2 and a.shape[-1] % 4 == 0 and b.shape[1] % 4 == 0:

@@ -15,7 +15,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from .onnx_ops import Node, run_graph
+from .onnx_ops import Node, _c, run_graph
 
 # TensorProto.DataType values used by encoder graphs (onnx.proto3)
 _DTYPES = {1: np.float32, 2: np.uint8, 3: np.int8, 5: np.int16, 6: np.int32, 7: np.int64, 9: np.bool_,
@@ -268,10 +268,10 @@ def run(ctx, model: OnnxModel, feeds: dict, spec: bool = False, precision: str =
     def value(a, feed):
         a = np.asarray(a)
         if np.issubdtype(a.dtype, np.floating):
-            return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+            return torch.from_numpy(_c(a, np.float32)).cuda()
         if feed:  # integer data (ids, masks) go to the device
-            return torch.from_numpy(np.ascontiguousarray(a.astype(np.int64))).cuda()
-        return np.ascontiguousarray(a)  # integer constants (axes, shapes, position ids) stay host metadata
+            return torch.from_numpy(_c(a, np.int64)).cuda()
+        return _c(a)  # integer constants (axes, shapes, position ids) stay host metadata
     inits = {k: value(v, False) for k, v in model.initializers.items()}
     missing = [i for i in model.inputs if i not in feeds]
     if missing:

@@ -62,6 +62,11 @@ class Node:
 
 
 # ---- value helpers -----------------------------------------------------------------------------
+def _c(a, dtype=None) -> np.ndarray:
+    """A C-contiguous copy of the same rank (np.ascontiguousarray would turn a 0-d array into 1-d)."""
+    return np.array(a, dtype=dtype, order="C", copy=True)
+
+
 def _host(v) -> bool:
     return isinstance(v, np.ndarray) or np.isscalar(v)
 
@@ -72,12 +77,12 @@ def _f32(rt: Runtime, v) -> torch.Tensor:
     if _host(v):
         a = np.asarray(v)
         if a.dtype == np.float32:
-            return torch.from_numpy(np.ascontiguousarray(a)).cuda()
-        t = torch.from_numpy(np.ascontiguousarray(a.astype(np.int64) if a.dtype.kind in "biu" else a)).cuda()
+            return torch.from_numpy(_c(a)).cuda()
+        t = torch.from_numpy(_c(a.astype(np.int64) if a.dtype.kind in "biu" else a)).cuda()
         if t.dtype == torch.float32:
             return t
         if t.dtype == torch.float64:
-            return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+            return torch.from_numpy(_c(a, np.float32)).cuda()
         return ops.cast(rt.ctx, t, torch.float32)
     v = v.contiguous()
     return v if v.dtype == torch.float32 else ops.cast(rt.ctx, v, torch.float32)
@@ -147,7 +152,7 @@ def _where(rt, ins, attrs):
 
 # ---- linear algebra ----------------------------------------------------------------------------
 def _mm2d(rt, a, b, bias=None, chain=(), trans_b=False):
-    f = ops.matmul_f32x3 if rt.precision == "f32x3" else ops.matmul_epilogue
+    f = E._mm2d_fn(rt.precision, a.shape[-1])
     return f(rt.ctx, a.contiguous(), b.contiguous(), bias, list(chain), trans_b=trans_b)
 
 
@@ -281,7 +286,7 @@ def _constant(rt, ins, attrs):
         v = np.asarray(attrs["value_ints"], np.int64)
     else:
         raise NotImplementedError("Constant without value / value_float / value_int(s)")
-    return [torch.from_numpy(np.ascontiguousarray(v, np.float32)).cuda() if v.dtype.kind == "f" and v.ndim else v]
+    return [torch.from_numpy(_c(v, np.float32)).cuda() if v.dtype.kind == "f" and v.ndim else v]
 
 
 def _reshape(rt, ins, attrs):
@@ -344,7 +349,7 @@ def _cast(rt, ins, attrs):
         return [np.asarray(x).astype(_ONNX_NP[to])]
     if _host(x):  # an integer tensor entering float computation (e.g. an attention mask)
         a = np.asarray(x)
-        x = torch.from_numpy(np.ascontiguousarray(a.astype(np.int64) if a.dtype.kind in "biu" else a)).cuda()
+        x = torch.from_numpy(_c(a.astype(np.int64) if a.dtype.kind in "biu" else a)).cuda()
     want = _ONNX_TORCH[to]
     if want == torch.bool:
         want = torch.uint8
