@@ -293,11 +293,20 @@ def _pack(ids, lens):
 
 
 def make_inputs(cfg, world):
+    """(ids [B, S], lengths [B], the global row ids of each rank).  configs[0] / configs[1] scale
+    weakly: rank r runs its own block of `batch` sequences whose lengths are those of the one-GPU
+    batch (seed 7) and whose tokens are drawn from seed 7 + r, so every rank does the one-GPU work.
+    configs[3] scales strongly: its fixed 8192-sequence batch is dealt by work (shard_by_tokens)."""
     from tenzor_b200 import synthetic as S
+    from tenzor_b200.shard import shard_by_tokens
     c = CONFIGS[cfg]
-    B = c["batch"] * (world if cfg != "c4" else 1)
-    ids, lens = S.token_batch(B, c["seq"], c["lmin"], c["lmax"], seed=7)
-    return ids, lens
+    ids0, lens0 = S.token_batch(c["batch"], c["seq"], c["lmin"], c["lmax"], seed=7)
+    if cfg == "c4":
+        return ids0, lens0, shard_by_tokens(lens0, world) if world > 1 else [np.arange(len(lens0))]
+    ids = np.concatenate([ids0] + [S.token_batch_with_lengths(lens0, c["seq"], seed=7 + r) for r in range(1, world)])
+    lens = np.concatenate([lens0] * world)
+    B = c["batch"]
+    return ids, lens, [np.arange(r * B, (r + 1) * B) for r in range(world)]
 
 
 def run_reference(a):
@@ -310,7 +319,7 @@ def run_reference(a):
     import oracle as O
     w = S.arctic_weights(1234)
     ck = O.quantize_checkpoint(w) if a.mode != "f32" else w
-    ids, lens = make_inputs(a.config, world)
+    ids, lens, _ = make_inputs(a.config, world)
     ref_mode = "w8a32" if a.mode != "f32" else "f32"  # the reference's own int8 path is W8A32
     vals = []
     sample = ""
@@ -360,8 +369,7 @@ def run_ours(a):
     ck = quantize_checkpoint(ctx, w) if a.mode != "f32" else w
     model = ArcticModel.from_checkpoint(ctx, ck, a.mode)
 
-    ids, lens = make_inputs(a.config, world)
-    shards = shard_by_tokens(lens, world) if world > 1 else [np.arange(len(lens))]
+    ids, lens, shards = make_inputs(a.config, world)
     mine = shards[rank]
     l_ids, l_lens = ids[mine], lens[mine]
     packed, cu = S.pack(l_ids, l_lens)
@@ -373,21 +381,39 @@ def run_ours(a):
     if world > 1:
         gather = RankGather(mine, len(lens), 384, torch.device("cuda", local),
                             lambda table, ids, out: ops.gather_rows(ctx, table, ids, out=out))
-    d_out = torch.zeros((gather.cap if gather else B, 384), device="cuda", dtype=torch.float32)
+    # two output buffers: step i's gather reads one while step i + 1's forward writes the other
+    d_outs = [torch.zeros((gather.cap if gather else B, 384), device="cuda", dtype=torch.float32) for _ in range(2)]
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)  # > 126 MB L2
-    # A dedicated stream: the forward, the L2 flush, the gather and the timing events all on it.
+    # A dedicated stream: the forward, the L2 flush and the timing events all on it; with N > 1 the
+    # gather of step i runs on a second stream, overlapping step i + 1's forward.
     stream = torch.cuda.Stream()
+    gstream = torch.cuda.Stream() if gather else None
     torch.cuda.set_stream(stream)
     assert stream.cuda_stream != 0
+    fdone = [torch.cuda.Event(), torch.cuda.Event()]  # forward of the buffer's step finished
+    gdone = [torch.cuda.Event(), torch.cuda.Event()]  # gather of the buffer's step finished
 
-    def step():
-        model.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), B, T, maxL, d_out.data_ptr(), stream.cuda_stream)
+    def step(i):
+        buf = i % 2
         if gather is not None:
-            gather.step(d_out)
+            stream.wait_event(gdone[buf])  # step i - 2's gather has read this buffer
+        model.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), B, T, maxL, d_outs[buf].data_ptr(), stream.cuda_stream)
+        if gather is not None:
+            fdone[buf].record(stream)
+            with torch.cuda.stream(gstream):
+                gstream.wait_event(fdone[buf])
+                gather.step(d_outs[buf])
+                gdone[buf].record(gstream)
+
+    def join(i):
+        """Makes the main stream wait for step i's gather (every gather ends inside a timed step)."""
+        if gather is not None and i >= 0:
+            stream.wait_event(gdone[i % 2])
 
     # warm-up (also captures nothing: the device path launches directly)
-    for _ in range(max(a.warmup, 3)):
-        step()
+    for i in range(max(a.warmup, 3)):
+        step(i)
+        join(i)
     torch.cuda.synchronize()
 
     def timed_loop(clk=None):
@@ -400,7 +426,10 @@ def run_ours(a):
         for i in range(a.steps):
             flush.zero_()
             evs[i][0].record(stream)
-            step()
+            step(i)
+            join(i - 1)  # the previous step's gather ran under this forward; it closes in this window
+            if i == a.steps - 1:
+                join(i)
             evs[i][1].record(stream)
         if clk:
             clk.mark()
@@ -430,7 +459,9 @@ def run_ours(a):
     launches_per_fwd = int(sum(cls_n)) // nfwd
 
     # end to end through the public host API (graph replay inside; H2D of ids + cu from pinned host
-    # memory, as a serving pipeline stages them, and D2H of out into pinned host memory)
+    # memory, as a serving pipeline stages them, and D2H of the embeddings into pinned host memory).
+    # One GPU: tz_arctic_forward.  N GPUs: ShardedForward, whose call also gathers every rank's rows
+    # to rank 0 and copies the whole batch back there; wall time per call, max over ranks.
     def pinned(arr):  # a page-locked copy (the torch tensor owns it) and its numpy view of arr's dtype
         t = torch.empty(arr.shape, dtype=torch.int32, pin_memory=True)
         v = t.numpy().view(arr.dtype)
@@ -440,14 +471,22 @@ def run_ours(a):
     keep_cu, h_cu = pinned(np.ascontiguousarray(cu, dtype=np.int32))
     h_out_t = torch.empty((B, 384), dtype=torch.float32, pin_memory=True)
     host_out = h_out_t.numpy()
+    if world > 1:
+        from tenzor_b200.shard import ShardedForward
+        sharded = ShardedForward(ctx, model, mine, len(lens), T, stream=stream)
+        call = lambda: sharded.forward(h_ids, h_cu, maxL)
+    else:
+        call = lambda: model.forward_packed(h_ids, h_cu, out=host_out)
     for _ in range(3):
-        model.forward_packed(h_ids, h_cu, out=host_out)
+        call()
     e2e_t = 0.0
     for i in range(a.steps):
         flush.zero_()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
-        model.forward_packed(h_ids, h_cu, out=host_out)
+        call()
         e2e_t += time.perf_counter() - t0
     e2e_t_t = torch.tensor([e2e_t], device="cuda", dtype=torch.float64)
     if world > 1:
@@ -502,13 +541,16 @@ def run_ours(a):
         line = {
             "metric": arctic_metric(a.config, a.mode),
             "value": value, "unit": "seq/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms / a.steps, "higher_is_better": True,
+            "scaling": "strong" if a.config == "c4" else "weak", "vs_baseline": None,
             "dtype": "int8 (W8A8, int32 acc)" if int8 else ("f16 operands / f32 acc" if a.mode == "f32" else "int8 weights as f16 / f32 acc"),
             "data": "synthetic (seeded N(0,0.02) weights, U ids / lengths)",
             "config": {"workload": cfg["desc"] + (" per GPU" if world > 1 else ""), "model": "Arctic-embed-xs",
                        "mode": a.mode, "global_batch": int(len(lens)), "per_gpu_batch": B, "tokens_per_gpu": T,
                        "seq_len": cfg["seq"], "parallelism": f"sequence-sharded x{world}, gather to rank 0",
                        "l2": "flushed (256 MB write) before every timed step",
+                       "gather": "N > 1: step i's NCCL gather to rank 0 runs on a second stream under step i + 1's "
+                                 "forward and completes inside step i + 1's timed window (the last one inside the last)",
                        "useful_gflop_per_step": flop_useful(lens) / 1e9},
             "roofline": {"kernel": CLASS_NAMES[dom], "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "peak_source": peak_note, "traffic": tr,
@@ -517,7 +559,8 @@ def run_ours(a):
                          "class_ms_per_forward": {CLASS_NAMES[c]: round(cls_ms[c] / nfwd, 4) for c in range(9) if cls_n[c]},
                          "profiled_ms_per_step": ms_prof / a.steps},
             "e2e": {"value": e2e_value, "unit": "seq/s", "h2d_bytes_per_step": int(T * 4 + (B + 1) * 4),
-                    "d2h_bytes_per_step": int(B * 384 * 4)},
+                    "d2h_bytes_per_step": int(len(lens) * 384 * 4),
+                    "api": "tz_arctic_forward" if world == 1 else "tenzor_b200.shard.ShardedForward (forward + NCCL gather to rank 0 + D2H of the whole batch on rank 0)"},
             "gpu_launches": launches_per_fwd * a.steps,
             "clocks": clk.summary(),
         }

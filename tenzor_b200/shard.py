@@ -109,3 +109,43 @@ class RankGather:
             self.reorder(self.recv, self.perm, self.out)
             return self.out
         return None
+
+
+class ShardedForward:
+    """The multi-GPU host API of the sequence-sharded forward (one process per GPU; replaces
+    forwardBatchParallel's thread pool, arctic.zig:959-1013, with one model per GPU): each rank
+    passes its shard's packed ids and offsets in (pinned) host memory; the ids are copied to the
+    device, the rank's forward runs from its captured CUDA graph, the [n_r, 384] embeddings are
+    gathered to rank 0 in global batch order (RankGather: one NCCL gather + one row gather), and rank
+    0 copies the whole [total, 384] batch back to host memory.  Returns that array on rank 0, None
+    elsewhere.  Everything is enqueued on one stream; the call returns when its results are on the
+    host."""
+
+    def __init__(self, ctx, model, index: np.ndarray, total: int, max_tokens: int, stream=None):
+        import torch
+        from . import ops
+        dev = torch.device("cuda", ctx.device)
+        self.model = model
+        self.stream = stream or torch.cuda.Stream(dev)
+        self.gather = RankGather(index, total, 384, dev, lambda table, ids, out: ops.gather_rows(ctx, table, ids, out=out))
+        self.n = len(index)
+        self.d_ids = torch.empty(max(1, max_tokens), dtype=torch.int32, device=dev)
+        self.d_cu = torch.empty(self.n + 1, dtype=torch.int32, device=dev)
+        self.d_out = torch.zeros((self.gather.cap, 384), dtype=torch.float32, device=dev)
+        self.h_out = torch.empty((total, 384), dtype=torch.float32, pin_memory=True) if self.gather.rank == 0 else None
+
+    def forward(self, h_ids, h_cu, max_len: int):
+        """h_ids: packed uint32 ids of this rank's shard, h_cu: int32 offsets [n_r + 1] (numpy views of
+        page-locked memory for overlapped copies; pageable arrays work too)."""
+        import torch
+        T = int(h_cu[-1])
+        with torch.cuda.stream(self.stream):
+            self.d_ids[:T].copy_(torch.from_numpy(np.asarray(h_ids).view(np.int32)), non_blocking=True)
+            self.d_cu.copy_(torch.from_numpy(np.asarray(h_cu, np.int32)), non_blocking=True)
+            self.model.forward_device(self.d_ids.data_ptr(), self.d_cu.data_ptr(), self.n, T, max_len,
+                                      self.d_out.data_ptr(), self.stream.cuda_stream)
+            out = self.gather.step(self.d_out)
+            if out is not None:
+                self.h_out.copy_(out, non_blocking=True)
+        self.stream.synchronize()
+        return self.h_out.numpy() if self.h_out is not None else None

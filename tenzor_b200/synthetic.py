@@ -126,6 +126,19 @@ def token_batch(batch: int, seq: int, lmin: int, lmax: int, seed: int = 7):
     return ids, lens
 
 
+def token_batch_with_lengths(lens: np.ndarray, seq: int, seed: int):
+    """Padded ids [B, S] with the given valid lengths and their own seeded body ids (the token
+    distribution of token_batch): equal-work batches with different tokens."""
+    lens = np.asarray(lens, np.int32)
+    body = randint(seed * 2 + 2, len(lens) * seq, 1000, VOCAB - 1).reshape(len(lens), seq)
+    ids = np.zeros((len(lens), seq), np.uint32)
+    for b in range(len(lens)):
+        L = int(lens[b])
+        ids[b, 0] = CLS_ID
+        ids[b, 1:L] = body[b, 1:L]
+    return ids
+
+
 def pack(ids: np.ndarray, lens: np.ndarray):
     """Padded [B,S] ids + lengths -> (packed ids [T] uint32, cu_seqlens [B+1] int32)."""
     cu = np.zeros(len(lens) + 1, np.int32)
