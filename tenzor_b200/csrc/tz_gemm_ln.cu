@@ -10,15 +10,24 @@
 //
 // One CTA owns whole 128-row blocks (persistent over row blocks): the full 384-column accumulator
 // lives in TMEM (two N=192 MMAs per K step).  64 + 16*32 threads: warp 0 TMA producer (A block and
-// the two 192-row halves of W per 128-byte K block, 2-stage ring), warp 1 TMEM owner + MMA issuer,
-// warps 2..17 epilogue: warp w reads TMEM lane quarter (w % 4) and a 96-column slice.  Per row:
-// pass A dequantises, adds bias and residual, writes x back into TMEM and sums; pass B sums squared
+// the two 192-row halves of W per 128-byte K block), warp 1 TMEM owner + MMA issuer, warps 2..17
+// epilogue: warp w reads TMEM lane quarter (w % 4) and a 96-column slice.  Per row: pass A
+// dequantises, adds bias and residual, writes x back into TMEM and sums; pass B sums squared
 // deviations; pass C normalises and stores x_out (+ f16 aux, or y back to TMEM and |max|); pass D
 // (AUX = 1) quantises.  The residual stream is in the blocked layout of xblk (tz_internal.h): a
-// warp's 32 x 16 residual chunk is 2 KB contiguous and arrives by one 1-D bulk copy (two in flight
-// per warp), and its x_out chunk leaves as four coalesced 512-byte stores.  The four slices of a row combine their partial sums through shared memory
-// at mbarriers (bounded waits, one phase per tile).  No separate LayerNorm launch and no round trip
-// of the pre-LN activations.
+// warp's 32 x 16 residual chunk is 2 KB contiguous, and its x_out chunk leaves as four coalesced
+// 512-byte stores.  The four slices of a row combine their partial sums through shared memory at
+// mbarriers (bounded waits, one phase per tile).  No separate LayerNorm launch and no round trip of
+// the pre-LN activations.
+//
+// Two shared-memory layouts (Layout<AQ>):
+//  * TMA-fed A (AQ = 0: the f16-operand modes): a 3-stage ring, so a K block's weight tile is
+//    requested two MMA blocks ahead and its L2 latency hides under the MMAs; the residual chunks are
+//    read with coalesced direct loads (the warp's 12 KB slice prefetched into L2 at the tile's start).
+//  * A quantised in the kernel (AQ = 1, W8A8): the mainloop is paced by the quantising epilogue
+//    warps, not the weight loads, so a 2-stage ring suffices and the freed 64 KB stage residual
+//    chunks (1-D bulk copies, two in flight per warp, the first two during the mainloop) and the
+//    int8 output blocks (one TMA store per warp).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -30,7 +39,7 @@
 namespace tz {
 namespace {
 
-constexpr int kN = 384, kHalf = 192, kStages = 2, kEpiWarps = 16, kThreads = 64 + 32 * kEpiWarps;
+constexpr int kN = 384, kHalf = 192, kEpiWarps = 16, kThreads = 64 + 32 * kEpiWarps;
 constexpr int kBox = 32 * 16 * 4;  // one 32-row x 16-column f32 chunk of the residual (2 KB, contiguous in xblk form)
 constexpr int kSlice = kN / 4;  // 96 columns per epilogue warp
 
@@ -53,16 +62,18 @@ struct LnParams {
     float* dbg_as;        // AQ parity capture (or null): their per-token scales [M]
 };
 
-template <int KIND>
+template <int KIND, int AQ>
 struct LnCfg {
     static constexpr int ELEM = KIND == KIND_I8 ? 1 : (KIND == KIND_TF32 ? 4 : 2);
     static constexpr int BK = 128 / ELEM;
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = kN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGING = kEpiWarps * 2 * kBox;  // two residual/output boxes per epilogue warp
+    static constexpr bool BOXES = AQ != 0;  // residual / int8 output staged in shared memory
+    static constexpr int STAGES = BOXES ? 2 : 3;
+    static constexpr int STAGING = BOXES ? kEpiWarps * 2 * kBox : 0;  // two residual/output boxes per epilogue warp
     static constexpr int RED_BYTES = 3 * 4 * 128 * 4 + 4 * kN * 4;  // row reductions + the 4 column vectors
-    static constexpr int SMEM = kStages * STAGE_BYTES + STAGING + RED_BYTES + 512 + 1024;  // + barriers, alignment
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + RED_BYTES + 512 + 1024;  // + barriers, alignment
     static_assert(SMEM <= 227 * 1024, "shared memory");
     static_assert((kSlice / 16) % 2 == 0, "x_out chunks are stored in pairs");
     static_assert(32 * kSlice <= 2 * kBox, "the int8 LayerNorm output of one warp fits its two staging boxes");
@@ -94,7 +105,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmAux, int M, int K,
                    LnParams p, int* status) {
-    using C = LnCfg<KIND>;
+    using C = LnCfg<KIND, AQ>;
+    constexpr int kStages = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = tzp::smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -112,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tempty = tfull + 1;
     uint64_t* drain = tempty + 1;
     uint64_t* red_bar = drain + 1;  // [3]: the epilogue warps' row reductions (sum, ssq, max)
-    uint64_t* res_bar = red_bar + 3;  // [16 warps][2 boxes]: residual tile arrivals
+    uint64_t* res_bar = red_bar + 3;  // [16 warps][2 boxes] (BOXES): residual tile arrivals
     uint64_t* afull = res_bar + 2 * kEpiWarps;  // [kStages] (AQ): A stage quantised by all epilogue threads
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afull + kStages);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -128,7 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tzp::mbar_init(tempty, kEpiWarps);
         tzp::mbar_init(drain, 1);
         for (int i = 0; i < 3; ++i) tzp::mbar_init(&red_bar[i], kEpiWarps);
-        for (int i = 0; i < 2 * kEpiWarps; ++i) tzp::mbar_init(&res_bar[i], 1);
+        if (C::BOXES)
+            for (int i = 0; i < 2 * kEpiWarps; ++i) tzp::mbar_init(&res_bar[i], 1);
         for (int s = 0; s < kStages; ++s) tzp::mbar_init(&afull[s], 32 * kEpiWarps);
         *abort_flag = 0;
         tzp::fence_mbar_init();
@@ -259,15 +272,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t cphase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int row0 = tile * 128 + q * 32;
-            // residual boxes of chunks 0 and 1 (the boxes' previous TMA stores must have read them)
-            if (lane == 0) {
-                tzp::bulk_wait_read<0>();
-                for (int b = 0; b < 2; ++b) {
-                    tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
-                    tzp::bulk_load_1d(box[b], p.residual + xblk(row0, c0 + 16 * b), kBox, &rbar[b]);
+            if constexpr (C::BOXES) {
+                // residual boxes of chunks 0 and 1 (the boxes' previous TMA stores must have read them)
+                if (lane == 0) {
+                    tzp::bulk_wait_read<0>();
+                    for (int b = 0; b < 2; ++b) {
+                        tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
+                        tzp::bulk_load_1d(box[b], p.residual + xblk(row0, c0 + 16 * b), kBox, &rbar[b]);
+                    }
                 }
+                __syncwarp();
+            } else {
+                // this warp's residual slice (32 rows x 96 columns, 12 KB contiguous) into L2 during the mainloop
+                if (lane == 0) tzp::bulk_prefetch_l2(p.residual + xblk(row0, c0), 32 * kSlice * 4);
             }
-            __syncwarp();
             if constexpr (AQ) {
                 // ---- quantise this tile's A rows into the int8 stages ----
                 // Thread t: row t / 4 of the tile, 32 columns (64 bytes of f16) at (t % 4) * 32 of
@@ -371,25 +389,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t rs2 = tzp::f2_pack(rs, rs);
             uint64_t sum2 = 0;  // (even columns, odd columns)
             bool bad = false;
+            const float* resw = p.residual + xblk(row0, c0) + lane * 4;  // !BOXES: quad 0 of chunk 0, this row
 #pragma unroll
             for (int c = 0; c < kSlice / 16; ++c) {
                 const int b = c & 1;
                 uint32_t r[16];
                 tzp::tmem_ld16(tbase + 16 * c, r);
-                if (!tzp::mbar_wait(&rbar[b], (rph >> b) & 1u, status, nullptr)) {
-                    tzp::tmem_ld_wait();
-                    bad = true;
-                    break;
-                }
-                rph ^= 1u << b;
-                float4 cur[4];  // this row's 16 residual values (64-byte swizzle of the TMA box)
+                float4 cur[4];  // this row's 16 residual values
+                if constexpr (C::BOXES) {
+                    if (!tzp::mbar_wait(&rbar[b], (rph >> b) & 1u, status, nullptr)) {
+                        tzp::tmem_ld_wait();
+                        bad = true;
+                        break;
+                    }
+                    rph ^= 1u << b;
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    cur[j] = *reinterpret_cast<const float4*>(box[b] + j * 512 + lane * 16);  // quad j, this row
-                __syncwarp();
-                if (lane == 0 && c + 2 < kSlice / 16) {  // refill this box with chunk c + 2
-                    tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
-                    tzp::bulk_load_1d(box[b], p.residual + xblk(row0, c0 + 16 * (c + 2)), kBox, &rbar[b]);
+                    for (int j = 0; j < 4; ++j)
+                        cur[j] = *reinterpret_cast<const float4*>(box[b] + j * 512 + lane * 16);  // quad j, this row
+                    __syncwarp();
+                    if (lane == 0 && c + 2 < kSlice / 16) {  // refill this box with chunk c + 2
+                        tzp::mbar_arrive_expect_tx(&rbar[b], kBox);
+                        tzp::bulk_load_1d(box[b], p.residual + xblk(row0, c0 + 16 * (c + 2)), kBox, &rbar[b]);
+                    }
+                } else {
+                    // quad j of the blocked chunk, lane = row: each quad one coalesced 512-byte load
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) cur[j] = *reinterpret_cast<const float4*>(resw + c * 512 + j * 128);
                 }
                 tzp::tmem_ld_wait();
                 const int col = c0 + 16 * c;
@@ -550,7 +575,8 @@ CUtensorMapDataType dtype_of(int kind) {
 
 template <int KIND, int AUX, int AQ = 0>
 int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
-    using C = LnCfg<KIND>;
+    using C = LnCfg<KIND, AQ>;
+    static_assert(AUX == 0 || C::BOXES, "the int8 output is staged in the residual boxes");
     auto kern = gemm_ln_kernel<KIND, AUX, AQ>;
     static unsigned attr_set = 0;
     int dev = 0;
@@ -604,8 +630,9 @@ int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
                  "gemm_ln: in-kernel A quantisation needs K %% 128 == 0 and 16-byte aligned f16 rows (K=%d)", g.K);
         return launch_ln_impl<KIND_I8, 1, 1>(ctx, g, s);
     }
-    if (g.kind == KIND_I8) return g.aux_int8 ? launch_ln_impl<KIND_I8, 1>(ctx, g, s) : launch_ln_impl<KIND_I8, 0>(ctx, g, s);
-    if (g.kind == KIND_F16) return g.aux_int8 ? launch_ln_impl<KIND_F16, 1>(ctx, g, s) : launch_ln_impl<KIND_F16, 0>(ctx, g, s);
+    TZ_CHECK(!g.aux_int8, TZ_EUNSUPPORTED, "gemm_ln: the int8 LayerNorm output needs the in-kernel A quantisation");
+    if (g.kind == KIND_I8) return launch_ln_impl<KIND_I8, 0>(ctx, g, s);
+    if (g.kind == KIND_F16) return launch_ln_impl<KIND_F16, 0>(ctx, g, s);
     return fail(TZ_EUNSUPPORTED, "gemm_ln: kind %d", g.kind);
 }
 

@@ -135,6 +135,12 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* s
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) of global memory into L2 (no completion
+// to wait for: a hint).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes)
+                 : "memory");
+}
 // Wait until at most N bulk groups of this thread are still reading shared memory.
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() {
