@@ -367,7 +367,7 @@ def run_ours(a):
     ctx = Context(local)
     w = S.arctic_weights(1234)
     ck = quantize_checkpoint(ctx, w) if a.mode != "f32" else w
-    model = ArcticModel.from_checkpoint(ctx, ck, a.mode)
+    model = ArcticModel.from_checkpoint(ctx, ck, a.mode, prec=a.prec)
 
     ids, lens, shards = make_inputs(a.config, world)
     mine = shards[rank]
@@ -543,7 +543,8 @@ def run_ours(a):
             "value": value, "unit": "seq/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": ms / a.steps, "higher_is_better": True,
             "scaling": "strong" if a.config == "c4" else "weak", "vs_baseline": None,
-            "dtype": "int8 (W8A8, int32 acc)" if int8 else ("f16 operands / f32 acc" if a.mode == "f32" else "int8 weights as f16 / f32 acc"),
+            "dtype": "int8 (W8A8, int32 acc)" if int8 else (f"{a.prec} operands / f32 acc" if a.mode == "f32"
+                                                             else f"int8 weights as {a.prec} / f32 acc"),
             "data": "synthetic (seeded N(0,0.02) weights, U ids / lengths)",
             "config": {"workload": cfg["desc"] + (" per GPU" if world > 1 else ""), "model": "Arctic-embed-xs",
                        "mode": a.mode, "global_batch": int(len(lens)), "per_gpu_batch": B, "tokens_per_gpu": T,
@@ -855,6 +856,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=list(CONFIGS))
     ap.add_argument("--mode", default="w8a8", choices=["w8a8", "w8a32", "f32"])
+    ap.add_argument("--prec", default="f16", choices=["f16", "bf16"],
+                    help="16-bit GEMM operand type of the f32 / w8a32 modes")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--micro", action="store_true", help="configs[2] fused-op microbenchmarks (one line each)")
     ap.add_argument("--model", default="arctic", choices=["arctic", "lenet"])

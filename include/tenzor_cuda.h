@@ -104,6 +104,16 @@ typedef struct {
  * Linear weight and the word / position tables; the 768-element type table stays f32).
  * Replaces ModelWeights.fromSafeTensors, arctic.zig:113-166 / getMatWeightAlloc 258-287. */
 int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_t* out);
+/* GEMM operand precision of the f16-operand modes (TZ_QUANT_F32 and TZ_QUANT_W8A32): the 16-bit type
+ * of every weight copy, GEMM operand and intermediate activation (QKV, attention and GELU outputs) of
+ * the forward; accumulation, LayerNorm, softmax statistics and the residual stream stay f32.
+ * TZ_PREC_BF16 trades three mantissa bits for f32's exponent range (checkpoints whose activations
+ * exceed the f16 range).  W8A8 runs int8 GEMMs and takes only TZ_PREC_F16.  The op-level f32 GEMMs
+ * offer the f32-accurate split-tf32 form (tz_matmul_f32x3); the model does not. */
+typedef enum { TZ_PREC_F16 = 0, TZ_PREC_BF16 = 1 } tz_gemm_prec;
+/* tz_arctic_load with an explicit GEMM precision (tz_arctic_load is prec = TZ_PREC_F16);
+ * TZ_EUNSUPPORTED for a precision the mode does not run. */
+int tz_arctic_load_ex(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, int prec, tz_model_t* out);
 /* Same, reading a safetensors checkpoint (f32, or I8 + '<name>.scale' F16 as written by
  * quantize_arctic_xs.zig), with or without the "bert." prefix.  safetensors.zig:275-295. */
 int tz_arctic_load_safetensors(tz_ctx_t ctx, const char* path, int mode, tz_model_t* out);

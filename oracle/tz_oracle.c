@@ -581,6 +581,12 @@ static void emb_row(float* dst, const float* wf, const int8_t* wq, const uint16_
     }
 }
 
+/* Rounds n values to IEEE half and back: the W8A8 scheme stores Q / K / V, the attention output and
+ * the GELU output as f16 before they are used (and, for the latter two, quantised per token). */
+static void round_f16(float* x, size_t n) {
+    for (size_t i = 0; i < n; i++) x[i] = tzo_f16_to_f32(tzo_f32_to_f16(x[i]));
+}
+
 /* selfAttention, arctic.zig:639-747. */
 static void self_attention(int mode, const tzo_layer* lw, float* out, const float* in,
                            scratch_t* s, int L) {
@@ -590,6 +596,7 @@ static void self_attention(int mode, const tzo_layer* lw, float* out, const floa
     linear(mode, in, lw->q_w, lw->q_q, lw->q_s, lw->q_b, q, L, H, H);
     linear(mode, in, lw->k_w, lw->k_q, lw->k_s, lw->k_b, k, L, H, H);
     linear(mode, in, lw->v_w, lw->v_q, lw->v_s, lw->v_b, v, L, H, H);
+    if (mode == TZO_MODE_W8A8) round_f16(s->qkv, (size_t)3 * L * H);
     const float scale = 1.0f / sqrtf(32.0f);
     for (int h = 0; h < TZO_HEADS; h++) {
         int off = h * 32;
@@ -616,6 +623,7 @@ static void self_attention(int mode, const tzo_layer* lw, float* out, const floa
         for (int t = 0; t < L; t++)
             memcpy(s->attn_out + (size_t)t * H + off, s->oh + t * 32, 32 * sizeof(float));
     }
+    if (mode == TZO_MODE_W8A8) round_f16(s->attn_out, (size_t)L * H);
     linear(mode, s->attn_out, lw->o_w, lw->o_q, lw->o_s, lw->o_b, s->tmp, L, H, H);
     for (int i = 0; i < L * H; i++) out[i] = in[i] + s->tmp[i];
     tzo_layernorm_rows(out, lw->ln1_g, lw->ln1_b, out, L, H, EPS);
@@ -626,6 +634,7 @@ static void feed_forward(int mode, const tzo_layer* lw, float* out, const float*
                          int L) {
     linear(mode, in, lw->ffn1_w, lw->ffn1_q, lw->ffn1_s, lw->ffn1_b, s->ffn, L, H, F);
     for (int i = 0; i < L * F; i++) s->ffn[i] = tzo_gelu_model(s->ffn[i]);
+    if (mode == TZO_MODE_W8A8) round_f16(s->ffn, (size_t)L * F);
     linear(mode, s->ffn, lw->ffn2_w, lw->ffn2_q, lw->ffn2_s, lw->ffn2_b, s->tmp, L, F, H);
     for (int i = 0; i < L * H; i++) out[i] = in[i] + s->tmp[i];
     tzo_layernorm_rows(out, lw->ln2_g, lw->ln2_b, out, L, H, EPS);

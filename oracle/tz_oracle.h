@@ -33,7 +33,8 @@ extern "C" {
 /* forward modes */
 #define TZO_MODE_F32 0   /* all-f32 forward, arctic.zig:874-898 */
 #define TZO_MODE_W8A32 1 /* int8 weights, f32 activations, matmul_w8a32.zig:14-58 */
-#define TZO_MODE_W8A8 2  /* builder-defined: per-token int8 activations, int32 accumulate */
+#define TZO_MODE_W8A8 2  /* builder-defined: per-token int8 activations, int32 accumulate; Q / K / V,
+                          * the attention output and the GELU output held in f16 */
 
 /* One transformer layer.  Matrices are PyTorch-layout [out, in] row-major.
  * f32 mode uses the *_w pointers; the int8 modes use *_q (int8) + *_s (IEEE half bits). */

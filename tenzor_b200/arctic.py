@@ -21,6 +21,7 @@ import numpy as np
 from . import _lib as L
 from .runtime import Context
 
+PRECS = {"f16": 0, "bf16": 1}
 MODES = {"f32": L.QUANT_F32, "w8a32": L.QUANT_W8A32, "w8a8": L.QUANT_W8A8}
 
 
@@ -122,10 +123,12 @@ class ArcticModel:
         ctx._adopt(self)
 
     @classmethod
-    def from_checkpoint(cls, ctx: Context, ckpt: dict, mode: str = "f32") -> "ArcticModel":
+    def from_checkpoint(cls, ctx: Context, ckpt: dict, mode: str = "f32", prec: str = "f16") -> "ArcticModel":
+        """`prec` is the 16-bit GEMM operand / activation type of the f32 and w8a32 modes: "f16" or
+        "bf16" (tz_arctic_load_ex)."""
         hw = _HostWeights(ckpt)
         h = C.c_void_p()
-        L.check(L.lib().tz_arctic_load(ctx.handle, C.byref(hw.struct), MODES[mode], C.byref(h)))
+        L.check(L.lib().tz_arctic_load_ex(ctx.handle, C.byref(hw.struct), MODES[mode], PRECS[prec], C.byref(h)))
         return cls(ctx, h, mode)
 
     @classmethod

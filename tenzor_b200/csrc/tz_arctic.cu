@@ -35,9 +35,11 @@
 
 namespace tz {
 int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const int* cu_seqlens, int batch, int max_len,
-                     void* out, unsigned* row_absmax, cudaStream_t s, bool pdl);
+                     void* out, unsigned* row_absmax, cudaStream_t s, bool pdl, bool bf16);
 int launch_f32_to_f16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s);
 int launch_i8_to_f16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s);
+int launch_f32_to_bf16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s);
+int launch_i8_to_bf16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s);
 int launch_f16bits_to_f32(tz_ctx_t ctx, const uint16_t* x, float* y, long long n, cudaStream_t s);
 
 namespace {
@@ -45,7 +47,7 @@ namespace {
 constexpr int kH = 384, kF = 1536, kV = 30522, kP = 512, kLayers = 6;
 constexpr float kEps = 1e-12f;  // arctic.zig:37
 
-// AUX: 0 = f16 copy, 1 = int8 + per-token scale.
+// AUX: 0 = f16 copy, 1 = int8 + per-token scale, 2 = bf16 copy.
 template <int AUX>
 // LayerNorm of one row held as 12 values per lane (columns lane*4 + 128c .. +3); the f32 result
 // goes to `xrow` (a 384-float shared-memory row whose 16-byte quads are XOR-swizzled by row % 8, so
@@ -78,14 +80,14 @@ __device__ __forceinline__ void ln_finish_row(float (&v)[12], const float* __res
             make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[4 * c]), fabsf(v[4 * c + 1])), fmaxf(fabsf(v[4 * c + 2]), fabsf(v[4 * c + 3]))));
     }
-    if constexpr (AUX == 0) {
-        __half* a = static_cast<__half*>(aux) + row * kH;
+    if constexpr (AUX == 0 || AUX == 2) {
+        uint16_t* a = static_cast<uint16_t*>(aux) + row * kH;
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             const int col = c * 128 + lane * 4;
             uint2 pk;
-            pk.x = tzp::pack_half2(v[4 * c], v[4 * c + 1]);
-            pk.y = tzp::pack_half2(v[4 * c + 2], v[4 * c + 3]);
+            pk.x = tzp::pack16x2<AUX == 2>(v[4 * c], v[4 * c + 1]);
+            pk.y = tzp::pack16x2<AUX == 2>(v[4 * c + 2], v[4 * c + 3]);
             *reinterpret_cast<uint2*>(a + col) = pk;
         }
     } else {
@@ -308,6 +310,9 @@ struct tz_model_s {
     tz_ctx_t ctx = nullptr;
     int device = 0;
     int mode = TZ_QUANT_F32;
+    // TZ_PREC_BF16: the f16-operand modes (F32, W8A32) run every 16-bit tensor of the forward --
+    // weight copies, GEMM operands, QKV, attention and GELU outputs -- in bf16 instead of IEEE half
+    bool bf16 = false;
     // int8 mode from an f32 checkpoint: the weights quantize_arctic_xs.zig would quantise are
     // quantised on the device during the load (GPU row quantiser, same rounding)
     bool quantize_on_load = false;
@@ -456,8 +461,9 @@ int upload_linear(tz_model_s* m, const tz_mat_weight& w, int rows, int cols, voi
         TZ_CUDA(cudaMalloc(&tmp, sizeof(float) * rows * cols));
         int rc = h2d(m, tmp, w.f32, sizeof(float) * rows * cols);
         if (!rc)
-            rc = launch_f32_to_f16(m->ctx, static_cast<float*>(tmp), static_cast<__half*>(dst) + static_cast<long long>(row0) * cols,
-                                   static_cast<long long>(rows) * cols, s);
+            rc = (m->bf16 ? launch_f32_to_bf16 : launch_f32_to_f16)(m->ctx, static_cast<float*>(tmp),
+                                                                   static_cast<uint16_t*>(dst) + static_cast<long long>(row0) * cols,
+                                                                   static_cast<long long>(rows) * cols, s);
         cudaStreamSynchronize(s);
         cudaFree(tmp);
         return rc;
@@ -477,9 +483,10 @@ int upload_linear(tz_model_s* m, const tz_mat_weight& w, int rows, int cols, voi
         if (m->mode == TZ_QUANT_W8A8)
             TZ_CUDA(cudaMemcpyAsync(static_cast<int8_t*>(dst) + static_cast<long long>(row0) * cols, tq,
                                     static_cast<size_t>(rows) * cols, cudaMemcpyDeviceToDevice, s));
-        else  // W8A32: int8 values widened exactly to f16; the scale is applied in the epilogue
-            rc = launch_i8_to_f16(m->ctx, static_cast<int8_t*>(tq), static_cast<__half*>(dst) + static_cast<long long>(row0) * cols,
-                                  static_cast<long long>(rows) * cols, s);
+        else  // W8A32: int8 values widened exactly to f16 (bf16); the scale is applied in the epilogue
+            rc = (m->bf16 ? launch_i8_to_bf16 : launch_i8_to_f16)(m->ctx, static_cast<int8_t*>(tq),
+                                                                 static_cast<uint16_t*>(dst) + static_cast<long long>(row0) * cols,
+                                                                 static_cast<long long>(rows) * cols, s);
     }
     cudaStreamSynchronize(s);
     cudaFree(tq);
@@ -652,8 +659,8 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
                            static_cast<long long>(T), m->emb, (const float*)m->emb_g,
                            (const float*)m->emb_b, m->X, m->XA, m->xs, ctx->d_status);
     else
-        rc = launch_kernel(embed_ln_kernel<0>, dim3(static_cast<unsigned>((T + 31) / 32)), dim3(256), 0, s, pdl, d_ids, d_cu, B,
-                           static_cast<long long>(T), m->emb, (const float*)m->emb_g,
+        rc = launch_kernel(m->bf16 ? embed_ln_kernel<2> : embed_ln_kernel<0>, dim3(static_cast<unsigned>((T + 31) / 32)), dim3(256), 0,
+                           s, pdl, d_ids, d_cu, B, static_cast<long long>(T), m->emb, (const float*)m->emb_g,
                            (const float*)m->emb_b, m->X, m->XA, (float*)nullptr, ctx->d_status);
     if (rc) return rc;
     if (m->keep_stages)
@@ -662,11 +669,12 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         const DevLayer& L = m->layers[l];
         GemmArgs g;
         g.pdl = pdl;
-        g.kind = q8 ? KIND_I8 : KIND_F16;
+        g.kind = q8 ? KIND_I8 : (m->bf16 ? KIND_BF16 : KIND_F16);
+        const int out16 = m->bf16 ? OUT_BF16 : OUT_F16;
         // QKV projection (3 linearProjection calls of selfAttention fused into one N=1152 GEMM)
         g.a = m->XA; g.lda = kH; g.b = L.wqkv; g.ldb = kH; g.M = M; g.N = 3 * kH; g.K = kH;
         g.bias = L.bqkv; g.col_scale = wscale ? L.sqkv : nullptr; g.row_scale = q8 ? m->xs : nullptr;
-        g.out = m->QKV; g.ldo = 3 * kH; g.out_type = OUT_F16;
+        g.out = m->QKV; g.ldo = 3 * kH; g.out_type = out16;
         const bool cap = q8 && l == 0 && m->keep_stages && m->d_acc[0];  // W8A8 layer-0 parity capture
         if (cap) g.dbg_acc = m->d_acc[0];
         if (l == 0 && (rc = keep_operand(m, 0, m->XA, m->xs, T, kH, s))) return rc;
@@ -676,7 +684,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         // attention
         // W8A8: the f16 attention output (with each row's |max|) goes through the (still free) H
         // buffer; the output projection quantises it per token inside its own kernel.
-        if ((rc = launch_attention(ctx, m->QKV, T, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s, pdl)))
+        if ((rc = launch_attention(ctx, m->QKV, T, d_cu, B, maxL, q8 ? m->Hh : m->OA, q8 ? m->omax : nullptr, s, pdl, m->bf16)))
             return rc;
         if (cap)  // the f16 attention output the next kernel quantises in its mainloop
             TZ_CUDA(cudaMemcpyAsync(m->d_in16[1], m->Hh, sizeof(__half) * T * kH, cudaMemcpyDeviceToDevice, s));
@@ -687,7 +695,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         o.a = q8 ? m->Hh : m->OA; o.lda = kH; o.b = L.wo; o.ldb = kH; o.M = M; o.K = kH;
         o.bias = L.bo; o.col_scale = wscale ? L.so : nullptr; o.a_absmax = q8 ? m->omax : nullptr;
         o.residual = m->X; o.gamma = L.ln1g; o.beta = L.ln1b; o.eps = kEps;
-        o.x_out = m->X; o.aux = m->XA; o.aux_scale = q8 ? m->xs : nullptr; o.aux_int8 = q8;
+        o.x_out = m->X; o.aux = m->XA; o.aux_scale = q8 ? m->xs : nullptr; o.aux_int8 = q8; o.aux_bf16 = m->bf16;
         if (cap) {
             o.dbg_acc = m->d_acc[1];
             o.dbg_aq = m->d_opq[1];
@@ -704,7 +712,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         f1.kind = g.kind;
         f1.a = m->XA; f1.lda = kH; f1.b = L.w1; f1.ldb = kH; f1.M = M; f1.N = kF; f1.K = kH;
         f1.bias = L.b1; f1.col_scale = wscale ? L.s1 : nullptr; f1.row_scale = q8 ? m->xs : nullptr;
-        f1.gelu = 1; f1.out = m->Hh; f1.ldo = kF; f1.out_type = OUT_F16; f1.row_absmax = q8 ? m->hmax : nullptr;
+        f1.gelu = 1; f1.out = m->Hh; f1.ldo = kF; f1.out_type = out16; f1.row_absmax = q8 ? m->hmax : nullptr;
         if (cap) f1.dbg_acc = m->d_acc[2];
         if (l == 0 && (rc = keep_operand(m, 2, m->XA, m->xs, T, kH, s))) return rc;
         if ((rc = prof_mark(m, P_FFN1, s))) return rc;
@@ -719,7 +727,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         f2.a = m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.K = kF;
         f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.a_absmax = q8 ? m->hmax : nullptr;
         f2.residual = m->X; f2.gamma = L.ln2g; f2.beta = L.ln2b; f2.eps = kEps;
-        f2.x_out = m->X; f2.aux = m->XA; f2.aux_scale = q8 ? m->xs : nullptr; f2.aux_int8 = q8;
+        f2.x_out = m->X; f2.aux = m->XA; f2.aux_scale = q8 ? m->xs : nullptr; f2.aux_int8 = q8; f2.aux_bf16 = m->bf16;
         if (cap) {
             f2.dbg_acc = m->d_acc[3];
             f2.dbg_aq = m->d_opq[3];
@@ -876,14 +884,23 @@ int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, f
 extern "C" {
 
 int tz_arctic_load(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, tz_model_t* out) {
+    return tz_arctic_load_ex(ctx, w, mode, TZ_PREC_F16, out);
+}
+
+int tz_arctic_load_ex(tz_ctx_t ctx, const tz_arctic_weights* w, int mode, int prec, tz_model_t* out) {
     TZ_CHECK(ctx && w && out, TZ_EINVAL, "tz_arctic_load: null argument");
     TZ_CHECK(mode >= TZ_QUANT_F32 && mode <= TZ_QUANT_W8A8, TZ_EINVAL, "tz_arctic_load: bad mode %d", mode);
+    TZ_CHECK(prec == TZ_PREC_F16 || prec == TZ_PREC_BF16, TZ_EUNSUPPORTED,
+             "tz_arctic_load: GEMM precision %d is not provided for the model (TZ_PREC_F16, TZ_PREC_BF16)", prec);
+    TZ_CHECK(prec == TZ_PREC_F16 || mode != TZ_QUANT_W8A8, TZ_EUNSUPPORTED,
+             "tz_arctic_load: W8A8 runs int8 GEMMs; the 16-bit precision applies to the F32 and W8A32 modes");
     *out = nullptr;
     TZ_CUDA(cudaSetDevice(ctx->device));
     auto m = std::make_unique<tz_model_s>();
     m->ctx = ctx;
     m->device = ctx->device;
     m->mode = mode;
+    m->bf16 = prec == TZ_PREC_BF16;
     m->quantize_on_load = mode != TZ_QUANT_F32 && w->layers[0].query.f32 && !w->layers[0].query.q8;
     int rc = TZ_OK;
     auto fail_cleanup = [&](int code) {

@@ -41,7 +41,7 @@ __device__ __forceinline__ uint32_t kv_off(int row, int chunk) {
 // the online-softmax update, then O += P V.  MASK = the block runs past the sequence's last key.
 // Scores stay in raw units (m0/m1 are raw maxima); the 1/sqrt(32)*log2(e) scale and the max are
 // applied by one FMA inside the exponent, which is exact in order: the scale is positive.
-template <int NCH, bool MASK>
+template <int NCH, bool MASK, bool BF>
 __device__ __forceinline__ void attend_block(int kb, int L, uint32_t kaddr, uint32_t vaddr, const uint32_t (&qa)[2][4],
                                              float (&o)[4][4], float& m0, float& m1, float& l0, float& l1, int lane) {
     constexpr float sl2 = 0.17677669529663687f * 1.4426950408889634f;  // 1/sqrt(32) * log2(e)
@@ -53,8 +53,8 @@ __device__ __forceinline__ void attend_block(int kb, int L, uint32_t kaddr, uint
         s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
         uint32_t bk[4];
         tzp::ldmatrix_x4(bk, kaddr + kv_off(kb + 8 * j + (lane & 7), mi));
-        tzp::mma_f16_16816(s[j], qa[0], bk[0], bk[1]);
-        tzp::mma_f16_16816(s[j], qa[1], bk[2], bk[3]);
+        tzp::mma16_16816<BF>(s[j], qa[0], bk[0], bk[1]);
+        tzp::mma16_16816<BF>(s[j], qa[1], bk[2], bk[3]);
     }
     if (MASK) {
 #pragma unroll
@@ -100,16 +100,16 @@ __device__ __forceinline__ void attend_block(int kb, int L, uint32_t kaddr, uint
 #pragma unroll
     for (int kk = 0; kk < NCH; ++kk) {
         uint32_t a[4];
-        a[0] = tzp::pack_half2(s[2 * kk][0], s[2 * kk][1]);
-        a[1] = tzp::pack_half2(s[2 * kk][2], s[2 * kk][3]);
-        a[2] = tzp::pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        a[3] = tzp::pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        a[0] = tzp::pack16x2<BF>(s[2 * kk][0], s[2 * kk][1]);
+        a[1] = tzp::pack16x2<BF>(s[2 * kk][2], s[2 * kk][3]);
+        a[2] = tzp::pack16x2<BF>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        a[3] = tzp::pack16x2<BF>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
         for (int jd = 0; jd < 2; ++jd) {
             uint32_t bv[4];
             tzp::ldmatrix_x4_trans(bv, vaddr + kv_off(kb + 16 * kk + (mi & 1) * 8 + (lane & 7), 2 * jd + (mi >> 1)));
-            tzp::mma_f16_16816(o[2 * jd], a, bv[0], bv[1]);
-            tzp::mma_f16_16816(o[2 * jd + 1], a, bv[2], bv[3]);
+            tzp::mma16_16816<BF>(o[2 * jd], a, bv[0], bv[1]);
+            tzp::mma16_16816<BF>(o[2 * jd + 1], a, bv[2], bv[3]);
         }
     }
 }
@@ -124,6 +124,7 @@ __device__ __forceinline__ bool chunk_wait(uint64_t* bar, int* status) {
 // Sequences of up to 128 keys: CTA = (64-query block, head, sequence), 4 warps x 16 query rows; the
 // whole K / V of the sequence and the Q rows complete one mbarrier.  80 registers: 6 CTAs (24 warps)
 // per SM.
+template <bool BF>
 __global__ void __launch_bounds__(128)
     attention_short_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmQKV64,
                      const int* __restrict__ cu_seqlens, int lpad,
@@ -205,12 +206,12 @@ __global__ void __launch_bounds__(128)
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
     int kb = 0;
-    for (; kb + 64 <= L; kb += 64) attend_block<4, false>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane);
+    for (; kb + 64 <= L; kb += 64) attend_block<4, false, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane);
     switch ((L - kb + 15) >> 4) {  // the ragged tail, in 16-key chunks
-        case 1: attend_block<1, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
-        case 2: attend_block<2, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
-        case 3: attend_block<3, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
-        case 4: attend_block<4, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        case 1: attend_block<1, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        case 2: attend_block<2, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        case 3: attend_block<3, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+        case 4: attend_block<4, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
         default: break;
     }
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -223,8 +224,8 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int jd = 0; jd < 4; ++jd) {
         const int col = h * kHd + 8 * jd + cq;
-        const uint32_t p0 = tzp::pack_half2(o[jd][0] * inv0, o[jd][1] * inv0);
-        const uint32_t p1 = tzp::pack_half2(o[jd][2] * inv1, o[jd][3] * inv1);
+        const uint32_t p0 = tzp::pack16x2<BF>(o[jd][0] * inv0, o[jd][1] * inv0);
+        const uint32_t p1 = tzp::pack16x2<BF>(o[jd][2] * inv1, o[jd][3] * inv1);
         if (r0 < L) *reinterpret_cast<uint32_t*>(out + static_cast<long long>(seq0 + r0) * kHidden + col) = p0;
         if (r1 < L) *reinterpret_cast<uint32_t*>(out + static_cast<long long>(seq0 + r1) * kHidden + col) = p1;
         if (row_absmax) {
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(128)
 // 0 also carries Q): the warps start on the first keys while the later chunks are still in flight.
 constexpr int kMaxChunks = 8;  // 512 keys
 
-template <int QW>
+template <int QW, bool BF>
 __global__ void __launch_bounds__(32 * QW, 3)
     attention_long_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmQKV64,
                      const int* __restrict__ cu_seqlens, int lpad,
@@ -381,16 +382,16 @@ __global__ void __launch_bounds__(32 * QW, 3)
     int kb = 0;
     for (; kb + 64 <= L; kb += 64) {
         if (kChunked && kb > 0 && !chunk_wait(&bar[kb >> 6], status)) return;
-        attend_block<4, false>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane);
+        attend_block<4, false, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane);
     }
     if (kb < L) {  // the ragged tail, in 16-key chunks: its chunk has landed and its V rows are zeroed
         if (kChunked && kb > 0 && !chunk_wait(&bar[kb >> 6], status)) return;
         if (kChunked && !chunk_wait(&vz, status)) return;
         switch ((L - kb + 15) >> 4) {
-            case 1: attend_block<1, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
-            case 2: attend_block<2, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
-            case 3: attend_block<3, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
-            case 4: attend_block<4, true>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+            case 1: attend_block<1, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+            case 2: attend_block<2, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+            case 3: attend_block<3, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
+            case 4: attend_block<4, true, BF>(kb, L, kaddr, vaddr, qa, o, m0, m1, l0, l1, lane); break;
             default: break;
         }
     }
@@ -404,8 +405,8 @@ __global__ void __launch_bounds__(32 * QW, 3)
 #pragma unroll
     for (int jd = 0; jd < 4; ++jd) {
         const int col = h * kHd + 8 * jd + cq;
-        const uint32_t p0 = tzp::pack_half2(o[jd][0] * inv0, o[jd][1] * inv0);
-        const uint32_t p1 = tzp::pack_half2(o[jd][2] * inv1, o[jd][3] * inv1);
+        const uint32_t p0 = tzp::pack16x2<BF>(o[jd][0] * inv0, o[jd][1] * inv0);
+        const uint32_t p1 = tzp::pack16x2<BF>(o[jd][2] * inv1, o[jd][3] * inv1);
         if (r0 < L) *reinterpret_cast<uint32_t*>(out + static_cast<long long>(seq0 + r0) * kHidden + col) = p0;
         if (r1 < L) *reinterpret_cast<uint32_t*>(out + static_cast<long long>(seq0 + r1) * kHidden + col) = p1;
         if (row_absmax) {
@@ -439,11 +440,13 @@ size_t attention_smem_bytes(int max_len) {
     return static_cast<size_t>(2) * lpad * 64 + static_cast<size_t>(qrows) * 64 + 1024;  // + alignment
 }
 
-// qkv f16 [T, 1152] (16-byte aligned); cu_seqlens device [B+1]; out f16 [T, 384]; row_absmax
-// (optional) [T] float bits, accumulated with atomicMax (must start at zero).
+// qkv [T, 1152] f16 (or bf16 with `bf16`; 16-byte aligned); cu_seqlens device [B+1]; out [T, 384] of
+// the same type; row_absmax (optional, f16 only) [T] float bits, accumulated with atomicMax (must start
+// at zero).
 int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const int* cu_seqlens, int batch, int max_len,
-                     void* out, unsigned* row_absmax, cudaStream_t s, bool pdl) {
+                     void* out, unsigned* row_absmax, cudaStream_t s, bool pdl, bool bf16) {
     TZ_CHECK(max_len >= 1 && max_len <= 512, TZ_EINVAL, "attention: max_len %d outside [1, 512]", max_len);
+    TZ_CHECK(!(bf16 && row_absmax), TZ_EINVAL, "attention: the row |max| is taken on IEEE-half outputs");
     if (batch == 0) return TZ_OK;
     const int lpad = (max_len + 63) / 64 * 64;
     const bool lng = attention_long(lpad);
@@ -452,28 +455,33 @@ int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const 
     int dev = 0;
     TZ_CUDA(cudaGetDevice(&dev));
     if (!(set & (1u << (dev & 31)))) {
-        TZ_CUDA(cudaFuncSetAttribute(attention_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(attention_smem_bytes(128))));
-        TZ_CUDA(cudaFuncSetAttribute(attention_long_kernel<kLongQW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(attention_smem_bytes(512))));
+        const int ss = static_cast<int>(attention_smem_bytes(128)), sl = static_cast<int>(attention_smem_bytes(512));
+        TZ_CUDA(cudaFuncSetAttribute(attention_short_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        TZ_CUDA(cudaFuncSetAttribute(attention_short_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        TZ_CUDA(cudaFuncSetAttribute(attention_long_kernel<kLongQW, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sl));
+        TZ_CUDA(cudaFuncSetAttribute(attention_long_kernel<kLongQW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sl));
         set |= 1u << (dev & 31);
     }
-    CUtensorMap tm, tm64;  // QKV f16 [T, 1152]: 16- and 64-row x 32-column boxes, 64-byte swizzle; rows >= T read as 0
-    int rc = encode_tmap_2d_swz(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens),
-                                kQKV * 2, kHd, 16, CU_TENSOR_MAP_SWIZZLE_64B);
+    // QKV [T, 1152]: 16- and 64-row x 32-column boxes, 64-byte swizzle; rows >= T read as 0
+    const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap tm, tm64;
+    int rc = encode_tmap_2d_swz(&tm, dt, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens), kQKV * 2, kHd, 16,
+                                CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
-    rc = encode_tmap_2d_swz(&tm64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens),
-                            kQKV * 2, kHd, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+    rc = encode_tmap_2d_swz(&tm64, dt, 2, qkv, kQKV, static_cast<uint64_t>(total_tokens), kQKV * 2, kHd, 64,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
+    __half* o = static_cast<__half*>(out);  // 16-bit container of either type
     if (lng) {
         const int qtile = 16 * kLongQW;
         dim3 grid(kHeads, batch, (max_len + qtile - 1) / qtile);
-        return launch_kernel(attention_long_kernel<kLongQW>, grid, dim3(32 * kLongQW), smem, s, pdl, tm, tm64, cu_seqlens,
-                             lpad, static_cast<__half*>(out), row_absmax, ctx->d_status);
+        auto k = bf16 ? attention_long_kernel<kLongQW, true> : attention_long_kernel<kLongQW, false>;
+        return launch_kernel(k, grid, dim3(32 * kLongQW), smem, s, pdl, tm, tm64, cu_seqlens, lpad, o, row_absmax,
+                             ctx->d_status);
     }
     dim3 grid(kHeads, batch, (max_len + kShortQ - 1) / kShortQ);
-    return launch_kernel(attention_short_kernel, grid, dim3(128), smem, s, pdl, tm, tm64, cu_seqlens, lpad,
-                         static_cast<__half*>(out), row_absmax, ctx->d_status);
+    auto k = bf16 ? attention_short_kernel<true> : attention_short_kernel<false>;
+    return launch_kernel(k, grid, dim3(128), smem, s, pdl, tm, tm64, cu_seqlens, lpad, o, row_absmax, ctx->d_status);
 }
 
 }  // namespace tz

@@ -294,6 +294,8 @@ constexpr int F_BMN = 32;
 // F_3X (general epilogue, tf32 only): the split-operand product of GemmArgs::a3x; the producer maps
 // K block kb of the MMA's K = 3P onto A's [hi | lo] row as hi, hi, lo (P = K / 3).
 constexpr int F_3X = 64;
+// F_OBF (specialised epilogue): the 16-bit output is bf16 instead of IEEE half.
+constexpr int F_OBF = 128;
 
 // Shared-memory descriptor of such an MN-major tile: 128-byte rows along MN (32 tf32 elements),
 // 4-row K groups 512 bytes apart (SBO), MN blocks of 32 elements `lbo` bytes apart (LBO), layout
@@ -323,6 +325,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     constexpr bool k3x = (FAST & F_3X) != 0;
     static_assert(!kBmn || (KIND == KIND_TF32 && !kFastEpi), "N-major B: tf32, general epilogue");
     static_assert(!k3x || (KIND == KIND_TF32 && !kFastEpi && !kBmn), "split tf32: tf32, general epilogue");
+    static_assert((FAST & F_OBF) == 0 || (FAST & F_AMAX) == 0, "the row |max| is taken on IEEE-half outputs");
     const int part3 = K / 3;  // F_3X: elements of one part
     uint64_t* full = reinterpret_cast<uint64_t*>(staging + (kFastEpi ? C::FAST_STAGING : C::STAGING));
     uint64_t* empty = full + STAGES;
@@ -603,7 +606,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                         x = tzp::f2_fma(hx, th, hx);
                     }
                     const float2 r = tzp::f2_unpack(x);
-                    h[j] = tzp::pack_half2(r.x, r.y);
+                    h[j] = tzp::pack16x2<(FAST & F_OBF) != 0>(r.x, r.y);
                     if constexpr ((FAST & F_AMAX) != 0)
                         amax2 = tzp::hmax2_xorsign_abs(amax2, h[j]);
                 }
@@ -758,7 +761,7 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     ep.ops = 0;
     ep.dbg_acc = g.dbg_acc;
     for (int i = 0; i < 8; ++i) ep.ops |= (static_cast<uint64_t>(g.ops[i]) & 31u) << (5 * i);
-    const int out_elem = g.out_type == OUT_F16 ? 2 : 4;
+    const int out_elem = (g.out_type == OUT_F16 || g.out_type == OUT_BF16) ? 2 : 4;
     const bool out_al = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldo * out_elem) % 16 == 0);
     const bool res_al = !g.residual || ((reinterpret_cast<uintptr_t>(g.residual) % 16 == 0) && ((g.ldr * 4) % 16 == 0));
     const bool vec_al = (!g.bias || reinterpret_cast<uintptr_t>(g.bias) % 16 == 0) &&
@@ -767,12 +770,14 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     ep.vec_ok = (out_al && res_al) ? 1 : 0;
     int use_tma = (out_al && g.N % CW == 0) ? 1 : 0;
     if (use_tma) {
-        const CUtensorMapDataType odt = g.out_type == OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                        : g.out_type == OUT_I32 ? CU_TENSOR_MAP_DATA_TYPE_INT32
-                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        const CUtensorMapDataType odt = g.out_type == OUT_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                        : g.out_type == OUT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                        : g.out_type == OUT_I32  ? CU_TENSOR_MAP_DATA_TYPE_INT32
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        const bool o16 = g.out_type == OUT_F16 || g.out_type == OUT_BF16;
         rc = encode_tmap_2d_swz(&to, odt, out_elem, g.out, static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.M),
                                 static_cast<uint64_t>(g.ldo) * out_elem, CW, 32,
-                                g.out_type == OUT_F16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
+                                o16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
         if (rc) return rc;
     } else {
         to = tb;  // unused
@@ -802,12 +807,14 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     TZ_CHECK(!g.row_scale || g.col_scale, TZ_EINVAL, "gemm: row_scale needs col_scale");
     // The specialised epilogue: f16 output with 16-byte aligned rows, N a multiple of 192, bias,
     // optional row/column dequantisation scales, optional GELU (tanh form) and row |max|.
-    const bool fast = (g.kind == KIND_I8 || g.kind == KIND_F16) && g.out_type == OUT_F16 && g.N % 192 == 0 && g.bias &&
-                      !g.residual && g.n_ops < 0 && (g.gelu == 0 || g.gelu == 1) &&
+    const bool fast = (((g.kind == KIND_I8 || g.kind == KIND_F16) && g.out_type == OUT_F16) ||
+                       (g.kind == KIND_BF16 && g.out_type == OUT_BF16 && !g.row_absmax)) &&
+                      g.N % 192 == 0 && g.bias && !g.residual && g.n_ops < 0 && (g.gelu == 0 || g.gelu == 1) &&
                       reinterpret_cast<uintptr_t>(g.out) % 16 == 0 && (g.ldo * 2) % 16 == 0;
+    TZ_CHECK(g.out_type != OUT_BF16 || fast, TZ_EUNSUPPORTED, "gemm: bf16 output only through the specialised epilogue");
     if (fast) {
         const int f = F_ON | (g.gelu == 1 ? F_GELU : 0) | (g.row_absmax ? F_AMAX : 0) |
-                      (g.row_scale ? F_RSCALE : (g.col_scale ? F_CSCALE : 0));
+                      (g.row_scale ? F_RSCALE : (g.col_scale ? F_CSCALE : 0)) | (g.out_type == OUT_BF16 ? F_OBF : 0);
 #define TZ_FAST_CASE(K_, F_) \
     case F_: return launch_impl<K_, 192, 3, 16, F_>(ctx, g, s);
 #define TZ_FAST_KIND(K_)                                                                                       \
@@ -828,8 +835,16 @@ int launch_gemm(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
     }
         if (g.kind == KIND_I8) {
             TZ_FAST_KIND(KIND_I8)
-        } else {
+        } else if (g.kind == KIND_F16) {
             TZ_FAST_KIND(KIND_F16)
+        } else {  // bf16 operands, bf16 output (no row |max|)
+            switch (f) {
+                TZ_FAST_CASE(KIND_BF16, F_ON | F_OBF)
+                TZ_FAST_CASE(KIND_BF16, F_ON | F_GELU | F_OBF)
+                TZ_FAST_CASE(KIND_BF16, F_ON | F_CSCALE | F_OBF)
+                TZ_FAST_CASE(KIND_BF16, F_ON | F_CSCALE | F_GELU | F_OBF)
+                default: break;
+            }
         }
 #undef TZ_FAST_KIND
 #undef TZ_FAST_CASE

@@ -3,6 +3,7 @@
 //   x_out[M, 384] = LayerNorm( dequant(A[M, K] * W[384, K]^T) + bias + residual )
 //   aux[M, 384]   = f16(x_out)                          (AUX = 0: the next GEMM's f16 operand)
 //                 | int8(x_out) with per-row scale       (AUX = 1: the next GEMM's W8A8 operand)
+//                 | bf16(x_out)                          (AUX = 2: the next GEMM's bf16 operand)
 //
 // Reference: selfAttention's output projection + residual + LayerNorm (arctic.zig:716-746) and
 // feedForward's second projection + residual + LayerNorm (arctic.zig:779-807); layerNormLastDim
@@ -494,13 +495,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 4; ++j)
                         *reinterpret_cast<float4*>(xq + j * 128) = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
                 }
-                if constexpr (AUX == 0) {
+                if constexpr (AUX == 0 || AUX == 2) {
+                    constexpr bool kBf = AUX == 2;
                     if (ok) {
-                        __half* a = static_cast<__half*>(p.aux) + static_cast<long long>(row) * kN + col;
-                        *reinterpret_cast<uint4*>(a) = make_uint4(tzp::pack_half2(y[0], y[1]), tzp::pack_half2(y[2], y[3]),
-                                                                  tzp::pack_half2(y[4], y[5]), tzp::pack_half2(y[6], y[7]));
-                        *reinterpret_cast<uint4*>(a + 8) = make_uint4(tzp::pack_half2(y[8], y[9]), tzp::pack_half2(y[10], y[11]),
-                                                                      tzp::pack_half2(y[12], y[13]), tzp::pack_half2(y[14], y[15]));
+                        uint16_t* a = static_cast<uint16_t*>(p.aux) + static_cast<long long>(row) * kN + col;
+                        *reinterpret_cast<uint4*>(a) = make_uint4(tzp::pack16x2<kBf>(y[0], y[1]), tzp::pack16x2<kBf>(y[2], y[3]),
+                                                                  tzp::pack16x2<kBf>(y[4], y[5]), tzp::pack16x2<kBf>(y[6], y[7]));
+                        *reinterpret_cast<uint4*>(a + 8) = make_uint4(tzp::pack16x2<kBf>(y[8], y[9]), tzp::pack16x2<kBf>(y[10], y[11]),
+                                                                      tzp::pack16x2<kBf>(y[12], y[13]), tzp::pack16x2<kBf>(y[14], y[15]));
                     }
                 } else {
 #pragma unroll
@@ -576,7 +578,7 @@ CUtensorMapDataType dtype_of(int kind) {
 template <int KIND, int AUX, int AQ = 0>
 int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     using C = LnCfg<KIND, AQ>;
-    static_assert(AUX == 0 || C::BOXES, "the int8 output is staged in the residual boxes");
+    static_assert(AUX != 1 || C::BOXES, "the int8 output is staged in the residual boxes");
     auto kern = gemm_ln_kernel<KIND, AUX, AQ>;
     static unsigned attr_set = 0;
     int dev = 0;
@@ -631,8 +633,10 @@ int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
         return launch_ln_impl<KIND_I8, 1, 1>(ctx, g, s);
     }
     TZ_CHECK(!g.aux_int8, TZ_EUNSUPPORTED, "gemm_ln: the int8 LayerNorm output needs the in-kernel A quantisation");
+    TZ_CHECK(g.aux_bf16 == (g.kind == KIND_BF16), TZ_EUNSUPPORTED, "gemm_ln: a bf16 aux goes with bf16 operands");
     if (g.kind == KIND_I8) return launch_ln_impl<KIND_I8, 0>(ctx, g, s);
     if (g.kind == KIND_F16) return launch_ln_impl<KIND_F16, 0>(ctx, g, s);
+    if (g.kind == KIND_BF16) return launch_ln_impl<KIND_BF16, 2>(ctx, g, s);
     return fail(TZ_EUNSUPPORTED, "gemm_ln: kind %d", g.kind);
 }
 

@@ -90,7 +90,7 @@ int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
 
 // ---- kernel launchers (defined in the .cu files) ---------------------------------------------
 enum GemmKind { KIND_F16 = 0, KIND_BF16 = 1, KIND_TF32 = 2, KIND_I8 = 3 };
-enum OutType { OUT_F32 = 0, OUT_F16 = 1, OUT_I32 = 2 };
+enum OutType { OUT_F32 = 0, OUT_F16 = 1, OUT_I32 = 2, OUT_BF16 = 3 };
 
 struct GemmArgs {
     int kind = KIND_F16;
@@ -153,6 +153,7 @@ struct GemmLnArgs {
     void* aux = nullptr;               // [M, 384] f16 or int8
     float* aux_scale = nullptr;        // [M] when aux is int8
     bool aux_int8 = false;
+    bool aux_bf16 = false;             // a 16-bit aux is bf16 (else IEEE half)
     // W8A8 with the A operand quantised inside the kernel: `a` is then f16 [M, K] (row stride lda)
     // and a_absmax [M] holds each row's |max| (float bits, accumulated by the producer with
     // atomicMax); the kernel derives the per-token scale from it, quantises A into its int8 stages

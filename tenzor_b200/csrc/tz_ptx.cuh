@@ -373,4 +373,35 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Two floats rounded to the forward's 16-bit activation type (BF = bf16, else IEEE half) and packed.
+template <bool BF>
+__device__ __forceinline__ uint32_t pack16x2(float lo, float hi) {
+    if constexpr (BF)
+        return pack_bf162(lo, hi);
+    else
+        return pack_half2(lo, hi);
+}
+
+// D += A B on m16n8k16 with bf16 operands, f32 accumulate (the bf16 form of mma_f16_16816).
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <bool BF>
+__device__ __forceinline__ void mma16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (BF)
+        mma_bf16_16816(d, a, b0, b1);
+    else
+        mma_f16_16816(d, a, b0, b1);
+}
+
 }  // namespace tzp

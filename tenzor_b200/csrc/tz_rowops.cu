@@ -199,6 +199,16 @@ __global__ void i8_to_f16_kernel(const int8_t* x, __half* y, long long n) {
          i += static_cast<long long>(gridDim.x) * blockDim.x)
         y[i] = __int2half_rn(static_cast<int>(x[i]));
 }
+__global__ void f32_to_bf16_kernel(const float* x, __nv_bfloat16* y, long long n) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+__global__ void i8_to_bf16_kernel(const int8_t* x, __nv_bfloat16* y, long long n) {  // exact: |q| <= 127
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        y[i] = __float2bfloat16_rn(static_cast<float>(x[i]));
+}
 __global__ void f16bits_to_f32_kernel(const uint16_t* x, float* y, long long n) {
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<long long>(gridDim.x) * blockDim.x)
@@ -385,6 +395,16 @@ inline int warp_rows_grid_r(long long rows, int r) { return warp_rows_grid((rows
 // ---- launchers shared with the model -----------------------------------------------------------
 int launch_f32_to_f16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s) {
     f32_to_f16_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(x, static_cast<__half*>(y), n);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+int launch_f32_to_bf16(tz_ctx_t ctx, const float* x, void* y, long long n, cudaStream_t s) {
+    f32_to_bf16_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(x, static_cast<__nv_bfloat16*>(y), n);
+    TZ_CUDA(cudaGetLastError());
+    return TZ_OK;
+}
+int launch_i8_to_bf16(tz_ctx_t ctx, const int8_t* x, void* y, long long n, cudaStream_t s) {
+    i8_to_bf16_kernel<<<ew_grid(ctx, n, 256), 256, 0, s>>>(x, static_cast<__nv_bfloat16*>(y), n);
     TZ_CUDA(cudaGetLastError());
     return TZ_OK;
 }
