@@ -292,7 +292,7 @@ def _pack(ids, lens):
     return S.pack(ids, lens)
 
 
-def make_inputs(cfg, world):
+def make_inputs(cfg, world, batch_override=None):
     """(ids [B, S], lengths [B], the global row ids of each rank).  configs[0] / configs[1] scale
     weakly: rank r runs its own block of `batch` sequences whose lengths are those of the one-GPU
     batch (seed 7) and whose tokens are drawn from seed 7 + r, so every rank does the one-GPU work.
@@ -300,13 +300,13 @@ def make_inputs(cfg, world):
     from tenzor_b200 import synthetic as S
     from tenzor_b200.shard import shard_by_tokens
     c = CONFIGS[cfg]
-    ids0, lens0 = S.token_batch(c["batch"], c["seq"], c["lmin"], c["lmax"], seed=7)
+    batch = batch_override or c["batch"]
+    ids0, lens0 = S.token_batch(batch, c["seq"], c["lmin"], c["lmax"], seed=7)
     if cfg == "c4":
         return ids0, lens0, shard_by_tokens(lens0, world) if world > 1 else [np.arange(len(lens0))]
     ids = np.concatenate([ids0] + [S.token_batch_with_lengths(lens0, c["seq"], seed=7 + r) for r in range(1, world)])
     lens = np.concatenate([lens0] * world)
-    B = c["batch"]
-    return ids, lens, [np.arange(r * B, (r + 1) * B) for r in range(world)]
+    return ids, lens, [np.arange(r * batch, (r + 1) * batch) for r in range(world)]
 
 
 def run_reference(a):
@@ -319,7 +319,7 @@ def run_reference(a):
     import oracle as O
     w = S.arctic_weights(1234)
     ck = O.quantize_checkpoint(w) if a.mode != "f32" else w
-    ids, lens, _ = make_inputs(a.config, world)
+    ids, lens, _ = make_inputs(a.config, world, a.batch)
     ref_mode = "w8a32" if a.mode != "f32" else "f32"  # the reference's own int8 path is W8A32
     vals = []
     sample = ""
@@ -369,7 +369,7 @@ def run_ours(a):
     ck = quantize_checkpoint(ctx, w) if a.mode != "f32" else w
     model = ArcticModel.from_checkpoint(ctx, ck, a.mode, prec=a.prec)
 
-    ids, lens, shards = make_inputs(a.config, world)
+    ids, lens, shards = make_inputs(a.config, world, a.batch)
     mine = shards[rank]
     l_ids, l_lens = ids[mine], lens[mine]
     packed, cu = S.pack(l_ids, l_lens)
@@ -546,7 +546,9 @@ def run_ours(a):
             "dtype": "int8 (W8A8, int32 acc)" if int8 else (f"{a.prec} operands / f32 acc" if a.mode == "f32"
                                                              else f"int8 weights as {a.prec} / f32 acc"),
             "data": "synthetic (seeded N(0,0.02) weights, U ids / lengths)",
-            "config": {"workload": cfg["desc"] + (" per GPU" if world > 1 else ""), "model": "Arctic-embed-xs",
+            "config": {"workload": cfg["desc"] + (" per GPU" if world > 1 else "") +
+                       (f" (batch overridden to {a.batch}: a profiling case, not the config)" if a.batch else ""),
+                       "model": "Arctic-embed-xs",
                        "mode": a.mode, "global_batch": int(len(lens)), "per_gpu_batch": B, "tokens_per_gpu": T,
                        "seq_len": cfg["seq"], "parallelism": f"sequence-sharded x{world}, gather to rank 0",
                        "l2": "flushed (256 MB write) before every timed step",
@@ -859,6 +861,8 @@ def main():
     ap.add_argument("--prec", default="f16", choices=["f16", "bf16"],
                     help="16-bit GEMM operand type of the f32 / w8a32 modes")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU instead of the config's (small cases for profiling; not a bench line)")
     ap.add_argument("--micro", action="store_true", help="configs[2] fused-op microbenchmarks (one line each)")
     ap.add_argument("--model", default="arctic", choices=["arctic", "lenet"])
     a = ap.parse_args()
