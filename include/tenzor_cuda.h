@@ -229,6 +229,15 @@ int tz_softmax_last_axis(tz_ctx_t ctx, const float* x, const float* mask, float*
  * softmax.zig:423-440 with mask = -inf beyond the valid length. */
 int tz_softmax_keylen(tz_ctx_t ctx, const float* x, const int32_t* key_len, float* y,
                       int64_t groups, int rows_per_group, int cols, tz_stream_t stream);
+/* selfAttention, arctic.zig:639-747, over packed sequences (the kernel of the Arctic forward):
+ * qkv [total_tokens, 1152] 16-bit, row t = Q | K | V of token t (12 heads of 32 columns each);
+ * cu_seqlens device int32 [batch + 1], nondecreasing from 0 to total_tokens; out [total_tokens, 384]
+ * of the same type: for each head, softmax(Q K^T / sqrt(32)) V over the keys of the token's own
+ * sequence.  max_len (1..512) must bound every sequence length: a longer sequence is refused on the
+ * device (tz_cuda_check_status then returns TZ_EINVAL).  bf16 = 1 reads and writes bfloat16, 0 IEEE
+ * half.  qkv and out 16-byte aligned. */
+int tz_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const int32_t* cu_seqlens, int batch,
+                 int max_len, void* out, int bf16, tz_stream_t stream);
 /* linearProjection f32 arm, arctic.zig:599-620 (matmulTransposeB matmul.zig:54-77 + bias):
  * y[m,n] = x[m,k] w[n,k]^T (+ bias) [+ residual].  tcgen05 kind::tf32. */
 int tz_linear_f32(tz_ctx_t ctx, const float* x, const float* w, const float* bias,

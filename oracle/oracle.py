@@ -52,6 +52,7 @@ def _declare(L):
     L.tzo_l2_normalize.argtypes = [P, C.c_int]
     L.tzo_sgemm_nt.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int]
     L.tzo_sgemm_nn.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int]
+    L.tzo_attention_packed.argtypes = [P, P, C.c_int, P]
     L.tzo_linear_f32.argtypes = [P, P, P, P, C.c_int, C.c_int, C.c_int]
     L.tzo_linear_w8a32.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int]
     L.tzo_linear_w8a8.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int]
@@ -137,6 +138,15 @@ def sgemm_nn(a, b):
     c = np.empty((m, n), np.float32)
     lib().tzo_sgemm_nn(ptr(a), ptr(b), ptr(c), m, k, n)
     return c
+
+
+def attention_packed(qkv, cu_seqlens):
+    """tzo_attention_packed: qkv [T, 1152] f32, cu_seqlens [B + 1] -> [T, 384] f32."""
+    qkv = c32(qkv)
+    cu = np.ascontiguousarray(cu_seqlens, np.int32)
+    out = np.zeros((qkv.shape[0], 384), np.float32)
+    lib().tzo_attention_packed(ptr(qkv), ptr(cu), len(cu) - 1, ptr(out))
+    return out
 
 
 def linear_w8a32(x, wq, s16, bias):

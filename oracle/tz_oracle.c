@@ -587,23 +587,17 @@ static void round_f16(float* x, size_t n) {
     for (size_t i = 0; i < n; i++) x[i] = tzo_f16_to_f32(tzo_f32_to_f16(x[i]));
 }
 
-/* selfAttention, arctic.zig:639-747. */
-static void self_attention(int mode, const tzo_layer* lw, float* out, const float* in,
-                           scratch_t* s, int L) {
-    float* q = s->qkv;
-    float* k = s->qkv + (size_t)L * H;
-    float* v = s->qkv + (size_t)2 * L * H;
-    linear(mode, in, lw->q_w, lw->q_q, lw->q_s, lw->q_b, q, L, H, H);
-    linear(mode, in, lw->k_w, lw->k_q, lw->k_s, lw->k_b, k, L, H, H);
-    linear(mode, in, lw->v_w, lw->v_q, lw->v_s, lw->v_b, v, L, H, H);
-    if (mode == TZO_MODE_W8A8) round_f16(s->qkv, (size_t)3 * L * H);
+/* The per-head core of selfAttention, arctic.zig:663-747: for each head, scores = Q_h K_h^T / sqrt(32),
+ * row softmax (max, exp, sum, divide), P V_h.  Q / K / V row t at q / k / v + t * ld. */
+static void attend_heads(const float* q, const float* k, const float* v, size_t ld, float* attn_out,
+                         scratch_t* s, int L) {
     const float scale = 1.0f / sqrtf(32.0f);
     for (int h = 0; h < TZO_HEADS; h++) {
         int off = h * 32;
         for (int t = 0; t < L; t++) {
-            memcpy(s->qh + t * 32, q + (size_t)t * H + off, 32 * sizeof(float));
-            memcpy(s->kh + t * 32, k + (size_t)t * H + off, 32 * sizeof(float));
-            memcpy(s->vh + t * 32, v + (size_t)t * H + off, 32 * sizeof(float));
+            memcpy(s->qh + t * 32, q + (size_t)t * ld + off, 32 * sizeof(float));
+            memcpy(s->kh + t * 32, k + (size_t)t * ld + off, 32 * sizeof(float));
+            memcpy(s->vh + t * 32, v + (size_t)t * ld + off, 32 * sizeof(float));
         }
         tzo_sgemm_nt(s->qh, s->kh, s->scores, L, 32, L);
         for (int i = 0; i < L * L; i++) s->scores[i] *= scale;
@@ -621,12 +615,37 @@ static void self_attention(int mode, const tzo_layer* lw, float* out, const floa
         }
         tzo_sgemm_nn(s->scores, s->vh, s->oh, L, L, 32);
         for (int t = 0; t < L; t++)
-            memcpy(s->attn_out + (size_t)t * H + off, s->oh + t * 32, 32 * sizeof(float));
+            memcpy(attn_out + (size_t)t * H + off, s->oh + t * 32, 32 * sizeof(float));
     }
+}
+
+/* selfAttention, arctic.zig:639-747. */
+static void self_attention(int mode, const tzo_layer* lw, float* out, const float* in,
+                           scratch_t* s, int L) {
+    float* q = s->qkv;
+    float* k = s->qkv + (size_t)L * H;
+    float* v = s->qkv + (size_t)2 * L * H;
+    linear(mode, in, lw->q_w, lw->q_q, lw->q_s, lw->q_b, q, L, H, H);
+    linear(mode, in, lw->k_w, lw->k_q, lw->k_s, lw->k_b, k, L, H, H);
+    linear(mode, in, lw->v_w, lw->v_q, lw->v_s, lw->v_b, v, L, H, H);
+    if (mode == TZO_MODE_W8A8) round_f16(s->qkv, (size_t)3 * L * H);
+    attend_heads(q, k, v, H, s->attn_out, s, L);
     if (mode == TZO_MODE_W8A8) round_f16(s->attn_out, (size_t)L * H);
     linear(mode, s->attn_out, lw->o_w, lw->o_q, lw->o_s, lw->o_b, s->tmp, L, H, H);
     for (int i = 0; i < L * H; i++) out[i] = in[i] + s->tmp[i];
     tzo_layernorm_rows(out, lw->ln1_g, lw->ln1_b, out, L, H, EPS);
+}
+
+void tzo_attention_packed(const float* qkv, const int32_t* cu_seqlens, int batch, float* out) {
+    for (int b = 0; b < batch; b++) {
+        const int L = cu_seqlens[b + 1] - cu_seqlens[b];
+        if (L <= 0) continue;
+        scratch_t s;
+        scratch_alloc(&s, L);
+        const float* rows = qkv + (size_t)cu_seqlens[b] * 3 * H;
+        attend_heads(rows, rows + H, rows + 2 * H, (size_t)3 * H, out + (size_t)cu_seqlens[b] * H, &s, L);
+        scratch_free(&s);
+    }
 }
 
 /* feedForward, arctic.zig:760-810. */

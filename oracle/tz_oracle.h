@@ -72,6 +72,9 @@ void tzo_l2_normalize(float* v, int n);
 /* ---- GEMMs ---- */
 void tzo_sgemm_nt(const float* a, const float* b, float* c, int m, int k, int n);
 void tzo_sgemm_nn(const float* a, const float* b, float* c, int m, int k, int n);
+/* The attention core of selfAttention (arctic.zig:663-747) on packed sequences: qkv [T, 1152] rows
+ * (Q | K | V, 12 heads of 32), cu_seqlens [batch + 1]; out [T, 384]. */
+void tzo_attention_packed(const float* qkv, const int32_t* cu_seqlens, int batch, float* out);
 void tzo_linear_f32(const float* x, const float* w, const float* bias, float* y, int m, int k,
                     int n);
 void tzo_linear_w8a32(const float* x, const int8_t* wq, const uint16_t* s16, const float* bias,

@@ -29,7 +29,7 @@ EXPORTS = [
     "tz_arctic_debug_hidden", "tz_arctic_debug_operand", "tz_arctic_debug_accum", "tz_arctic_debug_gemm_input",
     "tz_arctic_debug_capture",
     "tz_arctic_profile", "tz_arctic_profile_read", "tz_layernorm_last_dim",
-    "tz_softmax_last_axis", "tz_softmax_keylen", "tz_linear_f32", "tz_linear_w8a32",
+    "tz_softmax_last_axis", "tz_softmax_keylen", "tz_attention", "tz_linear_f32", "tz_linear_w8a32",
     "tz_linear_w8a8", "tz_linear_w8a8_noalloc", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
     "tz_matmul_epilogue", "tz_ew_add_mul_exp", "tz_ew_program_run", "tz_ew_unary_chain", "tz_reduce",
     "tz_gather_rows", "tz_lenet_load", "tz_lenet_free", "tz_lenet_reserve", "tz_lenet_forward",
@@ -136,6 +136,7 @@ def _declare(L):
         "tz_layernorm_last_dim": [P, P, P, P, P, i64, i, C.c_float, P],
         "tz_softmax_last_axis": [P, P, P, P, i64, i, P],
         "tz_softmax_keylen": [P, P, P, P, i64, i, i, P],
+        "tz_attention": [P, P, i64, P, i, i, P, i, P],
         "tz_linear_f32": [P, P, P, P, P, P, i, i, i, P],
         "tz_linear_w8a32": [P, P, P, P, P, P, i, i, i, P],
         "tz_linear_w8a8": [P, P, P, P, P, P, i, i, i, P],

@@ -485,3 +485,13 @@ int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const 
 }
 
 }  // namespace tz
+
+extern "C" int tz_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const int32_t* cu_seqlens, int batch,
+                            int max_len, void* out, int bf16, tz_stream_t stream) {
+    TZ_CHECK(ctx && qkv && cu_seqlens && out && total_tokens >= 0 && batch >= 0, TZ_EINVAL, "tz_attention: bad arguments");
+    TZ_CHECK((reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0, TZ_EINVAL,
+             "tz_attention: qkv and out must be 16-byte aligned");
+    if (total_tokens == 0 || batch == 0) return TZ_OK;
+    return tz::launch_attention(ctx, qkv, total_tokens, cu_seqlens, batch, max_len, out, nullptr,
+                                tz::pick_stream(ctx, stream), false, bf16 != 0);
+}

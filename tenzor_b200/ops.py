@@ -66,6 +66,22 @@ def softmax_keylen(ctx: Context, x, key_len, out=None):
     return out
 
 
+def attention(ctx: Context, qkv, cu_seqlens, max_len: int, out=None):
+    """selfAttention (arctic.zig:639-747) over packed sequences: qkv [T, 1152] float16 or bfloat16
+    (Q | K | V, 12 heads of 32), cu_seqlens int32 [B + 1] on the device; returns [T, 384] of qkv's type."""
+    if qkv.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("attention: qkv must be float16 or bfloat16")
+    _dev(qkv, qkv.dtype)
+    _dev(cu_seqlens, torch.int32)
+    T = qkv.shape[0]
+    if qkv.shape != (T, 1152):
+        raise ValueError(f"attention: qkv must be [T, 1152], got {tuple(qkv.shape)}")
+    out = torch.empty((T, 384), device=qkv.device, dtype=qkv.dtype) if out is None else out
+    L.check(L.lib().tz_attention(ctx.handle, _p(qkv), T, _p(cu_seqlens), cu_seqlens.numel() - 1, int(max_len), _p(out),
+                                 int(qkv.dtype == torch.bfloat16), _stream()))
+    return out
+
+
 def linear(ctx: Context, x, w, bias=None, residual=None, out=None):
     m, k = x.shape
     n = w.shape[0]
