@@ -3,8 +3,9 @@ oracle's attention core (`tzo_attention_packed`, the same per-head scores / soft
 oracle's forward runs) on the same 16-bit Q / K / V.
 
 Batches whose longest sequence exceeds 128 keys run the 8-warp kernel (128 queries per CTA, one
-staging barrier per 64-key chunk); shorter batches the 4-warp kernel.  Tolerances: P and the output are rounded to the 16-bit type (f16: 11 mantissa
-bits, outputs of magnitude <= ~4 here, half an ulp = 1e-3; bf16: 8 bits)."""
+staging barrier per 64-key chunk); shorter batches the 4-warp kernel.  Tolerances: P and the
+output are rounded to the 16-bit type (f16: 11 mantissa bits, outputs of magnitude <= ~4 here, half
+an ulp = 1e-3; bf16: 8 bits)."""
 import numpy as np
 import pytest
 
