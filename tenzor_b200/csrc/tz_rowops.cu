@@ -114,8 +114,10 @@ __global__ void softmax_rows_kernel(const float* x, const float* mask, const int
 }
 
 // Fast path for cols == 128 (the Arctic attention shape at S=128): a row is one float4 per lane;
-// a warp takes R rows and issues all their loads before the first reduction.
-template <int R>
+// a warp takes R rows and issues all their loads before the first reduction.  I32: every row index
+// fits 31 bits, so the group of a row is a 32-bit division (the 64-bit one is a long call sequence
+// on the key-length load's critical path).
+template <int R, bool I32>
 __global__ void softmax_rows128_kernel(const float* x, const float* mask, const int* key_len,
                                        int rows_per_group, float* y, long long rows) {
     const long long row0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * R;
@@ -132,7 +134,9 @@ __global__ void softmax_rows128_kernel(const float* x, const float* mask, const 
             const float4 m = reinterpret_cast<const float4*>(mask + row * 128)[lane];
             v[r].x += m.x; v[r].y += m.y; v[r].z += m.z; v[r].w += m.w;
         }
-        valid[r] = (key_len && in) ? min(max(key_len[static_cast<int>(row / rows_per_group)], 0), 128) : 128;
+        const long long grp = I32 ? static_cast<long long>(static_cast<unsigned>(row) / static_cast<unsigned>(rows_per_group))
+                                  : row / rows_per_group;
+        valid[r] = (key_len && in) ? min(max(key_len[grp], 0), 128) : 128;
     }
     const int c = lane * 4;
 #pragma unroll
@@ -467,7 +471,7 @@ int tz_softmax_last_axis(tz_ctx_t ctx, const float* x, const float* mask, float*
     const bool al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
                     (!mask || reinterpret_cast<uintptr_t>(mask) % 16 == 0);
     if (cols == 128 && al)
-        softmax_rows128_kernel<4><<<warp_rows_grid_r(rows, 4), 256, 0, s>>>(x, mask, nullptr, 1, y, rows);
+        softmax_rows128_kernel<2, false><<<warp_rows_grid_r(rows, 2), 256, 0, s>>>(x, mask, nullptr, 1, y, rows);
     else
         softmax_rows_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, mask, nullptr, 1, y, rows, cols);
     TZ_CUDA(cudaGetLastError());
@@ -483,7 +487,10 @@ int tz_softmax_keylen(tz_ctx_t ctx, const float* x, const int32_t* key_len, floa
     cudaStream_t s = pick_stream(ctx, stream);
     const bool al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
     if (cols == 128 && al)
-        softmax_rows128_kernel<4><<<warp_rows_grid_r(rows, 4), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows);
+        if (rows + 4 < (1ll << 31))
+            softmax_rows128_kernel<2, true><<<warp_rows_grid_r(rows, 2), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows);
+        else
+            softmax_rows128_kernel<4, false><<<warp_rows_grid_r(rows, 4), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows);
     else
         softmax_rows_kernel<<<warp_rows_grid(rows), 256, 0, s>>>(x, nullptr, key_len, rows_per_group, y, rows, cols);
     TZ_CUDA(cudaGetLastError());
