@@ -224,11 +224,15 @@ __global__ void __launch_bounds__(256, 4)
         *reinterpret_cast<float4*>(dst + q * 128 + lane * 4) = *reinterpret_cast<const float4*>(tile + lane * kH + ((q ^ (lane & 7)) << 2));
 }
 
-// CLS pooling + l2Normalize (arctic.zig:851-863, forward 894-897): warp per sequence.
+// CLS pooling + l2Normalize (arctic.zig:851-863, forward 894-897): warp per sequence.  `out` may be
+// the device view of the caller's page-locked host buffer; with `status_dst` (the device view of a
+// page-locked host word) thread 0 also hands the device status word to the host, since every
+// kernel of the forward has completed by griddepcontrol.wait.
 __global__ void pool_l2_kernel(const float* __restrict__ x, const int* __restrict__ cu, float* __restrict__ out,
-                               int batch) {
+                               int batch, const int* status_src, int* status_dst) {
     tzp::pdl_wait();
     tzp::pdl_trigger();
+    if (status_dst && blockIdx.x == 0 && threadIdx.x == 0) *status_dst = *status_src;
     const int seq = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (seq >= batch) return;
@@ -337,6 +341,7 @@ struct tz_model_s {
     int* h_cu = nullptr;
     float* h_out = nullptr;
     int* h_status = nullptr;    // pinned slot: the device status word, read back with the output
+    int* status_host_view = nullptr;  // set while a zero-copy host call is captured: h_status's device view
     // padded-input staging
     uint32_t* d_pad_ids = nullptr;
     int* d_pad_lens = nullptr;
@@ -742,7 +747,7 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
     }
     if ((rc = prof_mark(m, P_POOL, s))) return rc;
     if ((rc = launch_kernel(pool_l2_kernel, dim3((B * 32 + 255) / 256), dim3(256), 0, s, pdl, (const float*)m->X, d_cu,
-                            d_out, B)))
+                            d_out, B, (const int*)m->ctx->d_status, m->status_host_view)))
         return rc;
     if ((rc = prof_mark(m, -1, s))) return rc;
     if (m->profile) ++m->prof_fwd;
@@ -828,6 +833,19 @@ int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, f
     const bool io_graph = graph_ok && ids_pin && cu_pin && out_pin;
     const void* io[3] = {io_graph ? static_cast<const void*>(ids) : nullptr, io_graph ? static_cast<const void*>(cu) : nullptr,
                          io_graph ? static_cast<const void*>(out) : nullptr};
+    // Zero-copy output: when the caller's page-locked output buffer (and the model's status slot) have
+    // device views, the pooling kernel writes the embeddings and the status word straight into host
+    // memory -- no device-to-host copy nodes after the forward.  Otherwise the graph copies them.
+    float* out_view = nullptr;
+    int* status_view = nullptr;
+    if (io_graph) {
+        void* pv = nullptr;
+        if (cudaHostGetDevicePointer(&pv, out, 0) == cudaSuccess) out_view = static_cast<float*>(pv);
+        pv = nullptr;
+        if (out_view && cudaHostGetDevicePointer(&pv, m->h_status, 0) == cudaSuccess) status_view = static_cast<int*>(pv);
+        if (!status_view) out_view = nullptr;
+        (void)cudaGetLastError();  // a buffer without a device view is not an error: the copies serve it
+    }
     auto h2d_inputs = [&]() -> int {
         TZ_CUDA(cudaMemcpyAsync(m->d_ids, ids_pin ? ids : m->h_ids, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
         TZ_CUDA(cudaMemcpyAsync(m->d_cu, cu_pin ? cu : m->h_cu, sizeof(int) * (B + 1), cudaMemcpyHostToDevice, s));
@@ -847,8 +865,10 @@ int forward_host(tz_model_s* m, const uint32_t* ids, const int32_t* cu, int B, f
         cudaGraph_t gr = nullptr;
         TZ_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
         int crc = io_graph ? h2d_inputs() : TZ_OK;
-        if (!crc) crc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, m->out, s);
-        if (!crc && io_graph) crc = d2h_outputs();
+        m->status_host_view = status_view;
+        if (!crc) crc = enqueue_forward(m, m->d_ids, m->d_cu, B, T, maxL, out_view ? out_view : m->out, s);
+        m->status_host_view = nullptr;
+        if (!crc && io_graph && !out_view) crc = d2h_outputs();
         const cudaError_t ee = cudaStreamEndCapture(s, &gr);
         if (crc) {
             if (gr) cudaGraphDestroy(gr);
