@@ -367,19 +367,41 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
     // stages, which the model's previous kernel never writes.
 
     const int n_tiles = (N + BN - 1) / BN;
-    const int num_tiles = ((M + 127) / 128) * n_tiles;
+    const int m_tiles = (M + 127) / 128;
+    const int num_tiles = m_tiles * n_tiles;
     const int kblocks = (K + C::BK - 1) / C::BK;
+    // Tile schedule.  When the K blocks of a tile fill the stage ring exactly (kblocks == STAGES:
+    // stage = K block for every tile) and there are at least as many CTAs as column blocks, each CTA
+    // keeps one column block and walks row blocks: its weight (B) tiles are loaded once and stay in
+    // the stages' B regions, and only A streams through the TMA path.  Otherwise tiles are dealt
+    // round-robin over the linear (row block, column block) order.
+    const bool fixed_n = kblocks == STAGES && n_tiles > 1 && static_cast<int>(gridDim.x) >= n_tiles;
+    const int my_n = static_cast<int>(blockIdx.x) % n_tiles, my_r = static_cast<int>(blockIdx.x) / n_tiles;
+    const int my_cn = (static_cast<int>(gridDim.x) - 1 - my_n) / n_tiles + 1;  // CTAs sharing my_n
+    auto tile_of = [&](int i, int& m0, int& n0) -> bool {  // this CTA's i-th tile
+        if (fixed_n) {
+            const int m = my_r + i * my_cn;
+            m0 = m * 128;
+            n0 = my_n * BN;
+            return m < m_tiles;
+        }
+        const int t = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+        m0 = (t / n_tiles) * 128;
+        n0 = (t % n_tiles) * BN;
+        return t < num_tiles;
+    };
 
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer ----
             int pre = 0;  // K blocks of the first tile whose B tile is already requested
-            if (static_cast<int>(blockIdx.x) < num_tiles) {
+            int fm0 = 0, fn0 = 0;
+            if (tile_of(0, fm0, fn0)) {
                 pre = kblocks < STAGES ? kblocks : STAGES;
                 for (int kb = 0; kb < pre; ++kb) {
                     tzp::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
                     uint8_t* sb = smem + kb * C::STAGE_BYTES + C::A_BYTES;
-                    const int nb = (blockIdx.x % n_tiles) * BN;
+                    const int nb = fn0;
                     if constexpr (kBmn) {
 #pragma unroll
                         for (int j = 0; j < BN / 32; ++j) tzp::tma_load_2d(sb + j * C::BK * 128, &tmB, nb + 32 * j, kb * C::BK, &full[kb]);
@@ -391,9 +413,8 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
             tzp::pdl_wait();
             int stage = 0;
             uint32_t phase = 0, armed = 0, armed_par = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-                const int m0 = (tile / n_tiles) * 128;
-                const int n0 = (tile % n_tiles) * BN;
+            int m0 = 0, n0 = 0;
+            for (int it = 0; tile_of(it, m0, n0); ++it) {
                 bool ok = true;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!tzp::mbar_wait(&empty[stage], phase ^ 1u, status, abort_flag)) {
@@ -401,8 +422,10 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                         break;
                     }
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
-                    const bool b_done = tile == static_cast<int>(blockIdx.x) && kb < pre;
-                    if (!b_done) tzp::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    const bool armed_ab = it == 0 && kb < pre;  // armed for A + B before griddepcontrol.wait
+                    const bool resident = fixed_n && it > 0;     // stage kb still holds this column block's B
+                    const bool b_done = armed_ab || resident;
+                    if (!armed_ab) tzp::mbar_arrive_expect_tx(&full[stage], resident ? C::A_BYTES : C::STAGE_BYTES);
                     int ax = kb * C::BK;
                     if constexpr (k3x) ax = ax < 2 * part3 ? ax % part3 : ax - part3;  // hi, hi, lo
                     tzp::tma_load_2d(sa, &tmA, ax, m0, &full[stage]);
@@ -435,7 +458,8 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                                        (kBmn ? (1u << 16) : 0u);  // bit 16: B is MN-major
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            int m0 = 0, n0 = 0;
+            for (int it = 0; tile_of(it, m0, n0); ++it) {
                 if (!tzp::mbar_wait(&tempty[acc], acc_phase ^ 1u, status, abort_flag)) break;
                 tzp::tc_fence_after();
                 const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -502,10 +526,11 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         // waits and is converted, so no tile starts on a global-memory round trip.
         constexpr int VPL = (CPW + 31) / 32;
         float nrs = 1.0f, nb[VPL], ns[VPL];
-        auto fetch = [&](int t) {
-            if (t >= num_tiles) return;
-            const int r = (t / n_tiles) * 128 + q * 32 + lane;
-            const int cb = (t % n_tiles) * BN + slice * CPW;
+        auto fetch = [&](int i) {  // the CTA's i-th tile
+            int fm0 = 0, fn0 = 0;
+            if (!tile_of(i, fm0, fn0)) return;
+            const int r = fm0 + q * 32 + lane;
+            const int cb = fn0 + slice * CPW;
             if constexpr ((FAST & F_RSCALE) != 0) nrs = r < M ? __ldg(ep.row_scale + r) : 1.0f;
 #pragma unroll
             for (int v = 0; v < VPL; ++v) {
@@ -516,10 +541,9 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                 }
             }
         };
-        fetch(blockIdx.x);
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int m0 = (tile / n_tiles) * 128;
-            const int n0 = (tile % n_tiles) * BN;
+        fetch(0);
+        int m0 = 0, n0 = 0;
+        for (int it = 0; tile_of(it, m0, n0); ++it) {
             const int row0 = m0 + q * 32;
             const int row = row0 + lane;
             const bool row_ok = row < M;
@@ -538,7 +562,7 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
                 }
             }
             __syncwarp();
-            fetch(tile + gridDim.x);
+            fetch(it + 1);
             if (!tzp::mbar_wait(&tfull[acc], acc_phase, status, abort_flag)) break;
             tzp::tc_fence_after();
             const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + slice * CPW);
@@ -646,9 +670,8 @@ __global__ void __launch_bounds__(Cfg<KIND, BN, STAGES, EPI_WARPS>::THREADS, 1)
         const uint32_t bufs = tzp::smem_u32(staging) + static_cast<uint32_t>(e * 2 * C::EPI_BUF);
         int acc = 0, nbuf = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int m0 = (tile / n_tiles) * 128;
-            const int n0 = (tile % n_tiles) * BN;
+        int m0 = 0, n0 = 0;
+        for (int it = 0; tile_of(it, m0, n0); ++it) {
             if (!tzp::mbar_wait(&tfull[acc], acc_phase, status, abort_flag)) break;
             tzp::tc_fence_after();
             const int row0 = m0 + q * 32;
