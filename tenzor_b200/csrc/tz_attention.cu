@@ -472,16 +472,25 @@ int launch_attention(tz_ctx_t ctx, const void* qkv, int64_t total_tokens, const 
                             CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
     __half* o = static_cast<__half*>(out);  // 16-bit container of either type
-    if (lng) {
-        const int qtile = 16 * kLongQW;
-        dim3 grid(kHeads, batch, (max_len + qtile - 1) / qtile);
-        auto k = bf16 ? attention_long_kernel<kLongQW, true> : attention_long_kernel<kLongQW, false>;
-        return launch_kernel(k, grid, dim3(32 * kLongQW), smem, s, pdl, tm, tm64, cu_seqlens, lpad, o, row_absmax,
-                             ctx->d_status);
+    // grid.y is the sequence: batches beyond 65535 sequences go in consecutive launches over slices of
+    // cu_seqlens (its entries are absolute token offsets, so a slice needs no rebasing)
+    const int qtile = lng ? 16 * kLongQW : kShortQ;
+    for (int b0 = 0; b0 < batch; b0 += 65535) {
+        const int nb = batch - b0 < 65535 ? batch - b0 : 65535;
+        dim3 grid(kHeads, nb, (max_len + qtile - 1) / qtile);
+        int rc;
+        if (lng) {
+            auto k = bf16 ? attention_long_kernel<kLongQW, true> : attention_long_kernel<kLongQW, false>;
+            rc = launch_kernel(k, grid, dim3(32 * kLongQW), smem, s, pdl, tm, tm64, cu_seqlens + b0, lpad, o, row_absmax,
+                               ctx->d_status);
+        } else {
+            auto k = bf16 ? attention_short_kernel<true> : attention_short_kernel<false>;
+            rc = launch_kernel(k, grid, dim3(128), smem, s, pdl, tm, tm64, cu_seqlens + b0, lpad, o, row_absmax,
+                               ctx->d_status);
+        }
+        if (rc) return rc;
     }
-    dim3 grid(kHeads, batch, (max_len + kShortQ - 1) / kShortQ);
-    auto k = bf16 ? attention_short_kernel<true> : attention_short_kernel<false>;
-    return launch_kernel(k, grid, dim3(128), smem, s, pdl, tm, tm64, cu_seqlens, lpad, o, row_absmax, ctx->d_status);
+    return TZ_OK;
 }
 
 }  // namespace tz

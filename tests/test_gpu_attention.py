@@ -107,3 +107,11 @@ def test_length_beyond_max_len_is_refused(ctx):
     torch.cuda.synchronize()
     ctx.check_status()
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.gpu
+def test_more_sequences_than_one_grid_dimension(ctx, oracle):
+    """70,000 short sequences: the launches are split at 65,535 sequences (the grid's y extent)."""
+    from tenzor_b200 import synthetic as S
+    lens = S.randint(17, 70000, 1, 4).astype(np.int32)
+    _check(ctx, oracle, Q.normal_qkv(int(lens.sum()), seed=9), lens, 4, F16_ATOL)
