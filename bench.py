@@ -45,6 +45,7 @@ CONFIGS = {
     "c4": dict(batch=8192, seq=512, lmin=32, lmax=512, desc="configs[3] B=8192 S=512"),
 }
 LIN_FLOP_PER_TOKEN = 2 * (4 * 384 * 384 + 2 * 384 * 1536)  # per layer
+NCCL_SMS = 4  # N > 1: SMs left to the NCCL gather that overlaps the next forward
 CLASS_NAMES = ["embed_ln", "qkv_gemm", "attention", "oproj_gemm_ln", "layernorm", "ffn1_gemm",
                "requant", "ffn2_gemm_ln", "pool_l2"]
 
@@ -363,8 +364,13 @@ def run_ours(a):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        # The gather of step i overlaps step i + 1's forward: NCCL gets at most NCCL_SMS CTAs and the
+        # forward's persistent GEMM grids leave that many SMs free, so neither waits for the other's SMs.
+        os.environ.setdefault("NCCL_MAX_CTAS", str(NCCL_SMS))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     ctx = Context(local)
+    if world > 1:
+        ctx.set_sm_reserve(NCCL_SMS)
     w = S.arctic_weights(1234)
     ck = quantize_checkpoint(ctx, w) if a.mode != "f32" else w
     model = ArcticModel.from_checkpoint(ctx, ck, a.mode, prec=a.prec)

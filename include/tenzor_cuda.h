@@ -56,6 +56,11 @@ int tz_cuda_synchronize(tz_ctx_t ctx);
  * check fired (bit 1) since the last call.  Reading clears it. */
 int tz_cuda_check_status(tz_ctx_t ctx);
 int tz_cuda_sm_count(tz_ctx_t ctx);
+/* Persistent GEMM grids of this context (the model's projections and the op-level GEMMs) use at most
+ * SMs - n CTAs, so that n SMs stay free for kernels that run concurrently on another stream -- the
+ * collective of a multi-GPU pipeline (e.g. NCCL limited to n CTAs with NCCL_MAX_CTAS), which would
+ * otherwise hold SMs the one-CTA-per-SM grids wait for.  0 (the default) uses every SM. */
+int tz_cuda_set_sm_reserve(tz_ctx_t ctx, int n);
 /* Failure-detection self-test: runs a kernel whose bounded device wait (the one every kernel's
  * mbarrier waits use) can never be satisfied, so it expires after ~1 s and the kernel returns.
  * Returns TZ_ETIMEOUT (and clears the status word); the context stays usable. */

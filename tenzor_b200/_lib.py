@@ -23,7 +23,7 @@ RED = {"sum": 0, "mean": 1, "prod": 2, "max": 3, "min": 4}
 # Every symbol include/tenzor_cuda.h declares (checked by tests/test_abi.py).
 EXPORTS = [
     "tz_get_last_error", "tz_version", "tz_cuda_create", "tz_cuda_destroy", "tz_cuda_synchronize",
-    "tz_cuda_check_status", "tz_cuda_sm_count", "tz_cuda_selftest_wait", "tz_alloc", "tz_free", "tz_upload", "tz_download",
+    "tz_cuda_check_status", "tz_cuda_sm_count", "tz_cuda_set_sm_reserve", "tz_cuda_selftest_wait", "tz_alloc", "tz_free", "tz_upload", "tz_download",
     "tz_arctic_load", "tz_arctic_load_ex", "tz_arctic_load_safetensors", "tz_arctic_free", "tz_arctic_reserve",
     "tz_arctic_forward", "tz_arctic_forward_padded", "tz_arctic_forward_device",
     "tz_arctic_debug_hidden", "tz_arctic_debug_operand", "tz_arctic_debug_accum", "tz_arctic_debug_gemm_input",
@@ -119,7 +119,7 @@ def _declare(L):
     sig = {
         "tz_cuda_create": [i, C.POINTER(P)],
         "tz_cuda_destroy": [P], "tz_cuda_synchronize": [P], "tz_cuda_check_status": [P],
-        "tz_cuda_sm_count": [P], "tz_cuda_selftest_wait": [P],
+        "tz_cuda_sm_count": [P], "tz_cuda_set_sm_reserve": [P, i], "tz_cuda_selftest_wait": [P],
         "tz_alloc": [P, u, C.POINTER(P)], "tz_free": [P, P],
         "tz_upload": [P, P, P, u], "tz_download": [P, P, P, u],
         "tz_arctic_load": [P, C.POINTER(ArcticWeights), i, C.POINTER(P)],

@@ -810,7 +810,8 @@ int launch_impl(tz_ctx_t ctx, const GemmArgs& g, cudaStream_t s) {
         return fail(TZ_EINVAL, "gemm: accumulator capture needs the specialised epilogue and a 16-byte aligned buffer");
     const int n_tiles = (g.N + BN - 1) / BN;
     const int tiles = ((g.M + 127) / 128) * n_tiles;
-    const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+    const int sms = ctx->sm_count - ctx->sm_reserve;
+    const int grid = tiles < sms ? tiles : sms;
     if (grid <= 0) return TZ_OK;
     return launch_kernel(kern, dim3(grid), dim3(C::THREADS), SMEM, s, g.pdl, ta, tb, to, g.M, g.N, g.K, ep, use_tma,
                          ctx->d_status);

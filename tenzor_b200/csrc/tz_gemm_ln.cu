@@ -607,7 +607,8 @@ int launch_ln_impl(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s) {
     LnParams p{g.bias, g.col_scale, g.row_scale, g.residual, g.gamma, g.beta, g.eps, g.x_out, g.aux, g.aux_scale,
                AQ ? static_cast<const __half*>(g.a) : nullptr, g.lda, g.a_absmax, g.dbg_acc, g.dbg_aq, g.dbg_as};
     const int tiles = (g.M + 127) / 128;
-    const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+    const int sms = ctx->sm_count - ctx->sm_reserve;
+    const int grid = tiles < sms ? tiles : sms;
     if (grid <= 0) return TZ_OK;
     return launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, s, g.pdl, ta, tb, tq, g.M, g.K, p, ctx->d_status);
 }

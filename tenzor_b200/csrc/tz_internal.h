@@ -41,6 +41,7 @@ struct Scratch {
 struct tz_ctx_s {
     int device = 0;
     int sm_count = 0;
+    int sm_reserve = 0;  // SMs the persistent GEMM grids leave free (for concurrent collective kernels)
     cudaStream_t stream = nullptr;
     int* d_status = nullptr;   // device status word (TZ_DEV_* bits)
     tz::Scratch scratch;       // op-level temporaries

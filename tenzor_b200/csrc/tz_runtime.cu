@@ -187,6 +187,12 @@ int tz_cuda_check_status(tz_ctx_t ctx) {
 
 int tz_cuda_sm_count(tz_ctx_t ctx) { return ctx ? ctx->sm_count : 0; }
 
+int tz_cuda_set_sm_reserve(tz_ctx_t ctx, int n) {
+    TZ_CHECK(ctx && n >= 0 && n < ctx->sm_count, TZ_EINVAL, "tz_cuda_set_sm_reserve: %d outside [0, SMs)", n);
+    ctx->sm_reserve = n;
+    return TZ_OK;
+}
+
 int tz_cuda_selftest_wait(tz_ctx_t ctx) {
     TZ_CHECK(ctx, TZ_EINVAL, "null context");
     TZ_CUDA(cudaSetDevice(ctx->device));

@@ -25,6 +25,10 @@ class Context:
     def sm_count(self) -> int:
         return L.lib().tz_cuda_sm_count(self.handle)
 
+    def set_sm_reserve(self, n: int):
+        """Leave n SMs free in the persistent GEMM grids (for a collective running concurrently)."""
+        L.check(L.lib().tz_cuda_set_sm_reserve(self.handle, int(n)))
+
     def synchronize(self):
         L.check(L.lib().tz_cuda_synchronize(self.handle))
 
