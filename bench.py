@@ -47,7 +47,7 @@ CONFIGS = {
 LIN_FLOP_PER_TOKEN = 2 * (4 * 384 * 384 + 2 * 384 * 1536)  # per layer
 NCCL_SMS = 4  # N > 1: SMs left to the NCCL gather that overlaps the next forward
 CLASS_NAMES = ["embed_ln", "qkv_gemm", "attention", "oproj_gemm_ln", "layernorm", "ffn1_gemm",
-               "requant", "ffn2_gemm_ln", "pool_l2"]
+               "ffn_fused", "ffn2_gemm_ln", "pool_l2"]
 
 
 def arctic_metric(config, mode):
@@ -75,7 +75,8 @@ def class_bytes(cls, T, B, int8):
     the results it must write, each once (weights once per launch), for T packed tokens.  Per token:
     the GEMM operand XA is int8 + an f32 scale (W8A8) or f16; QKV, the attention output OA and the
     FFN hidden H are f16 (W8A8 adds a u32 row |max| to OA and H); the residual stream X is f32, read
-    and rewritten by each GEMM+LayerNorm kernel, which also writes the next XA."""
+    and rewritten by each GEMM+LayerNorm kernel, which also writes the next XA.  The fused W8A8 FFN
+    block (6) reads XA and X and writes X and the next XA; its hidden H stays on chip."""
     a_in = 384 + 4 if int8 else 768
     amax = 4 if int8 else 0
     wb = 1 if int8 else 2
@@ -85,7 +86,7 @@ def class_bytes(cls, T, B, int8):
             3: T * (384 * 2 + amax + 384 * 4 * 2 + a_in) + 384 * 384 * wb,
             4: T * 384 * (4 + 4 + 1) + T * 4,
             5: T * (a_in + 1536 * 2 + amax) + 1536 * 384 * wb,
-            6: T * 1536 * 3 + T * 8,
+            6: T * (a_in + 384 * 4 * 2 + a_in) + 2 * 1536 * 384 * wb,
             7: T * (1536 * 2 + amax + 384 * 4 * 2 + a_in) + 384 * 1536 * wb,
             8: B * 384 * 8}[cls]
 
@@ -374,6 +375,7 @@ def run_ours(a):
     w = S.arctic_weights(1234)
     ck = quantize_checkpoint(ctx, w) if a.mode != "f32" else w
     model = ArcticModel.from_checkpoint(ctx, ck, a.mode, prec=a.prec)
+    model.set_ffn_fusion(a.ffn == "fused")
 
     ids, lens, shards = make_inputs(a.config, world, a.batch)
     mine = shards[rank]
@@ -512,11 +514,13 @@ def run_ours(a):
         # overall is named too.
         per = [(cls_ms[c], c) for c in range(9) if cls_n[c] > 0]
         top_ms, top = max(per)
-        dom_ms, dom = max((cls_ms[c], c) for c in (5, 7) if cls_n[c] > 0)
+        dom_ms, dom = max((cls_ms[c], c) for c in (5, 6, 7) if cls_n[c] > 0)
         avg_ms = dom_ms / cls_n[dom]
         Tl = T
         int8 = a.mode == "w8a8"
+        # (6: the fused FFN block's algorithmic FLOPs, FFN1 + FFN2; its second FFN1 pass is not counted)
         flops = {1: 2 * Tl * 384 * 1152, 3: 2 * Tl * 384 * 384, 5: 2 * Tl * 384 * 1536, 7: 2 * Tl * 1536 * 384,
+                 6: 4 * Tl * 384 * 1536,
                  2: 4 * 384 * float((l_lens.astype(np.float64) ** 2).sum())}
         byts = class_bytes(dom, Tl, B, int8)
         t_hbm = byts / (hbm * 1e9)
@@ -555,7 +559,7 @@ def run_ours(a):
             "config": {"workload": cfg["desc"] + (" per GPU" if world > 1 else "") +
                        (f" (batch overridden to {a.batch}: a profiling case, not the config)" if a.batch else ""),
                        "model": "Arctic-embed-xs",
-                       "mode": a.mode, "global_batch": int(len(lens)), "per_gpu_batch": B, "tokens_per_gpu": T,
+                       "mode": a.mode, "ffn_block": (a.ffn if int8 else None), "global_batch": int(len(lens)), "per_gpu_batch": B, "tokens_per_gpu": T,
                        "seq_len": cfg["seq"], "parallelism": f"sequence-sharded x{world}, gather to rank 0",
                        "l2": "flushed (256 MB write) before every timed step",
                        "gather": "N > 1: step i's NCCL gather to rank 0 runs on a second stream under step i + 1's "
@@ -867,6 +871,8 @@ def main():
     ap.add_argument("--prec", default="f16", choices=["f16", "bf16"],
                     help="16-bit GEMM operand type of the f32 / w8a32 modes")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--ffn", default="split", choices=["fused", "split"],
+                    help="W8A8 feed-forward block: the FFN1 + FFN2 kernel pair (default) or one kernel")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the config's (small cases for profiling; not a bench line)")
     ap.add_argument("--micro", action="store_true", help="configs[2] fused-op microbenchmarks (one line each)")

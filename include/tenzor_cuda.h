@@ -170,13 +170,25 @@ int tz_arctic_debug_operand(tz_model_t model, int which, int8_t* q_out, float* s
 int tz_arctic_debug_accum(tz_model_t model, int which, int32_t* acc_out, int64_t total_tokens);
 int tz_arctic_debug_gemm_input(tz_model_t model, int which, uint16_t* x_out, int64_t total_tokens);
 
+/* W8A8 feed-forward form.  fused = 0 (the default): the FFN1 GEMM writes the f16 GELU output to
+ * device memory and the FFN2 kernel quantises it per token in its mainloop.  fused = 1: FFN1, GELU,
+ * the per-token int8 quantisation of the GELU output, FFN2, bias, residual and LayerNorm run as one
+ * kernel per layer and the GELU output never leaves the SM (FFN1 is computed twice per row tile:
+ * once for each row's max |GELU|, which the per-token scale needs before any value can be
+ * quantised, and once to quantise and feed FFN2); on B200 it is slower (the doubled GELU work is
+ * bound by the special-function unit's tanh rate).  Both forms give bit-identical results; other
+ * modes ignore the setting.  Replaces nothing in the reference: feedForward (arctic.zig:760-810) is
+ * one function there. */
+int tz_arctic_set_ffn_fusion(tz_model_t model, int fused);
+
 /* Kernel timing of the forward: when enabled (enable = number of forwards to keep, 0 = off), CUDA
  * events are recorded on the launching stream between consecutive launches (inside a captured
  * graph too).  tz_arctic_profile_read returns, summed over the kept forwards since enabling, the
  * milliseconds and the launch count per kernel class:
  * 0 embedding+LN, 1 QKV GEMM, 2 attention, 3 attention-output GEMM + residual + LayerNorm,
  * 4 (unused: LayerNorm is fused into 3 and 7), 5 FFN1 GEMM,
- * 6 per-token requantisation (W8A8: attention output and FFN1 output), 7 FFN2 GEMM + residual + LayerNorm, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
+ * 6 the fused W8A8 feed-forward block (FFN1 + GELU + FFN2 + residual + LayerNorm), 7 FFN2 GEMM +
+ * residual + LayerNorm, 8 CLS pool + L2 (arrays of TZ_PROF_CLASSES). */
 #define TZ_PROF_CLASSES 9
 int tz_arctic_profile(tz_model_t model, int enable);
 int tz_arctic_profile_read(tz_model_t model, float* ms, int* launches);

@@ -27,7 +27,7 @@ EXPORTS = [
     "tz_arctic_load", "tz_arctic_load_ex", "tz_arctic_load_safetensors", "tz_arctic_free", "tz_arctic_reserve",
     "tz_arctic_forward", "tz_arctic_forward_padded", "tz_arctic_forward_device",
     "tz_arctic_debug_hidden", "tz_arctic_debug_operand", "tz_arctic_debug_accum", "tz_arctic_debug_gemm_input",
-    "tz_arctic_debug_capture",
+    "tz_arctic_debug_capture", "tz_arctic_set_ffn_fusion",
     "tz_arctic_profile", "tz_arctic_profile_read", "tz_layernorm_last_dim",
     "tz_softmax_last_axis", "tz_softmax_keylen", "tz_attention", "tz_linear_f32", "tz_linear_w8a32",
     "tz_linear_w8a8", "tz_linear_w8a8_noalloc", "tz_gemm_i8_i32", "tz_quantize_weight_rows", "tz_quantize_act_rows",
@@ -132,6 +132,7 @@ def _declare(L):
         "tz_arctic_debug_hidden": [P, i, P, i64],
         "tz_arctic_debug_operand": [P, i, P, P, i64],
         "tz_arctic_debug_accum": [P, i, P, i64], "tz_arctic_debug_capture": [P, i], "tz_arctic_debug_gemm_input": [P, i, P, i64],
+        "tz_arctic_set_ffn_fusion": [P, i],
         "tz_arctic_profile": [P, i], "tz_arctic_profile_read": [P, P, P],
         "tz_layernorm_last_dim": [P, P, P, P, P, i64, i, C.c_float, P],
         "tz_softmax_last_axis": [P, P, P, P, i64, i, P],

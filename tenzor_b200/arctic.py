@@ -219,6 +219,12 @@ class ArcticModel:
         L.check(L.lib().tz_arctic_forward_device(self.handle, int(d_ids), int(d_cu), batch, total_tokens,
                                                  max_len, int(d_out), C.c_void_p(stream) if stream else None))
 
+    def set_ffn_fusion(self, fused: bool = True):
+        """W8A8: the feed-forward block as one kernel with the GELU output kept on chip, or (the
+        default, faster on B200) as the FFN1 GEMM + FFN2 kernel pair with the GELU output through
+        device memory.  Both forms give bit-identical results."""
+        L.check(L.lib().tz_arctic_set_ffn_fusion(self.handle, int(bool(fused))))
+
     # ---- parity hooks -----------------------------------------------------------------------
     def debug_hidden(self, stage: int, total_tokens: int) -> np.ndarray:
         out = np.empty((total_tokens, 384), np.float32)

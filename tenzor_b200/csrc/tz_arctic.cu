@@ -373,6 +373,10 @@ struct tz_model_s {
     int64_t g_tokens = -1;
     const void* g_io[3] = {nullptr, nullptr, nullptr};  // pinned ids / cu / out the graph copies (or none)
     bool use_graph = true;
+    // W8A8: the feed-forward block as the FFN1 GEMM + FFN2 gemm_ln pair with the GELU output through
+    // device memory (the default: faster on B200), or as one kernel with the GELU output kept on chip
+    // (tz_ffn.cu; tz_arctic_set_ffn_fusion)
+    bool ffn_fused = false;
     // graph cache for the device-pointer forward (keyed by buffers, shape and stream)
     cudaGraphExec_t dgraph = nullptr;
     const void* dkey[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -621,7 +625,7 @@ int reserve(tz_model_s* m, int batch, int64_t tokens) {
     return TZ_OK;
 }
 
-enum ProfClass { P_EMBED = 0, P_QKV, P_ATTN, P_OPROJ, P_LN, P_FFN1, P_QUANT, P_FFN2, P_POOL, P_NCLASS };
+enum ProfClass { P_EMBED = 0, P_QKV, P_ATTN, P_OPROJ, P_LN, P_FFN1, P_FFN, P_FFN2, P_POOL, P_NCLASS };
 
 // Records the event that closes launch (ev_n - 1) and opens the next one.
 int prof_mark(tz_model_s* m, int next_class, cudaStream_t s) {
@@ -711,35 +715,57 @@ int enqueue_forward(tz_model_s* m, const uint32_t* d_ids, const int* d_cu, int B
         if (l == 0 && m->keep_stages)  // layer 0's hidden state after the attention block
             TZ_CUDA(cudaMemcpyAsync(m->d_stages + static_cast<size_t>(7) * xblk_rows(m->cap_tokens) * kH, m->X,
                                     sizeof(float) * xblk_rows(T) * kH, cudaMemcpyDeviceToDevice, s));
-        // FFN1 + bias + GELU
-        GemmArgs f1;
-        f1.pdl = pdl;
-        f1.kind = g.kind;
-        f1.a = m->XA; f1.lda = kH; f1.b = L.w1; f1.ldb = kH; f1.M = M; f1.N = kF; f1.K = kH;
-        f1.bias = L.b1; f1.col_scale = wscale ? L.s1 : nullptr; f1.row_scale = q8 ? m->xs : nullptr;
-        f1.gelu = 1; f1.out = m->Hh; f1.ldo = kF; f1.out_type = out16; f1.row_absmax = q8 ? m->hmax : nullptr;
-        if (cap) f1.dbg_acc = m->d_acc[2];
-        if (l == 0 && (rc = keep_operand(m, 2, m->XA, m->xs, T, kH, s))) return rc;
-        if ((rc = prof_mark(m, P_FFN1, s))) return rc;
-        if ((rc = launch_gemm(ctx, f1, s))) return rc;
-        if (cap)  // the f16 GELU output the next kernel quantises in its mainloop
-            TZ_CUDA(cudaMemcpyAsync(m->d_in16[3], m->Hh, sizeof(__half) * T * kF, cudaMemcpyDeviceToDevice, s));
-        // FFN2 + bias + residual + LayerNorm in one kernel (arctic.zig:779-807); W8A8 quantises the
-        // f16 GELU output per token inside the kernel.
-        GemmLnArgs f2;
-        f2.pdl = pdl;
-        f2.kind = g.kind;
-        f2.a = m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.K = kF;
-        f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.a_absmax = q8 ? m->hmax : nullptr;
-        f2.residual = m->X; f2.gamma = L.ln2g; f2.beta = L.ln2b; f2.eps = kEps;
-        f2.x_out = m->X; f2.aux = m->XA; f2.aux_scale = q8 ? m->xs : nullptr; f2.aux_int8 = q8; f2.aux_bf16 = m->bf16;
-        if (cap) {
-            f2.dbg_acc = m->d_acc[3];
-            f2.dbg_aq = m->d_opq[3];
-            f2.dbg_as = m->d_ops[3];
+        if (q8 && m->ffn_fused) {
+            // the whole feed-forward block in one kernel (arctic.zig:760-810): FFN1 + GELU, the
+            // per-token int8 form of the GELU output kept on chip, FFN2 + residual + LayerNorm and the
+            // next layer's int8 operand
+            FfnArgs fa;
+            fa.pdl = pdl;
+            fa.xq = static_cast<const int8_t*>(m->XA); fa.xs = m->xs; fa.M = M;
+            fa.w1 = static_cast<const int8_t*>(L.w1); fa.s1 = L.s1; fa.b1 = L.b1;
+            fa.w2 = static_cast<const int8_t*>(L.w2); fa.s2 = L.s2; fa.b2 = L.b2;
+            fa.gamma = L.ln2g; fa.beta = L.ln2b; fa.eps = kEps; fa.x = m->X;
+            if (cap) {
+                fa.dbg_acc1 = m->d_acc[2];
+                fa.dbg_h16 = m->d_in16[3];
+                fa.dbg_hq = m->d_opq[3];
+                fa.dbg_hs = m->d_ops[3];
+                fa.dbg_acc2 = m->d_acc[3];
+            }
+            if (l == 0 && (rc = keep_operand(m, 2, m->XA, m->xs, T, kH, s))) return rc;
+            if ((rc = prof_mark(m, P_FFN, s))) return rc;
+            if ((rc = launch_ffn_w8a8(ctx, fa, s))) return rc;
+        } else {
+            // FFN1 + bias + GELU
+            GemmArgs f1;
+            f1.pdl = pdl;
+            f1.kind = g.kind;
+            f1.a = m->XA; f1.lda = kH; f1.b = L.w1; f1.ldb = kH; f1.M = M; f1.N = kF; f1.K = kH;
+            f1.bias = L.b1; f1.col_scale = wscale ? L.s1 : nullptr; f1.row_scale = q8 ? m->xs : nullptr;
+            f1.gelu = 1; f1.out = m->Hh; f1.ldo = kF; f1.out_type = out16; f1.row_absmax = q8 ? m->hmax : nullptr;
+            if (cap) f1.dbg_acc = m->d_acc[2];
+            if (l == 0 && (rc = keep_operand(m, 2, m->XA, m->xs, T, kH, s))) return rc;
+            if ((rc = prof_mark(m, P_FFN1, s))) return rc;
+            if ((rc = launch_gemm(ctx, f1, s))) return rc;
+            if (cap)  // the f16 GELU output the next kernel quantises in its mainloop
+                TZ_CUDA(cudaMemcpyAsync(m->d_in16[3], m->Hh, sizeof(__half) * T * kF, cudaMemcpyDeviceToDevice, s));
+            // FFN2 + bias + residual + LayerNorm in one kernel (arctic.zig:779-807); W8A8 quantises the
+            // f16 GELU output per token inside the kernel.
+            GemmLnArgs f2;
+            f2.pdl = pdl;
+            f2.kind = g.kind;
+            f2.a = m->Hh; f2.lda = kF; f2.b = L.w2; f2.ldb = kF; f2.M = M; f2.K = kF;
+            f2.bias = L.b2; f2.col_scale = wscale ? L.s2 : nullptr; f2.a_absmax = q8 ? m->hmax : nullptr;
+            f2.residual = m->X; f2.gamma = L.ln2g; f2.beta = L.ln2b; f2.eps = kEps;
+            f2.x_out = m->X; f2.aux = m->XA; f2.aux_scale = q8 ? m->xs : nullptr; f2.aux_int8 = q8; f2.aux_bf16 = m->bf16;
+            if (cap) {
+                f2.dbg_acc = m->d_acc[3];
+                f2.dbg_aq = m->d_opq[3];
+                f2.dbg_as = m->d_ops[3];
+            }
+            if ((rc = prof_mark(m, P_FFN2, s))) return rc;
+            if ((rc = launch_gemm_ln(ctx, f2, s))) return rc;
         }
-        if ((rc = prof_mark(m, P_FFN2, s))) return rc;
-        if ((rc = launch_gemm_ln(ctx, f2, s))) return rc;
         if (m->keep_stages)
             TZ_CUDA(cudaMemcpyAsync(m->d_stages + static_cast<size_t>(l + 1) * xblk_rows(m->cap_tokens) * kH, m->X,
                                     sizeof(float) * xblk_rows(T) * kH,
@@ -1097,6 +1123,16 @@ int tz_arctic_debug_capture(tz_model_t m, int on) {
     TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
     m->keep_stages = on != 0;
     if (!on) free_workspace(m);  // the next forward re-reserves without the capture buffers
+    return TZ_OK;
+}
+
+int tz_arctic_set_ffn_fusion(tz_model_t m, int fused) {
+    TZ_CHECK(m && (fused == 0 || fused == 1), TZ_EINVAL, "tz_arctic_set_ffn_fusion: bad arguments");
+    if ((fused != 0) == m->ffn_fused) return TZ_OK;
+    TZ_CUDA(cudaSetDevice(m->ctx->device));
+    TZ_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    drop_graphs(m);  // the captured graphs hold the other launch sequence
+    m->ffn_fused = fused != 0;
     return TZ_OK;
 }
 

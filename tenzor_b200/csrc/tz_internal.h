@@ -171,4 +171,32 @@ struct GemmLnArgs {
 };
 int launch_gemm_ln(tz_ctx_t ctx, const GemmLnArgs& g, cudaStream_t s);
 
+// The W8A8 feed-forward block in one kernel (tz_ffn.cu): FFN1 + GELU + per-token int8 + FFN2 +
+// bias + residual + LayerNorm + the next layer's int8 operand, with the GELU output kept on chip.
+struct FfnArgs {
+    const int8_t* xq = nullptr;   // [M, 384] int8 operand; overwritten with the int8 LayerNorm output
+    float* xs = nullptr;          // [M] its per-token scales; overwritten with the output's
+    const int8_t* w1 = nullptr;   // [1536, 384]
+    const float* s1 = nullptr;    // [1536] per-output-channel scales
+    const float* b1 = nullptr;    // [1536]
+    const int8_t* w2 = nullptr;   // [384, 1536]
+    const float* s2 = nullptr;    // [384]
+    const float* b2 = nullptr;    // [384]
+    const float* gamma = nullptr;
+    const float* beta = nullptr;
+    float eps = 1e-12f;
+    float* x = nullptr;           // [M, 384] f32 residual stream, blocked (xblk), updated in place
+    int M = 0;
+    bool pdl = false;
+    // Parity capture (runtime pointers of the same kernel): FFN1 accumulators [M, 1536], the f16 GELU
+    // output as quantised [M, 1536], its int8 form [M, 1536] and per-token scales [M], FFN2
+    // accumulators [M, 384].
+    int32_t* dbg_acc1 = nullptr;
+    void* dbg_h16 = nullptr;
+    int8_t* dbg_hq = nullptr;
+    float* dbg_hs = nullptr;
+    int32_t* dbg_acc2 = nullptr;
+};
+int launch_ffn_w8a8(tz_ctx_t ctx, const FfnArgs& a, cudaStream_t s);
+
 }  // namespace tz

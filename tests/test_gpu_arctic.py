@@ -148,6 +148,39 @@ def test_w8a8_int32_accumulators_bit_exact_full_c2(oracle, qweights, models):
     _check_w8a8_layer0_kernels(oracle, qweights, models["w8a8"], packed, cu, rows)
 
 
+@pytest.mark.parametrize("ffn", ["fused", "split"])
+def test_w8a8_int32_accumulators_bit_exact_both_ffn_forms(oracle, qweights, models, c1, ffn):
+    """The same layer-0 check with the feed-forward block as one kernel (GELU output kept on chip,
+    FFN1 computed twice) and as the FFN1 GEMM + FFN2 kernel pair."""
+    ids, lens, packed, cu = c1
+    m = models["w8a8"]
+    m.set_ffn_fusion(ffn == "fused")
+    try:
+        _check_w8a8_layer0_kernels(oracle, qweights, m, packed, cu)
+    finally:
+        m.set_ffn_fusion(False)
+
+
+@pytest.mark.parametrize("batch,lmin,lmax,seed", [(8, 16, 128, 7), (256, 16, 128, 7), (3, 1, 5, 3),
+                                                   (1500, 100, 128, 5)])
+def test_w8a8_fused_ffn_bit_identical_to_split(models, batch, lmin, lmax, seed):
+    """The fused feed-forward kernel repeats the split path's arithmetic operation for operation, so
+    the embeddings agree bit for bit: configs[0], configs[1] (142 row tiles, one per CTA), a tiny
+    batch (one partial tile) and ~178k tokens (1391 row tiles: several per persistent CTA, so the
+    tile-to-tile hand-over of TMEM, the H chunks and the XQ stage is exercised)."""
+    ids, lens = S.token_batch(batch, 128, lmin, lmax, seed=seed)
+    packed, cu = S.pack(ids, lens)
+    m = models["w8a8"]
+    split = m.forward_packed(packed, cu)
+    m.set_ffn_fusion(True)
+    try:
+        fused = m.forward_packed(packed, cu)
+    finally:
+        m.set_ffn_fusion(False)
+    assert np.isfinite(fused).all()
+    assert np.array_equal(fused, split), f"max-abs {np.abs(fused - split).max():.3e}"
+
+
 def test_packed_padded_batch_agree(models, c1):
     ids, lens, packed, cu = c1
     m = models["f32"]
