@@ -132,19 +132,24 @@ class Clocks:
     NVML (the library nvidia-smi reads) is polled every ~2 ms from a thread, so even a timed region of
     a few tens of milliseconds gets samples; `mark()` is called from the timing loop right after the
     steps are enqueued (the GPU is busy then) and only samples taken between `begin()` and `end()`
-    count.  Falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
+    count.  Falls back to `nvidia-smi -lms 200` when NVML is unavailable.  With `poll` false there is
+    no thread, only the `mark()` sample: under torchrun only rank 0 (whose clocks the JSON line
+    reports) polls, so that eight processes do not each make ~2000 NVML driver calls per second
+    during the timed steps."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, gpu: int):
+    def __init__(self, gpu: int, poll: bool = True):
         self.gpu = gpu
+        self.poll = poll
         self.rows = []  # (t, sm_mhz, max_mhz, power_w, [reason names])
         self.window = []
         self.proc = None
         self.nv = None
+        self.t = None
         self.stop = threading.Event()
 
     def _nvml_handle(self):
@@ -178,11 +183,14 @@ class Clocks:
         try:
             self.nv = self._nvml_handle()
             self._sample_nvml()
-            self.t = threading.Thread(target=self._poll, daemon=True)
-            self.t.start()
+            if self.poll:
+                self.t = threading.Thread(target=self._poll, daemon=True)
+                self.t.start()
             return self
         except Exception:
             self.nv = None
+        if not self.poll:
+            return self
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -222,7 +230,7 @@ class Clocks:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-        elif self.nv:
+        elif self.t is not None:
             self.t.join(timeout=1)
 
     def summary(self):
@@ -401,21 +409,25 @@ def run_ours(a):
     fdone = [torch.cuda.Event(), torch.cuda.Event()]  # forward of the buffer's step finished
     gdone = [torch.cuda.Event(), torch.cuda.Event()]  # gather of the buffer's step finished
 
+    overlap = gather is not None and a.gather == "overlap"
+
     def step(i):
         buf = i % 2
-        if gather is not None:
+        if overlap:
             stream.wait_event(gdone[buf])  # step i - 2's gather has read this buffer
         model.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), B, T, maxL, d_outs[buf].data_ptr(), stream.cuda_stream)
-        if gather is not None:
+        if overlap:
             fdone[buf].record(stream)
             with torch.cuda.stream(gstream):
                 gstream.wait_event(fdone[buf])
                 gather.step(d_outs[buf])
                 gdone[buf].record(gstream)
+        elif gather is not None:  # serial: the gather follows the forward on the same stream
+            gather.step(d_outs[buf])
 
     def join(i):
         """Makes the main stream wait for step i's gather (every gather ends inside a timed step)."""
-        if gather is not None and i >= 0:
+        if overlap and i >= 0:
             stream.wait_event(gdone[i % 2])
 
     # warm-up (also captures nothing: the device path launches directly)
@@ -446,14 +458,17 @@ def run_ours(a):
             clk.end()
         if world > 1:
             dist.barrier()
-        t = sum(s_.elapsed_time(e_) for s_, e_ in evs)
+        per = [s_.elapsed_time(e_) for s_, e_ in evs]
+        t = sum(per)
+        if world > 1 and a.verbose_steps:
+            print(f"rank {rank} step ms: " + " ".join(f"{x:.3f}" for x in per), file=sys.stderr, flush=True)
         t_t = torch.tensor([t], device="cuda")
         if world > 1:
             dist.all_reduce(t_t, op=dist.ReduceOp.MAX)
         return float(t_t.item())
 
     # 1) the headline: K steps, nothing but the forward (+ gather) on the stream
-    with Clocks(local) as clk:
+    with Clocks(local, poll=rank == 0 and a.clock_poll) as clk:
         ms = timed_loop(clk)
     # 2) the same K steps with CUDA events recorded between the forward's launches on the launching
     #    stream: per-kernel-class durations for the roofline
@@ -562,8 +577,10 @@ def run_ours(a):
                        "mode": a.mode, "ffn_block": (a.ffn if int8 else None), "global_batch": int(len(lens)), "per_gpu_batch": B, "tokens_per_gpu": T,
                        "seq_len": cfg["seq"], "parallelism": f"sequence-sharded x{world}, gather to rank 0",
                        "l2": "flushed (256 MB write) before every timed step",
-                       "gather": "N > 1: step i's NCCL gather to rank 0 runs on a second stream under step i + 1's "
-                                 "forward and completes inside step i + 1's timed window (the last one inside the last)",
+                       "gather": ("N > 1: step i's NCCL gather to rank 0 runs on a second stream under step i + 1's "
+                                  "forward and completes inside step i + 1's timed window (the last one inside the last)")
+                                 if a.gather == "overlap" else
+                                 "N > 1: each step's NCCL gather to rank 0 follows its forward on the same stream, inside its timed window",
                        "useful_gflop_per_step": flop_useful(lens) / 1e9},
             "roofline": {"kernel": CLASS_NAMES[dom], "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "peak_source": peak_note, "traffic": tr,
@@ -871,6 +888,11 @@ def main():
     ap.add_argument("--prec", default="f16", choices=["f16", "bf16"],
                     help="16-bit GEMM operand type of the f32 / w8a32 modes")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--gather", default="overlap", choices=["overlap", "serial"],
+                    help="N > 1: step i's gather runs under step i + 1's forward (overlap) or after step i's forward")
+    ap.add_argument("--verbose-steps", action="store_true", help="N > 1: print each rank's per-step times to stderr")
+    ap.add_argument("--no-clock-poll", dest="clock_poll", action="store_false",
+                    help="no NVML polling thread (one clock sample inside the timed region only)")
     ap.add_argument("--ffn", default="split", choices=["fused", "split"],
                     help="W8A8 feed-forward block: the FFN1 + FFN2 kernel pair (default) or one kernel")
     ap.add_argument("--batch", type=int, default=None,
