@@ -99,3 +99,46 @@ def test_bench_flop_accounting():
     import bench
     assert bench.flop_useful([72]) == 6 * (3538944 * 72 + 1536 * 72 * 72)
     assert abs(bench.flop_useful([128]) / 1e9 - 2.869) < 1e-3
+
+
+def test_bench_inputs_weak_and_strong_sharding():
+    """configs[1] weak scaling: every rank gets the one-GPU batch's lengths (equal work) and its own
+    tokens; configs[3] strong scaling: the fixed batch is dealt so that every sequence lands on exactly
+    one rank."""
+    sys.path.insert(0, ROOT)
+    import bench
+    ids, lens, shards = bench.make_inputs("c2", 4)
+    assert len(shards) == 4 and all(len(s) == 256 for s in shards)
+    for s in shards[1:]:
+        assert np.array_equal(lens[s], lens[shards[0]])
+        assert not np.array_equal(ids[s], ids[shards[0]])
+    ids, lens, shards = bench.make_inputs("c4", 8, batch_override=512)
+    allrows = np.sort(np.concatenate(shards))
+    assert np.array_equal(allrows, np.arange(512))
+
+
+def test_bench_metric_and_bytes_bookkeeping():
+    sys.path.insert(0, ROOT)
+    import bench
+    # both arms print the same metric string (the driver divides them)
+    assert bench.arctic_metric("c2", "w8a8") == bench.arctic_metric("c2", "w8a32") == "Arctic-embed-xs seq/s @seq128 (int8)"
+    assert bench.arctic_metric("c4", "f32") == "Arctic-embed-xs seq/s @seq512 (f32)"
+    # the fused FFN block's algorithmic bytes are the split pair's minus the GELU output's round trip
+    T = 18106
+    split = bench.class_bytes(5, T, 256, True) + bench.class_bytes(7, T, 256, True)
+    fused = bench.class_bytes(6, T, 256, True)
+    h_round_trip = T * (1536 * 2 + 4) * 2  # f16 H + its row |max|, written by FFN1 and read by FFN2
+    assert split - fused == h_round_trip
+
+
+def test_bench_clock_sampler_without_polling():
+    """A rank that does not poll (under torchrun only rank 0 polls) still opens and closes cleanly."""
+    sys.path.insert(0, ROOT)
+    import bench
+    c = bench.Clocks(0, poll=False)
+    with c:
+        c.begin()
+        c.mark()
+        c.end()
+    assert c.t is None and c.proc is None
+    assert "samples" in c.summary()
